@@ -1,0 +1,381 @@
+"""Throughput of the cuda backend: RTFx (audio seconds per wall second) of the whole path
+(log-mel front-end, 24-layer encoder, TDT greedy decode) on synthetic speech-like clips
+of 2-30 s (seeded, uniform), with seeded random-init weights of the Parakeet-TDT-0.6B-v3
+architecture, bf16. One process per GPU; each rank decodes its own shard of clips with
+no collective on the data path (weak scaling: `--clips-per-rank` per GPU, 512 by
+default, so 8 GPUs process the 4096-clip set of the whole-box workload).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Prints one JSON line (rank 0). `value` is device-timed with inputs resident in HBM;
+`e2e` is the same metric through the public API (Bark.tokens_batch on host arrays,
+host<->device copies inside the timed region). `--impl reference` times the reference
+path's CPU implementation (the CPU oracle: tinybark's front-end restated in numpy,
+transformers' ParakeetEncoder, the TDT loop restated in torch) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "RTFx (audio-s per wall-s) per box at 1/2/4/8 B200; encoder ms per 10 s clip"
+WORKLOAD = "whole-box: synthetic clips 2-30 s (uniform, seeded), packed end to end, front-end + encoder + TDT decode"
+SEED = 4
+
+
+def args_parser():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--clips-per-rank", type=int, default=512)
+    p.add_argument("--layers", type=int, default=24)
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p
+
+
+def rank_info():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def shard(rank: int, count: int):
+    """This rank's clips: durations uniform in [2, 30) s and audio, both seeded by rank."""
+    from tinybark_b200 import synthetic
+
+    durs = synthetic.durations(count, SEED * 1000 + rank)
+    seeds = [SEED * 10_000_000 + rank * 100_000 + i for i in range(count)]
+    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as pool:
+        pcm = list(pool.map(lambda a: synthetic.clip(*a), zip(durs, seeds)))
+    return [synthetic.to_float(p) for p in pcm], durs
+
+
+def weights(layers: int):
+    from tinybark_b200 import synthetic
+    from tinybark_b200 import weights as w
+
+    cfg = synthetic.config(layers)
+    return w.convert(synthetic.state_dict(0, layers=layers), cfg), cfg
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 8:
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[4:]))
+                except ValueError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for _, _, flags in rows for n, f in zip(names, flags) if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_pipeline_factory(layers: int):
+    """The reference path on the host: tinybark's front-end (restated in numpy),
+    transformers' ParakeetEncoder (bf16 when the CPU has AVX512-BF16, as
+    tinybark/pytorch/__init__.py:53-58 picks, else fp32), and the TDT loop."""
+    import torch
+
+    from oracle import decoder, encoder, frontend
+    from tinybark_b200 import synthetic
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sd = synthetic.state_dict(0, layers=layers)
+    bf16 = getattr(torch.cpu, "_is_avx512_bf16_supported", lambda: False)()
+    dtype = torch.bfloat16 if bf16 else torch.float32
+    try:
+        enc_model = encoder.hf_encoder(sd, layers).to(dtype)
+    except Exception:  # transformers without Parakeet: the restated encoder
+        enc_model = None
+    proj_w = torch.from_numpy(sd["encoder_projector.weight"]).to(dtype)
+    proj_b = torch.from_numpy(sd["encoder_projector.bias"]).to(dtype)
+    dec = decoder.Decoder(sd)
+
+    def run(samples: np.ndarray) -> list[int]:
+        feats = frontend.features(samples)
+        if len(feats) < 2:
+            return []
+        with torch.inference_mode():
+            if enc_model is not None:
+                hidden = enc_model(torch.from_numpy(feats)[None].to(dtype)).last_hidden_state[0]
+                enc = torch.nn.functional.linear(hidden, proj_w, proj_b).float().numpy()
+            else:
+                enc = encoder.encode(sd, feats)
+        return dec.greedy(enc, len(feats))
+
+    return run, ("bf16" if bf16 else "fp32"), torch.get_num_threads()
+
+
+def cpu_baseline(clips, durs, layers: int, budget_s: float):
+    run, dtype, threads = cpu_pipeline_factory(layers)
+    run(clips[0][:16000])  # warm-up
+    audio, start, n = 0.0, time.perf_counter(), 0
+    while n < len(clips) and (n == 0 or time.perf_counter() - start < budget_s):
+        run(clips[n])
+        audio += durs[n]
+        n += 1
+    wall = time.perf_counter() - start
+    return {"value": audio / wall, "unit": "audio-s/s", "cores": threads, "kind": "port",
+            "sample": f"{n} clips ({audio:.1f} s of audio) of the same workload, one at a time, {dtype}, "
+                      f"tinybark front-end restated + transformers ParakeetEncoder + TDT loop restated"}
+
+
+def run_reference(args):
+    rank, world, _ = rank_info()
+    if rank != 0:
+        return
+    clips, durs = shard(0, max(8, args.steps + args.warmup))
+    run, dtype, threads = cpu_pipeline_factory(args.layers)
+    for i in range(args.warmup):
+        run(clips[i % len(clips)][:32000])
+    audio, times = 0.0, []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        run(clips[i % len(clips)])
+        times.append(time.perf_counter() - t0)
+        audio += durs[i % len(clips)]
+    wall = sum(times)
+    value = audio / wall
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "audio-s/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * wall / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": "one clip per step, clips of rank 0's shard",
+                   "layers": args.layers},
+        "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} clips ({audio:.1f} s audio), {dtype}"},
+        "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = rank_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(minutes=10), device_id=dev)
+
+    import tinybark_b200
+    from tinybark_b200 import _lib as L
+    from tinybark_b200.engine import Engine
+
+    clips, durs = shard(rank, args.clips_per_rank)
+    tensors, cfg = weights(args.layers)
+    bark = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg))
+    eng: Engine = bark.engine
+    audio_rank = float(np.sum(durs))
+    plan = eng.plan([len(c) // 160 for c in clips])
+    samples, sample_off = eng.upload(clips)
+    torch.cuda.synchronize()
+
+    def step():
+        feats = eng.features(samples, sample_off, plan)
+        enc = eng.encode(feats, plan)
+        return eng.decode(enc, plan)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    eng.check()
+
+    # Device-timed region, inputs resident.
+    barrier()
+    launches0 = L.lib.tb_launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            tokens, counts = step()
+        end.record()
+        torch.cuda.synchronize()
+    launches = (L.lib.tb_launch_count() - launches0) // args.steps
+    eng.check()
+    ms = max_over_ranks(start.elapsed_time(end)) / args.steps
+    barrier()
+    total_audio = audio_rank
+    if world > 1:
+        t = torch.tensor([audio_rank], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        total_audio = float(t.item())
+    value = total_audio / (ms / 1000.0)
+
+    # End to end through the public API: host float32 arrays in, token lists out.
+    for _ in range(1):
+        bark.tokens_batch(clips)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = bark.tokens_batch(clips)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    h2d = int(sum(len(c) for c in clips) * 4 + (len(clips) + 1) * 8 + plan.meta.numel() * 4)
+    d2h = int(len(clips) * plan.max_cap * 4 + len(clips) * 4)
+
+    # Encoder ms per 10 s clip, batch 1.
+    from tinybark_b200 import synthetic
+
+    one = [synthetic.to_float(synthetic.clip(10.0, 0))]
+    p1 = eng.plan([1000])
+    s1, o1 = eng.upload(one)
+    f1 = eng.features(s1, o1, p1)
+    for _ in range(3):
+        eng.encode(f1, p1)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(10):
+        eng.encode(f1, p1)
+    b.record()
+    torch.cuda.synchronize()
+    enc10_ms = a.elapsed_time(b) / 10
+
+    # Roofline of the dominant kernel (the tcgen05 GEMM), timed alone at the FFN
+    # up-projection of this step: M = encoder frames of the shard, N = 4096, K = 1024.
+    M = plan.batch.t3_total
+    x = torch.randn(M, 1024, device=dev).to(torch.bfloat16)
+    w = (torch.randn(4096, 1024, device=dev) / 32).to(torch.bfloat16)
+    h = torch.empty(M, 4096, device=dev, dtype=torch.bfloat16)
+    ep = L.Epilogue(kind=L.EPI_SILU, out_dtype=L.BF16, out=h.data_ptr(), ldo=4096)
+    import ctypes
+
+    def ffn():
+        L.check(L.lib.tb_gemm(L.BF16, x.data_ptr(), 1024, w.data_ptr(), M, 4096, 1024, ctypes.byref(ep),
+                              eng.err.data_ptr(), torch.cuda.current_stream().cuda_stream), "tb_gemm")
+
+    for _ in range(3):
+        ffn()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(20):
+        ffn()
+    g1.record()
+    torch.cuda.synchronize()
+    gemm_s = g0.elapsed_time(g1) / 20 / 1000
+    hbm, tflops, kind = peaks()
+    achieved = 2.0 * M * 4096 * 1024 / gemm_s / 1e12
+    traffic = None
+    tpath = ROOT / "profiles" / "traffic.json"
+    if tpath.exists():
+        t = json.loads(tpath.read_text()).get("gemm_ffn_up_bytes_per_row")
+        traffic = None if t is None else t * M
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        base = None
+        if world == 1 and not args.no_cpu_baseline:
+            base = cpu_baseline(clips, durs, args.layers, args.cpu_seconds)
+        line = {
+            "metric": METRIC, "value": value, "unit": "audio-s/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "clips_per_rank": len(clips), "audio_s_per_rank": round(audio_rank, 2),
+                       "encoder_frames_per_rank": int(M), "layers": args.layers, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (samples and weights, >126 MB per step)"},
+            "encoder_ms_per_10s_clip": enc10_ms,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
+                         "frac": achieved / tflops, "traffic": traffic,
+                         "kernel": f"gemm_tc_kernel<256> FFN up M={M} N=4096 K=1024, timed alone",
+                         "peak_kind": f"{kind} burst bf16"},
+            "cpu_baseline": base,
+            "e2e": {"value": total_audio / (e2e_ms / 1000.0), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = args_parser().parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

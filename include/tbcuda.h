@@ -1,0 +1,239 @@
+/* tbcuda: the C ABI of the B200 (sm_100a) inference path for the
+ * Parakeet-TDT-0.6B-v3 / Underdog Bark speech-to-text model.
+ *
+ * Plain C types only: device pointers, sizes and a cudaStream_t passed as void*.
+ * The library allocates no device memory: the caller passes every buffer, including
+ * a workspace whose size the *_workspace_bytes functions give. Every function returns
+ * TB_OK (0) or a TB_ERR_* status; kernels that wait on hardware barriers report a
+ * timeout by or-ing a TB_DEV_* bit into the caller's device error word `err`
+ * (int32, zeroed by the caller) instead of hanging.
+ *
+ * Threading: functions are reentrant; calls on one stream are ordered. Use one
+ * process per GPU.
+ */
+#ifndef TBCUDA_H
+#define TBCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum tb_status {
+  TB_OK = 0,
+  TB_ERR_ARG = 1,         /* bad size, pointer or enum */
+  TB_ERR_CUDA = 2,        /* a CUDA runtime call failed (see tb_last_cuda_error) */
+  TB_ERR_UNSUPPORTED = 3, /* no kernel for this shape / dtype */
+  TB_ERR_WORKSPACE = 4    /* workspace smaller than *_workspace_bytes */
+};
+
+/* Bits a kernel or-s into the device error word. */
+enum tb_device_error {
+  TB_DEV_GEMM_TIMEOUT = 1 << 0,
+  TB_DEV_ATTN_TIMEOUT = 1 << 1,
+  TB_DEV_DECODE_TIMEOUT = 1 << 2
+};
+
+/* Arithmetic type of a path: fp32 everywhere, or bf16 operands with fp32
+ * accumulation, fp32 residual stream and fp32 LayerNorm/softmax statistics. */
+enum tb_dtype { TB_F32 = 0, TB_BF16 = 1 };
+
+/* Model dimensions, fixed by the architecture (tinybark/mojo/bark/model.mojo:29-43). */
+#define TB_HIDDEN 1024
+#define TB_HEADS 8
+#define TB_HEAD_DIM 128
+#define TB_FFN 4096
+#define TB_KERNEL 9
+#define TB_CHANNELS 256
+#define TB_MELS 128
+#define TB_VOCAB 8193
+#define TB_BLANK 8192
+#define TB_EOS 3
+#define TB_DURATIONS 5
+#define TB_PRED 640
+#define TB_TOKEN_ROWS 8256 /* token head padded to a multiple of 64 (tinybark/weights.py:24,84-86) */
+#define TB_JOINT_ROWS 8448 /* token rows, then the 5 duration rows at TB_TOKEN_ROWS, zero rows to a multiple of 256 */
+
+/* GEMM epilogues: C = A(M x K) * W(N x K)^T, then one of: */
+enum tb_epilogue_kind {
+  TB_EPI_STORE = 0,     /* out[m,n] = acc (+ bias[n])                                     */
+  TB_EPI_SILU = 1,      /* out[m,n] = silu(acc)                                            */
+  TB_EPI_RESIDUAL = 2,  /* res[m,n] += alpha * acc (res is fp32 `out`)                     */
+  TB_EPI_BIAS_RELU = 3, /* out[m,n] = relu(acc + bias[n])                                  */
+  TB_EPI_GLU = 4,       /* W rows interleaved (a0,g0,a1,g1..): out[m,n/2] = a*sigmoid(g)   */
+  TB_EPI_QKV = 5,       /* N = 3072: out = q+bias_u, out2 = q+bias_v, out3 = k, out4 = v    */
+  TB_EPI_ARGMAX = 6,    /* joint head: argmax of acc+bias over [0,split) into keys[m] and
+                           over [split, split_end) into keys2[m]; first index wins ties   */
+  TB_EPI_LSTM = 7       /* W rows gate-interleaved (row 4u+g, gates i,f,g,o): LSTM cell for
+                           rows with mask[m] != 0: c[m,u], h[m,u] updated, h also written
+                           to out[m*ldo+u] and out2[m*ldo2+u] (out_dtype)                  */
+};
+
+typedef struct tb_epilogue {
+  int kind;
+  int out_dtype; /* tb_dtype of out/out2/out3/out4 (RESIDUAL: out is always fp32) */
+  void* out;
+  long long ldo; /* elements */
+  const float* bias;
+  float alpha;
+  void* out2;
+  long long ldo2;
+  void* out3;
+  void* out4;
+  const float* bias_u;
+  const float* bias_v;
+  unsigned long long* keys;
+  unsigned long long* keys2;
+  int split;
+  int split_end;
+  float* c;
+  float* h;
+  const int* mask;
+} tb_epilogue;
+
+/* One conformer layer, device pointers. Matrices are tb_model.dtype; vectors fp32. */
+typedef struct tb_layer {
+  const float* norm_w[5]; /* norm_feed_forward1, norm_self_att, norm_conv, norm_feed_forward2, norm_out */
+  const float* norm_b[5];
+  const void* ff1_w1; /* [4096, 1024] */
+  const void* ff1_w2; /* [1024, 4096] */
+  const void* ff2_w1;
+  const void* ff2_w2;
+  const void* qkv;    /* [3072, 1024]: q, k, v rows */
+  const void* o_proj; /* [1024, 1024] */
+  const void* pw1;    /* [2048, 1024]: pointwise_conv1 rows interleaved (a0, g0, a1, g1, ...) */
+  const void* pw2;    /* [1024, 1024] */
+  const float* bias_u; /* [8, 128] */
+  const float* bias_v;
+  const float* dw_w;  /* [1024, 9] depthwise taps with BatchNorm folded in */
+  const float* dw_b;  /* [1024] */
+  const void* rel;    /* [2*max_len-1, 1024]: positions(max_len) @ relative_k_proj^T */
+} tb_layer;
+
+typedef struct tb_model {
+  int dtype;
+  int layers;
+  int max_len; /* encoder frames the rel tables cover */
+  /* subsampling (dw_striding, 8x) */
+  const float* sub0_w;  /* [256, 9] conv 1->256, 3x3 */
+  const float* sub0_b;
+  const float* sub_dw_w[2]; /* [256, 9] depthwise 3x3 */
+  const float* sub_dw_b[2];
+  const void* sub_pw_w[2];  /* [256, 256] pointwise */
+  const float* sub_pw_b[2];
+  const void* sub_linear_w; /* [1024, 4096], columns in (frequency, channel) order */
+  const float* sub_linear_b;
+  const tb_layer* layer;    /* host array of `layers` entries */
+  const void* enc_proj_w;   /* [640, 1024] */
+  const float* enc_proj_b;
+  /* prediction network and joint */
+  const void* embedding;    /* [8193, 640] */
+  const void* lstm_w[2];    /* [2560, 1280] = [W_ih | W_hh], rows gate-interleaved (4u+g) */
+  const float* lstm_b[2];   /* [2560] = b_ih + b_hh, same row order */
+  const void* dec_proj_w;   /* [640, 640] */
+  const float* dec_proj_b;
+  const void* joint_w;      /* [TB_JOINT_ROWS, 640] */
+  const float* joint_b;     /* [TB_JOINT_ROWS], -inf on padding rows */
+  /* front-end tables */
+  const float* window;      /* [512] */
+  const float* mel_w;       /* packed non-zero filter weights */
+  const int* mel_start;     /* [128] first FFT bin of each filter */
+  const int* mel_off;       /* [129] offsets of each filter's weights in mel_w */
+} tb_model;
+
+/* A batch of clips, packed end to end at every stage (no padding between clips).
+ * Offsets are cumulative row counts, [clips + 1], on the device; *_total are the
+ * last entries, also passed by value. */
+typedef struct tb_batch {
+  int clips;
+  int frames_total; /* feature frames */
+  int t1_total;     /* after the first stride-2 conv */
+  int t2_total;     /* after the second */
+  int t3_total;     /* encoder frames */
+  const int* frame_off;
+  const int* t1_off;
+  const int* t2_off;
+  const int* t3_off;
+  const int* t2_clip;  /* [t2_total] clip of each row */
+  const int* t3_clip;  /* [t3_total] clip of each row */
+  const int* sub_tiles;  /* [n_sub_tiles * 2]: (clip, first t2 row in clip) */
+  int n_sub_tiles;
+  const int* attn_tiles; /* [n_attn_tiles * 2]: (clip, first query row in clip) */
+  int n_attn_tiles;
+  int max_t3;
+} tb_batch;
+
+/* ---- library ---- */
+int tb_version(void);
+/* Rows per work item in tb_batch.sub_tiles (second-stage frames) and
+ * tb_batch.attn_tiles (query frames) for the given dtype. */
+int tb_tile_rows(int dtype, int* sub_rows, int* attn_rows);
+/* Kernels this process has launched through the library so far. */
+long long tb_launch_count(void);
+const char* tb_last_cuda_error(void);
+int tb_sm_count(int device, int* out);
+
+/* ---- front-end: tinybark/audio.py:42-55 (features) ----
+ * samples: float32, clips packed end to end (sample_off [clips+1], device, int64).
+ * feats: [frames_total, 128] float32; frame_off [clips+1] device, frames = samples // 160,
+ * every clip at least 2 frames. stats: workspace of tb_frontend_workspace_bytes. */
+size_t tb_frontend_workspace_bytes(int clips, int frames_total);
+int tb_frontend(const tb_model* m, const float* samples, const long long* sample_off, const int* frame_off,
+                int clips, int frames_total, int max_frames, float* feats, void* ws, size_t ws_bytes, void* stream);
+
+/* ---- LayerNorm over 1024: tinybark/tinygrad/model.py:56-57 (layernorm) ----
+ * y = LN(x) (y_dtype), fp32 statistics, eps 1e-5. If x_out != NULL, LN(x) is also
+ * written there in fp32 (x_out may be x). If w2 != NULL (needs x_out), y = LN2(LN(x)):
+ * a block's norm_out fused with the next block's norm_feed_forward1. */
+int tb_layernorm(const float* x, const float* w, const float* b, float* x_out, const float* w2, const float* b2,
+                 void* y, int y_dtype, int rows, void* stream);
+
+/* ---- linear layers: tinybark/tinygrad/model.py:37-40 (linear), tinybark/mojo/bark/gpu.mojo:429-436 (mm) ----
+ * A [M, K] (lda elements) times W [N, K] transposed, epilogue `epi`. dtype TB_BF16 runs
+ * the tcgen05 tensor-core kernel (K % 64 == 0, N % 256 == 0 or N % 128 == 0); TB_F32 a
+ * CUDA-core fp32 kernel (K % 16 == 0, N % 128 == 0). */
+int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue* epi,
+            int* err, void* stream);
+
+/* ---- relative-position MHSA core: tinybark/tinygrad/model.py:99-116 (_attention),
+ * tinybark/mojo/bark/gpu.mojo:202-224 (softmax_kernel) ----
+ * qu = q + bias_u, qv = q + bias_v, k, v: [t3_total, 1024] (dtype) packed by clip;
+ * rel: [2*max_len-1, 1024]; out: [t3_total, 1024] (dtype), heads side by side. */
+int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
+                        int max_len, const tb_batch* batch, void* out, int* err, void* stream);
+
+/* ---- conv module middle: tinybark/tinygrad/model.py:121-124 (_conv: GLU output,
+ * depthwise k=9 with folded BatchNorm, SiLU) ----
+ * glu: [t3_total, 1024] (dtype) = a * sigmoid(g); out = silu(dw(glu) + b) (dtype). */
+int tb_conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch* batch, void* out,
+                      void* stream);
+
+/* ---- subsampling: tinybark/tinygrad/model.py:87-97 (_subsample) ----
+ * feats [frames_total, 128] fp32 -> x [t3_total, 1024] fp32. */
+size_t tb_subsample_workspace_bytes(int dtype, int t2_total, int t3_total);
+int tb_subsample(const tb_model* m, const tb_batch* batch, const float* feats, float* x, void* ws, size_t ws_bytes,
+                 int* err, void* stream);
+
+/* ---- whole encoder: tinybark/tinygrad/model.py:140-158 (_encode),
+ * tinybark/mojo/bark/gpu.mojo:399-426 (GpuEncoder.encode) ----
+ * feats -> enc [t3_total, 640] fp32 (encoder frames projected for the joint). */
+size_t tb_encoder_workspace_bytes(int dtype, int t2_total, int t3_total);
+int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* feats, float* enc, void* ws,
+                       size_t ws_bytes, int* err, void* stream);
+
+/* ---- TDT greedy decode: tinybark/tinygrad/model.py:162-233 (_step, generate),
+ * tinybark/mojo/bark/model.mojo:294-318 (decode) ----
+ * One lane per clip, all lanes stepped together. enc [t3_total, 640] fp32 packed by
+ * clip (enc_off [lanes+1]); cap [lanes] = 10 * subsampled(frames + 1, 3) - 1.
+ * tokens: [lanes, max_cap] int32; counts: [lanes]. host_flag: pinned host int used to
+ * stop early once every lane is done (may be NULL: then max_cap iterations run). */
+size_t tb_decode_workspace_bytes(int dtype, int lanes);
+int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
+                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TBCUDA_H */

@@ -1,0 +1,284 @@
+"""Each sm_100a kernel through the C ABI against a float64 torch restatement of the same
+operation. fp32 kernels within 1e-5 (max-rel), bf16 kernels within 1e-2 of the
+reference computed from the same bf16-rounded inputs."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import max_rel
+
+pytestmark = pytest.mark.gpu
+
+TOL = {0: 1e-5, 1: 1e-2}
+
+
+@pytest.fixture(scope="module")
+def L():
+    from tinybark_b200 import _lib
+
+    return _lib
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def tdt(dtype):
+    return torch.bfloat16 if dtype == 1 else torch.float32
+
+
+def gemm(L, dtype, a, w, ep, err):
+    L.check(L.lib.tb_gemm(dtype, a.data_ptr(), a.stride(0), w.data_ptr(), a.shape[0], w.shape[0], a.shape[1],
+                          ctypes.byref(ep), err.data_ptr(), stream()), "tb_gemm")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+
+
+def operands(dtype, m, n, k, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(m, k, device="cuda", generator=g).to(tdt(dtype))
+    w = (torch.randn(n, k, device="cuda", generator=g) / k**0.5).to(tdt(dtype))
+    return a, w, a.double() @ w.double().T
+
+
+@pytest.fixture
+def err():
+    return torch.zeros(1, dtype=torch.int32, device="cuda")
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (77, 384, 128), (300, 512, 1024), (129, 640, 640), (1000, 1024, 4096)])
+def test_gemm_store_bias(L, dtype, m, n, k, err):
+    a, w, ref = operands(dtype, m, n, k)
+    bias = torch.randn(n, device="cuda")
+    out = torch.full((m, n), float("nan"), device="cuda")
+    ep = L.Epilogue(kind=L.EPI_STORE, out_dtype=0, out=out.data_ptr(), ldo=n, bias=bias.data_ptr())
+    gemm(L, dtype, a, w, ep, err)
+    assert max_rel(out.cpu(), (ref + bias.double()).cpu()) < TOL[dtype] / 10
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_gemm_silu_residual_relu(L, dtype, err):
+    m, n, k = 333, 512, 256
+    a, w, ref = operands(dtype, m, n, k, seed=1)
+    out = torch.empty(m, n, device="cuda", dtype=tdt(dtype))
+    gemm(L, dtype, a, w, L.Epilogue(kind=L.EPI_SILU, out_dtype=dtype, out=out.data_ptr(), ldo=n), err)
+    assert max_rel(out.float().cpu(), F.silu(ref).cpu()) < TOL[dtype]
+
+    res = torch.randn(m, n, device="cuda")
+    expect = res.double() + 0.5 * ref
+    gemm(L, dtype, a, w, L.Epilogue(kind=L.EPI_RESIDUAL, out=res.data_ptr(), ldo=n, alpha=0.5), err)
+    assert max_rel(res.cpu(), expect.cpu()) < TOL[dtype] / 10
+
+    bias = torch.randn(n, device="cuda")
+    gemm(L, dtype, a, w, L.Epilogue(kind=L.EPI_BIAS_RELU, out_dtype=dtype, out=out.data_ptr(), ldo=n,
+                                    bias=bias.data_ptr()), err)
+    assert max_rel(out.float().cpu(), torch.relu(ref + bias.double()).cpu()) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_gemm_glu(L, dtype, err):
+    m, n, k = 200, 2048, 256
+    a, w, ref = operands(dtype, m, n, k, seed=2)
+    out = torch.empty(m, n // 2, device="cuda", dtype=tdt(dtype))
+    gemm(L, dtype, a, w, L.Epilogue(kind=L.EPI_GLU, out_dtype=dtype, out=out.data_ptr(), ldo=n // 2), err)
+    expect = ref[:, 0::2] * torch.sigmoid(ref[:, 1::2])
+    assert max_rel(out.float().cpu(), expect.cpu()) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_gemm_qkv(L, dtype, err):
+    m, k = 150, 128
+    a, w, ref = operands(dtype, m, 3072, k, seed=3)
+    u, v = torch.randn(1024, device="cuda"), torch.randn(1024, device="cuda")
+    outs = [torch.empty(m, 1024, device="cuda", dtype=tdt(dtype)) for _ in range(4)]
+    ep = L.Epilogue(kind=L.EPI_QKV, out_dtype=dtype, out=outs[0].data_ptr(), out2=outs[1].data_ptr(),
+                    out3=outs[2].data_ptr(), out4=outs[3].data_ptr(), ldo=1024, bias_u=u.data_ptr(),
+                    bias_v=v.data_ptr())
+    gemm(L, dtype, a, w, ep, err)
+    q, kk, vv = ref[:, :1024], ref[:, 1024:2048], ref[:, 2048:]
+    for got, want in zip(outs, (q + u.double(), q + v.double(), kk, vv)):
+        assert max_rel(got.float().cpu(), want.cpu()) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_gemm_lstm_cell(L, dtype, err):
+    lanes = 70
+    a, w, ref = operands(dtype, lanes, 2560, 1280, seed=4)
+    bias = torch.randn(2560, device="cuda")
+    c = torch.randn(lanes, 640, device="cuda")
+    h = torch.zeros(lanes, 640, device="cuda")
+    hout = torch.zeros(lanes, 1280, device="cuda", dtype=tdt(dtype))
+    mask = (torch.arange(lanes, device="cuda") % 3 != 0).int()
+    c0 = c.clone()
+    ep = L.Epilogue(kind=L.EPI_LSTM, out_dtype=dtype, out=hout.data_ptr(), ldo=1280, out2=None, ldo2=0,
+                    bias=bias.data_ptr(), c=c.data_ptr(), h=h.data_ptr(), mask=mask.data_ptr())
+    gemm(L, dtype, a, w, ep, err)
+    g = (ref + bias.double()).view(lanes, 640, 4)
+    i, f, gg, o = torch.sigmoid(g[..., 0]), torch.sigmoid(g[..., 1]), torch.tanh(g[..., 2]), torch.sigmoid(g[..., 3])
+    c_new = f * c0.double() + i * gg
+    h_new = o * torch.tanh(c_new)
+    keep = mask.bool()
+    assert max_rel(c[keep].cpu(), c_new[keep].cpu()) < TOL[dtype]
+    assert max_rel(h[keep].cpu(), h_new[keep].cpu()) < TOL[dtype]
+    assert torch.equal(c[~keep], c0[~keep]) and bool((h[~keep] == 0).all())
+    assert max_rel(hout[keep, :640].float().cpu(), h_new[keep].cpu()) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_gemm_argmax(L, dtype, err):
+    lanes, split, n = 90, 8256, 8448
+    a, w, ref = operands(dtype, lanes, n, 640, seed=5)
+    bias = torch.randn(n, device="cuda")
+    bias[8193:8256] = float("-inf")
+    bias[split + 5 :] = float("-inf")
+    keys = torch.zeros(lanes, dtype=torch.int64, device="cuda")
+    keys2 = torch.zeros(lanes, dtype=torch.int64, device="cuda")
+    ep = L.Epilogue(kind=L.EPI_ARGMAX, bias=bias.data_ptr(), keys=keys.data_ptr(), keys2=keys2.data_ptr(),
+                    split=split, split_end=split + 5)
+    gemm(L, dtype, a, w, ep, err)
+    logits = ref + bias.double()
+    tok = (0xFFFFFFFF - (keys & 0xFFFFFFFF)).cpu().numpy()
+    dur = (0xFFFFFFFF - (keys2 & 0xFFFFFFFF)).cpu().numpy()
+    lt, ld = logits[:, :split].cpu().numpy(), logits[:, split : split + 5].cpu().numpy()
+    scale = np.abs(lt[np.isfinite(lt)]).max()
+    for r in range(lanes):
+        assert tok[r] < 8193 and lt[r, tok[r]] >= lt[r].max() - 1e-5 * scale * (1 if dtype == 0 else 100)
+        assert ld[r, dur[r]] >= ld[r].max() - 1e-5 * scale * (1 if dtype == 0 else 100)
+    if dtype == 0:
+        assert (tok == lt.argmax(1)).all() and (dur == ld.argmax(1)).all()
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("fused", [False, True])
+def test_layernorm(L, dtype, fused):
+    rows = 300
+    x = torch.randn(rows, 1024, device="cuda") * 3 + 1
+    w, b = torch.randn(1024, device="cuda"), torch.randn(1024, device="cuda")
+    w2, b2 = torch.randn(1024, device="cuda"), torch.randn(1024, device="cuda")
+    y = torch.empty(rows, 1024, device="cuda", dtype=tdt(dtype))
+    xd = x.double()
+    ref = F.layer_norm(xd, (1024,), w.double(), b.double(), 1e-5)
+    xo = torch.empty_like(x) if fused else None
+    L.check(L.lib.tb_layernorm(x.data_ptr(), w.data_ptr(), b.data_ptr(), xo.data_ptr() if fused else None,
+                               w2.data_ptr() if fused else None, b2.data_ptr() if fused else None, y.data_ptr(),
+                               dtype, rows, stream()), "tb_layernorm")
+    torch.cuda.synchronize()
+    if fused:
+        assert max_rel(xo.cpu(), ref.cpu()) < 1e-5
+        ref = F.layer_norm(ref, (1024,), w2.double(), b2.double(), 1e-5)
+    assert max_rel(y.float().cpu(), ref.cpu()) < TOL[dtype]
+
+
+def batch_for(L, t3_list, attn_rows):
+    """A tb_batch with only the encoder-frame fields set (attention, depthwise conv)."""
+    t3 = np.array(t3_list)
+    off = np.concatenate([[0], np.cumsum(t3)]).astype(np.int32)
+    clip = np.repeat(np.arange(len(t3), dtype=np.int32), t3)
+    order = np.argsort(-t3, kind="stable")
+    tiles = np.array([(c, r) for c in order for r in range(0, t3[c], attn_rows)], np.int32).reshape(-1)
+    keep = [torch.from_numpy(a).cuda() for a in (off, clip, tiles)]
+    b = L.Batch()
+    b.clips, b.t3_total, b.max_t3 = len(t3), int(off[-1]), int(t3.max())
+    b.t3_off, b.t3_clip, b.attn_tiles, b.n_attn_tiles = keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), len(tiles) // 2
+    return b, keep, off
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_relpos_attention(L, dtype, err):
+    t3 = [1, 2, 7, 33, 130, 64]
+    max_len = 256
+    _, attn_rows = L.tile_rows(dtype)
+    b, keep, off = batch_for(L, t3, attn_rows)
+    R = off[-1]
+    g = torch.Generator(device="cuda").manual_seed(7)
+    qu, qv, k, v = (torch.randn(R, 1024, device="cuda", generator=g).to(tdt(dtype)) for _ in range(4))
+    rel = torch.randn(2 * max_len - 1, 1024, device="cuda", generator=g).to(tdt(dtype))
+    out = torch.empty(R, 1024, device="cuda", dtype=tdt(dtype))
+    L.check(L.lib.tb_relpos_attention(dtype, qu.data_ptr(), qv.data_ptr(), k.data_ptr(), v.data_ptr(), rel.data_ptr(),
+                                      max_len, ctypes.byref(b), out.data_ptr(), err.data_ptr(), stream()),
+            "tb_relpos_attention")
+    torch.cuda.synchronize()
+    for c, T in enumerate(t3):
+        s = slice(off[c], off[c + 1])
+        hq = lambda x: x[s].double().view(T, 8, 128).transpose(0, 1)
+        i = torch.arange(T, device="cuda")[:, None]
+        j = torch.arange(T, device="cuda")[None, :]
+        r = rel.double()[max_len - 1 - i + j].view(T, T, 8, 128).permute(2, 0, 1, 3)  # (H, i, j, d)
+        scores = hq(qu) @ hq(k).transpose(1, 2) + (hq(qv)[:, :, None, :] * r).sum(-1)
+        p = torch.softmax(scores / 128**0.5, -1)
+        ref = (p @ hq(v)).transpose(0, 1).reshape(T, 1024)
+        assert max_rel(out[s].float().cpu(), ref.cpu()) < TOL[dtype], (c, T)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_depthwise_conv_silu(L, dtype):
+    t3 = [1, 5, 9, 40, 3]
+    b, keep, off = batch_for(L, t3, 32)
+    R = off[-1]
+    x = torch.randn(R, 1024, device="cuda").to(tdt(dtype))
+    w = torch.randn(1024, 9, device="cuda")
+    bias = torch.randn(1024, device="cuda")
+    y = torch.empty(R, 1024, device="cuda", dtype=tdt(dtype))
+    L.check(L.lib.tb_conv_depthwise(dtype, x.data_ptr(), w.data_ptr(), bias.data_ptr(), ctypes.byref(b), y.data_ptr(),
+                                    stream()), "tb_conv_depthwise")
+    torch.cuda.synchronize()
+    for c in range(len(t3)):
+        s = slice(off[c], off[c + 1])
+        ref = F.conv1d(x[s].double().T[None], w.double()[:, None, :], bias.double(), padding=4, groups=1024)[0].T
+        assert max_rel(y[s].float().cpu(), F.silu(ref).cpu()) < TOL[dtype], c
+
+
+@pytest.fixture(scope="module")
+def engine2():
+    from conftest import state_dict
+    from tinybark_b200 import synthetic, weights
+    from tinybark_b200.engine import Engine
+
+    return Engine(weights.convert(state_dict(2), synthetic.config(2)), synthetic.config(2), dtype="fp32")
+
+
+def test_frontend_matches_oracle(engine2):
+    from conftest import golden_npz
+    from oracle import frontend
+    from tinybark_b200 import synthetic
+
+    g = golden_npz("frontend.npz")
+    clips = [g[f"{n}_samples"] for n in ("two_frames", "odd", "one_second")]
+    clips.append(synthetic.to_float(synthetic.clip(7.3, 5)))
+    plan = engine2.plan([len(c) // 160 for c in clips])
+    samples, off = engine2.upload(clips)
+    feats = engine2.features(samples, off, plan).cpu().numpy()
+    fo = plan.batch
+    start = 0
+    for c in clips:
+        ref = frontend.features(c)
+        got = feats[start : start + len(ref)]
+        start += len(ref)
+        np.testing.assert_allclose(got, ref, rtol=0, atol=2e-4)
+
+
+def test_subsample_matches_oracle(engine2):
+    from oracle import encoder as oenc
+    from oracle import frontend
+    from conftest import state_dict
+    from tinybark_b200 import _lib as L, synthetic
+
+    clips = [synthetic.to_float(synthetic.clip(s, 40 + i)) for i, s in enumerate((0.05, 1.37, 4.0))]
+    feats = [frontend.features(c) for c in clips]
+    plan = engine2.plan([len(f) for f in feats])
+    x = torch.empty(plan.batch.t3_total, 1024, device="cuda")
+    fdev = torch.from_numpy(np.concatenate(feats)).cuda()
+    nbytes = L.lib.tb_subsample_workspace_bytes(0, plan.batch.t2_total, plan.batch.t3_total)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    L.check(L.lib.tb_subsample(ctypes.byref(engine2.model), ctypes.byref(plan.batch), fdev.data_ptr(), x.data_ptr(),
+                               ws.data_ptr(), nbytes, engine2.err.data_ptr(), stream()), "tb_subsample")
+    engine2.check()
+    off = plan.t3_off.cpu().numpy()
+    for i, f in enumerate(feats):
+        ref = oenc.subsample(state_dict(2), torch.from_numpy(f)).numpy()
+        assert max_rel(x[off[i] : off[i + 1]].cpu().numpy(), ref) < 1e-5

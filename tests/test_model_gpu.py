@@ -1,0 +1,132 @@
+"""The whole path on the GPU against the oracle: encoder outputs within max-rel 1e-4
+(fp32) and 2e-2 (bf16), greedy TDT tokens identical in fp32 on the reference loop's
+golden cases, and end-to-end transcription tokens identical to the oracle pipeline."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_json, max_rel, state_dict
+
+pytestmark = pytest.mark.gpu
+
+
+def make_engine(layers, dtype, sd=None):
+    from tinybark_b200 import synthetic, weights
+    from tinybark_b200.engine import Engine
+
+    sd = state_dict(layers) if sd is None else sd
+    return Engine(weights.convert(sd, synthetic.config(layers)), synthetic.config(layers), dtype=dtype)
+
+
+def oracle_encode(layers, clip):
+    from oracle import encoder, frontend
+
+    return encoder.encode(state_dict(layers), frontend.features(clip), hidden=True)
+
+
+def gpu_encode(eng, clips):
+    plan = eng.plan([len(c) // 160 for c in clips])
+    samples, off = eng.upload(clips)
+    enc = eng.encode(eng.features(samples, off, plan), plan)
+    eng.check()
+    o = plan.t3_off.cpu().numpy()
+    e = enc.cpu().numpy()
+    return [e[o[i] : o[i + 1]] for i in range(len(clips))]
+
+
+def clips_of(seconds, seed=50):
+    from tinybark_b200 import synthetic
+
+    return [synthetic.to_float(synthetic.clip(s, seed + i)) for i, s in enumerate(seconds)]
+
+
+@pytest.mark.parametrize("dtype,tol", [("fp32", 1e-4), ("bf16", 2e-2)])
+def test_encoder_two_layers_packed_batch(dtype, tol):
+    eng = make_engine(2, dtype)
+    clips = clips_of((0.5, 1.0, 3.33, 0.02))
+    got = gpu_encode(eng, clips)
+    for c, g in zip(clips, got):
+        ref, _ = oracle_encode(2, c)
+        assert g.shape == ref.shape
+        assert max_rel(g, ref) < tol
+
+
+@pytest.mark.parametrize("dtype,tol", [("fp32", 1e-4), ("bf16", 2e-2)])
+def test_encoder_24_layers_10s(dtype, tol):
+    from tinybark_b200 import synthetic
+
+    eng = make_engine(24, dtype)
+    clip = synthetic.to_float(synthetic.clip(10.0, 0))
+    (got,) = gpu_encode(eng, [clip])
+    ref, _ = oracle_encode(24, clip)
+    assert got.shape == (125, 640)
+    err = max_rel(got, ref)
+    print(f"encoder 24 layers {dtype}: max-rel {err:.2e}")
+    assert err < tol
+
+
+def run_decode(eng, frames_list, feature_frames):
+    plan = eng.plan(feature_frames)
+    enc = torch.from_numpy(np.concatenate(frames_list)).cuda()
+    tokens, counts = eng.decode(enc, plan)
+    eng.check()
+    t, c = tokens.cpu().numpy(), counts.cpu().numpy()
+    return [t[i, : c[i]].tolist() for i in range(len(frames_list))]
+
+
+@pytest.mark.parametrize("case", ["mixed", "eos", "cap", "single"])
+def test_decode_matches_reference_loop(case):
+    from golden.make_golden import decode_frames, decode_weights
+
+    g = golden_json("decode.json")[case]
+    eng = make_engine(2, "fp32", decode_weights(g["case"]))
+    (tokens,) = run_decode(eng, [decode_frames(g["case"])], [g["case"]["feature_frames"]])
+    assert tokens == g["tokens"]
+
+
+def test_decode_lanes_are_independent():
+    """The four golden cases' encoder frames as four lanes of one batch, under the
+    'mixed' weights, each equal to the oracle's single-clip loop."""
+    from golden.make_golden import DECODE_CASES, decode_frames, decode_weights
+    from oracle import decoder
+
+    sd = decode_weights(DECODE_CASES["mixed"])
+    eng = make_engine(2, "fp32", sd)
+    cases = list(DECODE_CASES.values())
+    frames = [decode_frames(c) for c in cases]
+    ff = [c["feature_frames"] for c in cases]
+    got = run_decode(eng, frames, ff)
+    dec = decoder.Decoder(sd)
+    for fr, f, g in zip(frames, ff, got):
+        assert g == dec.greedy(fr, f)
+
+
+def test_end_to_end_fp32_tokens_match_oracle():
+    import tinybark_b200
+    from oracle import decoder
+    from tinybark_b200 import synthetic, weights
+
+    sd = state_dict(24)
+    bark = tinybark_b200.load("gpu", dtype="fp32", weights=(weights.convert(sd, synthetic.config(24)), synthetic.config(24)))
+    clip = synthetic.to_float(synthetic.clip(10.0, 0))
+    got = bark.tokens(clip)
+    enc, _ = oracle_encode(24, clip)
+    ref = decoder.Decoder(sd).greedy(enc, len(clip) // 160)
+    assert got == ref
+    assert bark.tokens(np.zeros(100, np.float32)) == []  # fewer than 2 frames
+    batch = bark.tokens_batch([clip[:16000], clip, np.zeros(10, np.float32)])
+    assert batch[1] == got and batch[2] == [] and batch[0] == bark.tokens(clip[:16000])
+
+
+def test_end_to_end_bf16_batch_consistent():
+    import tinybark_b200
+    from tinybark_b200 import synthetic, weights
+
+    sd = state_dict(24)
+    bark = tinybark_b200.load("gpu", weights=(weights.convert(sd, synthetic.config(24)), synthetic.config(24)))
+    clips = clips_of((2.0, 10.0, 5.5), seed=60)
+    batch = bark.tokens_batch(clips)
+    for c, b in zip(clips, batch):
+        assert bark.tokens(c) == b
+        assert len(b) > 0

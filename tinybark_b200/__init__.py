@@ -1,0 +1,94 @@
+"""Parakeet-TDT-0.6B-v3 / Underdog Bark speech-to-text on NVIDIA B200: the `cuda`
+backend of tinybark. Python host code calls hand-written sm_100a kernels through
+libtbcuda's C ABI; torch only allocates device memory.
+
+    bark = tinybark_b200.load()            # the converted weights tinybark caches
+    text = bark.transcribe(samples)        # 16 kHz mono float32 NumPy array
+    ids = bark.tokens_batch([a, b, c])     # many clips in one pass
+
+Same API as tinybark's backends (tinybark/backends.py:21-26; tinybark/tinygrad/__init__.py:21-35):
+`device`, `tokens`, `transcribe`, `transcribe_pcm`, plus `tokens_batch` and `close`.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from pathlib import Path
+
+import numpy as np
+
+__all__ = ["Bark", "load"]
+
+# Where tinybark caches the converted weights (tinybark/weights.py:17-21,106-120).
+CACHE = Path(os.environ.get("XDG_CACHE_HOME", Path.home() / ".cache")) / "tinybark"
+CONVERTED = "bark-6d34ed8639b2-v2"
+TOKENIZER_REPO = "nvidia/parakeet-tdt-0.6b-v3"
+
+
+def converted_weights(path: str | Path | None = None) -> tuple[dict[str, np.ndarray], dict]:
+    """tinybark's converted fp16 cache (tinybark/weights.py:106-120) and its config."""
+    from . import weights
+
+    base = Path(path) if path else CACHE / CONVERTED
+    tensors_path, config_path = base.with_suffix(".safetensors"), base.with_suffix(".json")
+    if not tensors_path.exists() or not config_path.exists():
+        raise FileNotFoundError(
+            f"{tensors_path} not found: run tinybark's weights.converted() once, or pass weights=(tensors, config)"
+        )
+    return weights.load(tensors_path), json.loads(config_path.read_text())
+
+
+class Bark:
+    def __init__(self, device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None,
+                 max_seconds: float = 30.0):
+        if device != "gpu":
+            raise RuntimeError(f"the cuda backend runs on the gpu, not {device!r}")
+        import torch
+
+        from . import lengths
+        from .engine import Engine
+
+        tensors, config = weights if weights is not None else converted_weights()
+        max_len = lengths.subsampled(int(max_seconds * 100), 3)
+        self.engine = Engine(tensors, config, dtype=dtype, device="cuda", max_len=max_len)
+        self.device = torch.cuda.get_device_name(self.engine.device)
+        self._tokenizer_path = tokenizer
+        self._tokenizer = None
+
+    def tokens(self, samples: np.ndarray) -> list[int]:
+        """Token ids of one clip (16 kHz mono float32), without start/blank/pad; EOS kept if hit."""
+        return self.engine.tokens_batch([samples])[0]
+
+    def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
+        """Token ids of many clips, packed into one GPU pass."""
+        return self.engine.tokens_batch(clips)
+
+    @property
+    def tokenizer(self):
+        if self._tokenizer is None:
+            from .text import Tokenizer
+
+            path = self._tokenizer_path
+            if path is None:
+                from huggingface_hub import hf_hub_download
+
+                path = hf_hub_download(TOKENIZER_REPO, "tokenizer.json")
+            self._tokenizer = Tokenizer(path)
+        return self._tokenizer
+
+    def transcribe(self, samples: np.ndarray) -> str:
+        return self.tokenizer.decode(self.tokens(samples))
+
+    def transcribe_pcm(self, pcm: bytes) -> str:
+        """16 kHz s16le mono PCM (tinybark/tinygrad/__init__.py:33-35)."""
+        return self.transcribe(np.frombuffer(pcm, dtype="<i2").astype(np.float32) / 32768)
+
+    def close(self) -> None:
+        self.engine = None
+
+
+def load(device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None) -> Bark:
+    """The cuda backend on this process's current GPU, bf16 by default ("fp32" for the
+    fp32 parity path)."""
+    return Bark(device, dtype=dtype, weights=weights, tokenizer=tokenizer)

@@ -1,0 +1,113 @@
+"""ctypes bindings of libtbcuda.so (include/tbcuda.h). The library is required: there
+is no CPU fallback, so importing this module without the built library raises."""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libtbcuda.so"
+
+F32, BF16 = 0, 1
+EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_BIAS_RELU, EPI_GLU, EPI_QKV, EPI_ARGMAX, EPI_LSTM = range(8)
+STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or dtype", 4: "workspace too small"}
+DEVICE_ERRORS = {1: "GEMM barrier wait timed out", 2: "attention barrier wait timed out", 4: "decode wait timed out"}
+
+HIDDEN, HEADS, HEAD_DIM, FFN, KERNEL, CHANNELS, MELS = 1024, 8, 128, 4096, 9, 256, 128
+VOCAB, BLANK, EOS, DURATIONS, PRED = 8193, 8192, 3, 5, 640
+TOKEN_ROWS, JOINT_ROWS = 8256, 8448
+
+vp, ll, i32, f32 = C.c_void_p, C.c_longlong, C.c_int, C.c_float
+
+
+class Epilogue(C.Structure):
+    _fields_ = [
+        ("kind", i32), ("out_dtype", i32), ("out", vp), ("ldo", ll), ("bias", vp), ("alpha", f32),
+        ("out2", vp), ("ldo2", ll), ("out3", vp), ("out4", vp), ("bias_u", vp), ("bias_v", vp),
+        ("keys", vp), ("keys2", vp), ("split", i32), ("split_end", i32), ("c", vp), ("h", vp), ("mask", vp),
+    ]
+
+
+class Layer(C.Structure):
+    _fields_ = [
+        ("norm_w", vp * 5), ("norm_b", vp * 5), ("ff1_w1", vp), ("ff1_w2", vp), ("ff2_w1", vp), ("ff2_w2", vp),
+        ("qkv", vp), ("o_proj", vp), ("pw1", vp), ("pw2", vp), ("bias_u", vp), ("bias_v", vp),
+        ("dw_w", vp), ("dw_b", vp), ("rel", vp),
+    ]
+
+
+class Model(C.Structure):
+    _fields_ = [
+        ("dtype", i32), ("layers", i32), ("max_len", i32),
+        ("sub0_w", vp), ("sub0_b", vp), ("sub_dw_w", vp * 2), ("sub_dw_b", vp * 2), ("sub_pw_w", vp * 2),
+        ("sub_pw_b", vp * 2), ("sub_linear_w", vp), ("sub_linear_b", vp), ("layer", C.POINTER(Layer)),
+        ("enc_proj_w", vp), ("enc_proj_b", vp),
+        ("embedding", vp), ("lstm_w", vp * 2), ("lstm_b", vp * 2), ("dec_proj_w", vp), ("dec_proj_b", vp),
+        ("joint_w", vp), ("joint_b", vp),
+        ("window", vp), ("mel_w", vp), ("mel_start", vp), ("mel_off", vp),
+    ]
+
+
+class Batch(C.Structure):
+    _fields_ = [
+        ("clips", i32), ("frames_total", i32), ("t1_total", i32), ("t2_total", i32), ("t3_total", i32),
+        ("frame_off", vp), ("t1_off", vp), ("t2_off", vp), ("t3_off", vp), ("t2_clip", vp), ("t3_clip", vp),
+        ("sub_tiles", vp), ("n_sub_tiles", i32), ("attn_tiles", vp), ("n_attn_tiles", i32), ("max_t3", i32),
+    ]
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH.name} is not built: run `python -m tinybark_b200.build` (needs nvcc). "
+            "The cuda backend has no CPU fallback."
+        )
+    lib = C.CDLL(str(LIB_PATH))
+    sz = C.c_size_t
+    P = C.POINTER
+    sig = {
+        "tb_version": (i32, []),
+        "tb_tile_rows": (i32, [i32, P(i32), P(i32)]),
+        "tb_launch_count": (ll, []),
+        "tb_last_cuda_error": (C.c_char_p, []),
+        "tb_sm_count": (i32, [i32, P(i32)]),
+        "tb_frontend_workspace_bytes": (sz, [i32, i32]),
+        "tb_frontend": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, sz, vp]),
+        "tb_layernorm": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
+        "tb_gemm": (i32, [i32, vp, ll, vp, i32, i32, i32, P(Epilogue), vp, vp]),
+        "tb_relpos_attention": (i32, [i32, vp, vp, vp, vp, vp, i32, P(Batch), vp, vp, vp]),
+        "tb_conv_depthwise": (i32, [i32, vp, vp, vp, P(Batch), vp, vp]),
+        "tb_subsample_workspace_bytes": (sz, [i32, i32, i32]),
+        "tb_subsample": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),
+        "tb_encoder_workspace_bytes": (sz, [i32, i32, i32]),
+        "tb_encoder_forward": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),
+        "tb_decode_workspace_bytes": (sz, [i32, i32]),
+        "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    return lib
+
+
+lib = _load()
+
+# Every symbol include/tbcuda.h declares, for the export check.
+EXPORTS = (
+    "tb_version", "tb_tile_rows", "tb_launch_count", "tb_last_cuda_error", "tb_sm_count", "tb_frontend_workspace_bytes", "tb_frontend",
+    "tb_layernorm", "tb_gemm", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
+    "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
+)
+
+
+def check(status: int, what: str) -> None:
+    """Raises RuntimeError on a non-zero status, as the reference's backends raise on failure."""
+    if status:
+        detail = lib.tb_last_cuda_error().decode() if status == 2 else ""
+        raise RuntimeError(f"{what}: {STATUS.get(status, status)} {detail}".strip())
+
+
+def tile_rows(dtype: int) -> tuple[int, int]:
+    a, b = C.c_int(), C.c_int()
+    check(lib.tb_tile_rows(dtype, C.byref(a), C.byref(b)), "tb_tile_rows")
+    return a.value, b.value

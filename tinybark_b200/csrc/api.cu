@@ -1,0 +1,275 @@
+// The extern "C" entry points of libtbcuda (declared in include/tbcuda.h) and the
+// encoder orchestration: subsampling, the conformer layers and the encoder projector,
+// as tinybark/tinygrad/model.py:140-158 (_encode) and tinybark/mojo/bark/gpu.mojo:399-426
+// (GpuEncoder.encode) run them.
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include "host.h"
+
+namespace tb {
+
+int frontend(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
+             int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream);
+size_t frontend_ws(int clips);
+size_t decode_ws(int dtype, int lanes);
+int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
+               int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, cudaStream_t stream);
+
+static thread_local std::string g_last_error;
+
+int fail_cuda() {
+  cudaError_t e = cudaGetLastError();
+  g_last_error = cudaGetErrorString(e);
+  return TB_ERR_CUDA;
+}
+
+static std::atomic<long long> g_launches{0};
+
+int check_launch() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return TB_OK;
+  g_last_error = cudaGetErrorString(e);
+  return TB_ERR_CUDA;
+}
+
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int sm_count() {
+  static int count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!count[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    count[dev] = n > 0 ? n : 148;
+  }
+  return count[dev];
+}
+
+// ---------------------------------------------------------------------------
+// Encoder
+
+struct EncWs {
+  float* x;
+  void *xn, *hid, *qu, *qv, *k, *v, *att, *glu, *dwo;
+  void* sub;
+  size_t sub_bytes;
+};
+
+static EncWs carve_encoder(void* ws, int dtype, int t2_total, int t3_total) {
+  const size_t e = dsize(dtype), R = t3_total;
+  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
+  auto take = [&](size_t bytes) {
+    void* q = p;
+    p += align256(bytes);
+    return q;
+  };
+  EncWs w;
+  w.x = (float*)take(R * TB_HIDDEN * 4);
+  w.xn = take(R * TB_HIDDEN * e);
+  w.hid = take(R * TB_FFN * e);
+  w.qu = take(R * TB_HIDDEN * e);
+  w.qv = take(R * TB_HIDDEN * e);
+  w.k = take(R * TB_HIDDEN * e);
+  w.v = take(R * TB_HIDDEN * e);
+  w.att = take(R * TB_HIDDEN * e);
+  w.glu = take(R * TB_HIDDEN * e);
+  w.dwo = take(R * TB_HIDDEN * e);
+  w.sub_bytes = subsample_ws(dtype, t2_total, t3_total);
+  w.sub = take(w.sub_bytes);
+  return w;
+}
+
+static size_t encoder_ws(int dtype, int t2_total, int t3_total) {
+  uint8_t* base = nullptr;
+  EncWs w = carve_encoder(base, dtype, t2_total, t3_total);
+  return (size_t)(reinterpret_cast<uint8_t*>(w.sub) - base) + align256(w.sub_bytes);
+}
+
+static int encoder_forward(const tb_model& m, const tb_batch& b, const float* feats, float* enc, void* ws,
+                           size_t ws_bytes, int* err, cudaStream_t s) {
+  if (b.t3_total <= 0) return TB_OK;
+  if (!m.layer || m.layers <= 0 || !feats || !enc || !ws) return TB_ERR_ARG;
+  if (ws_bytes < encoder_ws(m.dtype, b.t2_total, b.t3_total)) return TB_ERR_WORKSPACE;
+  if (b.max_t3 > m.max_len) return TB_ERR_ARG;
+  const int dt = m.dtype, R = b.t3_total;
+  EncWs w = carve_encoder(ws, dt, b.t2_total, b.t3_total);
+
+  if (int rc = subsample(m, b, feats, w.x, w.sub, w.sub_bytes, err, s)) return rc;
+
+  tb_epilogue silu = {};
+  silu.kind = TB_EPI_SILU;
+  silu.out_dtype = dt;
+  silu.out = w.hid;
+  silu.ldo = TB_FFN;
+  tb_epilogue half = {};
+  half.kind = TB_EPI_RESIDUAL;
+  half.out = w.x;
+  half.ldo = TB_HIDDEN;
+  half.alpha = 0.5f;
+  tb_epilogue full = half;
+  full.alpha = 1.0f;
+  tb_epilogue glu = {};
+  glu.kind = TB_EPI_GLU;
+  glu.out_dtype = dt;
+  glu.out = w.glu;
+  glu.ldo = TB_HIDDEN;
+  tb_epilogue qkv = {};
+  qkv.kind = TB_EPI_QKV;
+  qkv.out_dtype = dt;
+  qkv.out = w.qu;
+  qkv.out2 = w.qv;
+  qkv.out3 = w.k;
+  qkv.out4 = w.v;
+  qkv.ldo = TB_HIDDEN;
+
+  const tb_layer& first = m.layer[0];
+  if (int rc = layernorm(w.x, first.norm_w[0], first.norm_b[0], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
+  for (int i = 0; i < m.layers; ++i) {
+    const tb_layer& L = m.layer[i];
+    // x += 0.5 * FF1(LN(x))  (the LN was applied at the end of the previous layer)
+    if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.ff1_w1, R, TB_FFN, TB_HIDDEN, silu, err, s)) return rc;
+    if (int rc = gemm(dt, w.hid, TB_FFN, L.ff1_w2, R, TB_HIDDEN, TB_FFN, half, err, s)) return rc;
+    // x += MHSA(LN(x))
+    if (int rc = layernorm(w.x, L.norm_w[1], L.norm_b[1], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
+    qkv.bias_u = L.bias_u;
+    qkv.bias_v = L.bias_v;
+    if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.qkv, R, 3 * TB_HIDDEN, TB_HIDDEN, qkv, err, s)) return rc;
+    if (int rc = relpos_attention(dt, w.qu, w.qv, w.k, w.v, L.rel, m.max_len, b, w.att, err, s)) return rc;
+    if (int rc = gemm(dt, w.att, TB_HIDDEN, L.o_proj, R, TB_HIDDEN, TB_HIDDEN, full, err, s)) return rc;
+    // x += Conv(LN(x))
+    if (int rc = layernorm(w.x, L.norm_w[2], L.norm_b[2], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
+    if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.pw1, R, 2 * TB_HIDDEN, TB_HIDDEN, glu, err, s)) return rc;
+    if (int rc = conv_depthwise(dt, w.glu, L.dw_w, L.dw_b, b, w.dwo, s)) return rc;
+    if (int rc = gemm(dt, w.dwo, TB_HIDDEN, L.pw2, R, TB_HIDDEN, TB_HIDDEN, full, err, s)) return rc;
+    // x += 0.5 * FF2(LN(x))
+    if (int rc = layernorm(w.x, L.norm_w[3], L.norm_b[3], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
+    if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.ff2_w1, R, TB_FFN, TB_HIDDEN, silu, err, s)) return rc;
+    if (int rc = gemm(dt, w.hid, TB_FFN, L.ff2_w2, R, TB_HIDDEN, TB_FFN, half, err, s)) return rc;
+    // x = LN_out(x), fused with the next layer's first LN (or, after the last layer, the
+    // projector's input cast).
+    if (i + 1 < m.layers) {
+      const tb_layer& N = m.layer[i + 1];
+      if (int rc = layernorm(w.x, L.norm_w[4], L.norm_b[4], w.x, N.norm_w[0], N.norm_b[0], w.xn, dt, R, s)) return rc;
+    } else {
+      if (int rc = layernorm(w.x, L.norm_w[4], L.norm_b[4], w.x, nullptr, nullptr, w.xn, dt, R, s)) return rc;
+    }
+  }
+  tb_epilogue pj = {};
+  pj.kind = TB_EPI_STORE;
+  pj.out_dtype = TB_F32;
+  pj.out = enc;
+  pj.ldo = TB_PRED;
+  pj.bias = m.enc_proj_b;
+  return gemm(dt, w.xn, TB_HIDDEN, m.enc_proj_w, R, TB_PRED, TB_HIDDEN, pj, err, s);
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+int tb_version(void) { return 1; }
+
+long long tb_launch_count(void) { return g_launches.load(); }
+
+int tb_tile_rows(int dtype, int* sub_rows, int* attn_rows) {
+  if (!sub_rows || !attn_rows || (dtype != TB_F32 && dtype != TB_BF16)) return TB_ERR_ARG;
+  *sub_rows = 2;
+  *attn_rows = attention_tile_rows(dtype);
+  return TB_OK;
+}
+
+const char* tb_last_cuda_error(void) { return g_last_error.c_str(); }
+
+int tb_sm_count(int device, int* out) {
+  if (!out) return TB_ERR_ARG;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return fail_cuda();
+  *out = n;
+  return TB_OK;
+}
+
+size_t tb_frontend_workspace_bytes(int clips, int frames_total) {
+  (void)frames_total;
+  return frontend_ws(clips);
+}
+
+int tb_frontend(const tb_model* m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
+                int frames_total, int max_frames, float* feats, void* ws, size_t ws_bytes, void* stream) {
+  (void)max_frames;
+  if (!m) return TB_ERR_ARG;
+  return frontend(*m, samples, sample_off, frame_off, clips, frames_total, feats, ws, ws_bytes, as_stream(stream));
+}
+
+int tb_layernorm(const float* x, const float* w, const float* b, float* x_out, const float* w2, const float* b2,
+                 void* y, int y_dtype, int rows, void* stream) {
+  return layernorm(x, w, b, x_out, w2, b2, y, y_dtype, rows, as_stream(stream));
+}
+
+int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue* epi,
+            int* err, void* stream) {
+  if (!epi) return TB_ERR_ARG;
+  return gemm(dtype, a, lda, w, m, n, k, *epi, err, as_stream(stream));
+}
+
+int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
+                        int max_len, const tb_batch* batch, void* out, int* err, void* stream) {
+  if (!batch) return TB_ERR_ARG;
+  return relpos_attention(dtype, qu, qv, k, v, rel, max_len, *batch, out, err, as_stream(stream));
+}
+
+int tb_conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch* batch, void* out,
+                      void* stream) {
+  if (!batch) return TB_ERR_ARG;
+  return conv_depthwise(dtype, glu, w, b, *batch, out, as_stream(stream));
+}
+
+size_t tb_subsample_workspace_bytes(int dtype, int t2_total, int t3_total) {
+  return subsample_ws(dtype, t2_total, t3_total);
+}
+
+int tb_subsample(const tb_model* m, const tb_batch* batch, const float* feats, float* x, void* ws, size_t ws_bytes,
+                 int* err, void* stream) {
+  if (!m || !batch) return TB_ERR_ARG;
+  return subsample(*m, *batch, feats, x, ws, ws_bytes, err, as_stream(stream));
+}
+
+size_t tb_encoder_workspace_bytes(int dtype, int t2_total, int t3_total) {
+  return encoder_ws(dtype, t2_total, t3_total);
+}
+
+int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* feats, float* enc, void* ws,
+                       size_t ws_bytes, int* err, void* stream) {
+  if (!m || !batch) return TB_ERR_ARG;
+  return encoder_forward(*m, *batch, feats, enc, ws, ws_bytes, err, as_stream(stream));
+}
+
+size_t tb_decode_workspace_bytes(int dtype, int lanes) { return decode_ws(dtype, lanes); }
+
+int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
+                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, void* stream) {
+  if (!m) return TB_ERR_ARG;
+  return tdt_decode(*m, enc, enc_off, cap, lanes, max_cap, tokens, counts, ws, ws_bytes, host_flag, err,
+                    as_stream(stream));
+}
+
+}  // extern "C"

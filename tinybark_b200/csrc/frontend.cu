@@ -1,0 +1,185 @@
+// Log-mel front-end, replacing tinybark/audio.py:42-55 (a numpy port of transformers'
+// ParakeetFeatureExtractor):
+//   pre-emphasis x[n] - 0.97 x[n-1] (x[0] kept), zero padding of 256 on each side,
+//   frames of 512 at hop 160 (frames = samples // 160), the 400-tap Hann window centred
+//   in the frame, |rfft|^2, 128 slaney mel filters, log(. + 2^-24), then per clip and
+//   per mel bin (m - mean) / (std + 1e-5), std with ddof 1.
+//
+// logmel_kernel: one warp per frame. The 512-point real FFT is a 256-point complex FFT
+// of (even, odd) sample pairs (radix-2, in shared memory) followed by the standard
+// split into the 257 real-input bins. Twiddles come from sincospi in fp64 per block.
+// stats_kernel / finish_kernel / normalize_kernel: per-clip mean and std per mel bin,
+// accumulated in fp64 over frame ranges, then applied in place.
+#include "common.cuh"
+#include "host.h"
+
+namespace tb {
+
+constexpr int FE_WARPS = 8;
+constexpr int FE_SPLIT = 8;  // frame ranges per clip for the statistics
+constexpr float PREEMPH = 0.97f;
+
+__device__ __forceinline__ int find_clip(const int* off, int clips, int row) {
+  int lo = 0, hi = clips;  // off[lo] <= row < off[hi]
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (off[mid] <= row) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float preemph_sample(const float* x, long long n, long long len) {
+  if (n < 0 || n >= len) return 0.f;
+  // Rounded as numpy rounds it: the product, then the difference.
+  return n == 0 ? x[0] : __fsub_rn(x[n], __fmul_rn(PREEMPH, x[n - 1]));
+}
+
+__global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ samples,
+                                                     const long long* __restrict__ sample_off,
+                                                     const int* __restrict__ frame_off, int clips, int frames_total,
+                                                     const float* __restrict__ window, const float* __restrict__ mel_w,
+                                                     const int* __restrict__ mel_start, const int* __restrict__ mel_off,
+                                                     float* __restrict__ feats) {
+  __shared__ float2 tw256[128];     // e^{-2 pi i k / 256}
+  __shared__ float2 tw512[257];     // e^{-2 pi i k / 512}
+  __shared__ float2 z[FE_WARPS][256];
+  __shared__ float pw[FE_WARPS][260];
+  __shared__ float win[512];
+  for (int k = threadIdx.x; k < 128; k += 256) {
+    double s, c;
+    sincospi(-2.0 * k / 256.0, &s, &c);
+    tw256[k] = make_float2((float)c, (float)s);
+  }
+  for (int k = threadIdx.x; k < 257; k += 256) {
+    double s, c;
+    sincospi(-2.0 * k / 512.0, &s, &c);
+    tw512[k] = make_float2((float)c, (float)s);
+  }
+  for (int k = threadIdx.x; k < 512; k += 256) win[k] = window[k];
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * FE_WARPS + warp;
+  if (row >= frames_total) return;
+  const int clip = find_clip(frame_off, clips, row);
+  const int f = row - frame_off[clip];
+  const float* x = samples + sample_off[clip];
+  const long long len = sample_off[clip + 1] - sample_off[clip];
+  float2* zw = z[warp];
+
+  // Windowed frame, paired as complex z[n] = w[2n] + i w[2n+1], stored bit-reversed.
+  for (int n = lane; n < 256; n += 32) {
+    const int k0 = 2 * n, k1 = 2 * n + 1;
+    const long long p0 = (long long)f * 160 + k0 - 256, p1 = p0 + 1;
+    const float a = win[k0] != 0.f ? __fmul_rn(preemph_sample(x, p0, len), win[k0]) : 0.f;
+    const float b = win[k1] != 0.f ? __fmul_rn(preemph_sample(x, p1, len), win[k1]) : 0.f;
+    zw[__brev(n) >> 24] = make_float2(a, b);
+  }
+  __syncwarp();
+  // 8 radix-2 stages, 128 butterflies each, 4 per lane.
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const int half = 1 << s;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int bfly = lane + 32 * i;
+      const int grp = bfly >> s, pos = bfly & (half - 1);
+      const int i0 = (grp << (s + 1)) + pos, i1 = i0 + half;
+      const float2 t = tw256[pos << (7 - s)];
+      const float2 u = zw[i0], v = zw[i1];
+      const float2 vt = make_float2(v.x * t.x - v.y * t.y, v.x * t.y + v.y * t.x);
+      zw[i0] = make_float2(u.x + vt.x, u.y + vt.y);
+      zw[i1] = make_float2(u.x - vt.x, u.y - vt.y);
+    }
+    __syncwarp();
+  }
+  // Split into the real-input spectrum, power per bin.
+  for (int k = lane; k <= 256; k += 32) {
+    const float2 zk = zw[k & 255], zc = zw[(256 - k) & 255];
+    const float er = 0.5f * (zk.x + zc.x), ei = 0.5f * (zk.y - zc.y);   // (Z[k] + conj Z[256-k]) / 2
+    const float orr = 0.5f * (zk.y + zc.y), oi = -0.5f * (zk.x - zc.x); // (Z[k] - conj Z[256-k]) / 2i
+    const float2 w = tw512[k];
+    const float xr = er + (w.x * orr - w.y * oi), xi = ei + (w.x * oi + w.y * orr);
+    pw[warp][k] = xr * xr + xi * xi;
+  }
+  __syncwarp();
+  float* out = feats + (long long)row * TB_MELS;
+  for (int m = lane; m < TB_MELS; m += 32) {
+    const int b0 = mel_start[m], o0 = mel_off[m], o1 = mel_off[m + 1];
+    float acc = 0.f;
+    for (int o = o0; o < o1; ++o) acc = fmaf(mel_w[o], pw[warp][b0 + o - o0], acc);
+    out[m] = logf(acc + 5.9604644775390625e-8f);  // 2^-24
+  }
+}
+
+// Partial sums over one of FE_SPLIT frame ranges of a clip: (sum, sum of squares) per mel.
+__global__ void __launch_bounds__(TB_MELS) stats_kernel(const float* __restrict__ feats, const int* __restrict__ frame_off,
+                                                        double2* __restrict__ part) {
+  const int clip = blockIdx.x, split = blockIdx.y, m = threadIdx.x;
+  const int base = frame_off[clip], n = frame_off[clip + 1] - base;
+  const int lo = (int)((long long)n * split / FE_SPLIT), hi = (int)((long long)n * (split + 1) / FE_SPLIT);
+  double s = 0.0, q = 0.0;
+  for (int t = lo; t < hi; ++t) {
+    const double v = feats[(long long)(base + t) * TB_MELS + m];
+    s += v;
+    q += v * v;
+  }
+  part[((long long)clip * FE_SPLIT + split) * TB_MELS + m] = make_double2(s, q);
+}
+
+__global__ void __launch_bounds__(TB_MELS) finish_kernel(const double2* __restrict__ part,
+                                                         const int* __restrict__ frame_off, float2* __restrict__ stats) {
+  const int clip = blockIdx.x, m = threadIdx.x;
+  const double n = frame_off[clip + 1] - frame_off[clip];
+  double s = 0.0, q = 0.0;
+  for (int k = 0; k < FE_SPLIT; ++k) {
+    const double2 p = part[((long long)clip * FE_SPLIT + k) * TB_MELS + m];
+    s += p.x;
+    q += p.y;
+  }
+  const double mean = s / n;
+  double var = (q - s * mean) / (n - 1.0);
+  var = var > 0.0 ? var : 0.0;
+  const float stdv = (float)sqrt(var);
+  stats[(long long)clip * TB_MELS + m] = make_float2((float)mean, stdv + 1e-5f);
+}
+
+__global__ void __launch_bounds__(256) normalize_kernel(float* __restrict__ feats, const int* __restrict__ frame_off,
+                                                        int clips, int frames_total, const float2* __restrict__ stats) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= frames_total) return;
+  const int clip = find_clip(frame_off, clips, row);
+  float* r = feats + (long long)row * TB_MELS;
+  const float2* st = stats + (long long)clip * TB_MELS;
+  for (int m = lane; m < TB_MELS; m += 32) {
+    const float2 s = st[m];
+    r[m] = (r[m] - s.x) / s.y;
+  }
+}
+
+size_t frontend_ws(int clips) {
+  return align256((size_t)clips * FE_SPLIT * TB_MELS * sizeof(double2)) + align256((size_t)clips * TB_MELS * sizeof(float2));
+}
+
+int frontend(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
+             int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (clips <= 0 || frames_total <= 0) return TB_OK;
+  if (!samples || !sample_off || !frame_off || !feats || !m.window || !m.mel_w || !m.mel_start || !m.mel_off)
+    return TB_ERR_ARG;
+  if (ws_bytes < frontend_ws(clips)) return TB_ERR_WORKSPACE;
+  double2* part = reinterpret_cast<double2*>(ws);
+  float2* stats = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(ws) +
+                                            align256((size_t)clips * FE_SPLIT * TB_MELS * sizeof(double2)));
+  logmel_kernel<<<(frames_total + FE_WARPS - 1) / FE_WARPS, 256, 0, stream>>>(
+      samples, sample_off, frame_off, clips, frames_total, m.window, m.mel_w, m.mel_start, m.mel_off, feats);
+  if (int rc = check_launch()) return rc;
+  stats_kernel<<<dim3(clips, FE_SPLIT), TB_MELS, 0, stream>>>(feats, frame_off, part);
+  if (int rc = check_launch()) return rc;
+  finish_kernel<<<clips, TB_MELS, 0, stream>>>(part, frame_off, stats);
+  if (int rc = check_launch()) return rc;
+  normalize_kernel<<<(frames_total + 7) / 8, 256, 0, stream>>>(feats, frame_off, clips, frames_total, stats);
+  return check_launch();
+}
+
+}  // namespace tb

@@ -1,0 +1,344 @@
+// Linear layers: C = A (M x K, row-major) * W (N x K, row-major)^T with a fused
+// epilogue. Replaces tinybark/tinygrad/model.py:37-40 (linear) and the MAX matmul calls
+// of tinybark/mojo/bark/gpu.mojo:429-436.
+//
+// bf16: a persistent, warp-specialized tcgen05 kernel. Warp 0 issues TMA tile loads
+// into a STAGES-deep shared-memory ring, warp 1 issues tcgen05.mma (128 x BN x 16 per
+// instruction) into one of two tensor-memory accumulators, warps 2-5 drain the other
+// accumulator through the epilogue, so a tile's epilogue overlaps the next tile's
+// main loop.
+// fp32: a CUDA-core kernel, 128 x 128 tiles, 8 x 8 outputs per thread, for the fp32
+// parity path.
+#include "epilogue.cuh"
+#include "host.h"
+
+namespace tb {
+
+// ---------------------------------------------------------------------------
+// tcgen05 bf16 kernel
+
+template <int BN>
+struct TcCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+};
+
+struct TcBars {
+  uint64_t full[8], empty[8], tfull[2], tempty[2], done;
+  uint32_t tmem;
+  int abort;
+};
+
+// Bounded wait used while winding down: ignores the abort flag.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - start > TB_WAIT_NS) break;
+}
+
+// One lane waits, the warp follows.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, TB_DEV_GEMM_TIMEOUT, abort);
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
+                   const tb_epilogue e, int* err) {
+  using C = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  TcBars* bars = reinterpret_cast<TcBars*>(smem + C::STAGES * C::STAGE_BYTES);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->tfull[a], 1);
+      mbar_init(&bars->tempty[a], 4);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+
+  const int m_tiles = (M + C::BM - 1) / C::BM, n_tiles = N / BN, tiles = m_tiles * n_tiles, kb_count = K / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tw);
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int mt = t / n_tiles, nt = t % n_tiles;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, err, TB_DEV_GEMM_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          mbar_expect_tx(&bars->full[s], C::STAGE_BYTES);
+          tma_load_2d(sa, &ta, &bars->full[s], kb * C::BK, mt * C::BM);
+          tma_load_2d(sa + C::A_BYTES, &tw, &bars->full[s], kb * C::BK, nt * BN);
+          ++issued;
+          if (++s == C::STAGES) s = 0, ph ^= 1;
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before the CTA exits.
+        long long back = issued < C::STAGES ? issued : C::STAGES;
+        for (long long i = 1; i <= back; ++i) {
+          long long idx = issued - i;
+          drain_wait(&bars->full[idx % C::STAGES], (uint32_t)((idx / C::STAGES) & 1));
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(C::BM, BN);
+      int s = 0, acc = 0;
+      uint32_t ph = 0, acc_ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&bars->tempty[acc], acc_ph ^ 1, err, TB_DEV_GEMM_TIMEOUT, abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(&bars->full[s], ph, err, TB_DEV_GEMM_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint64_t ad = sdesc_sw128(sa), bd = sdesc_sw128(sa + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / 16; ++k) umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&bars->empty[s]);
+          if (++s == C::STAGES) s = 0, ph ^= 1;
+        }
+        if (!ok) break;
+        umma_commit(&bars->tfull[acc]);
+        if (++acc == 2) acc = 0, acc_ph ^= 1;
+      }
+      // Every MMA issued has completed once this commit arrives.
+      umma_commit(&bars->done);
+      drain_wait(&bars->done, 0);
+    }
+  } else {
+    const int q = warp & 3;  // tensor-memory lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int mt = t / n_tiles, nt = t % n_tiles;
+      if (!warp_wait(&bars->tfull[acc], acc_ph, err, abort)) break;
+      tc_fence_after();
+      const int m = mt * C::BM + row;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
+      ArgmaxAcc am;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
+        if (m < M) {
+          const int n0 = nt * BN + c;
+          if (e.kind == TB_EPI_ARGMAX) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) am.add(e, n0 + j, __uint_as_float(r[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              epi_group(e, m, n0 + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                        __uint_as_float(r[j + 3]));
+          }
+        }
+      }
+      if (e.kind == TB_EPI_ARGMAX && m < M) am.flush(e, m);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+      if (++acc == 2) acc = 0, acc_ph ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fp32 CUDA-core kernel
+
+constexpr int SG_BM = 128, SG_BN = 128, SG_BK = 16, SG_PAD = 4;
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, long long lda,
+                                                       const float* __restrict__ W, int M, int N, int K,
+                                                       const tb_epilogue e) {
+  __shared__ __align__(16) float As[2][SG_BK][SG_BM + SG_PAD];
+  __shared__ __align__(16) float Ws[2][SG_BK][SG_BN + SG_PAD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * SG_BM, n0 = blockIdx.x * SG_BN;
+  // Loader mapping: rows lr and lr + 64, k offset lk.
+  const int lr = tid >> 2, lk = (tid & 3) * 4;
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  float4 ra[2], rw[2];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int m = m0 + lr + h * 64;
+      ra[h] = m < M ? *reinterpret_cast<const float4*>(A + (long long)m * lda + k0 + lk) : make_float4(0, 0, 0, 0);
+      int n = n0 + lr + h * 64;
+      rw[h] = *reinterpret_cast<const float4*>(W + (long long)n * K + k0 + lk);
+    }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int r = lr + h * 64;
+      As[buf][lk + 0][r] = ra[h].x, As[buf][lk + 1][r] = ra[h].y, As[buf][lk + 2][r] = ra[h].z,
+      As[buf][lk + 3][r] = ra[h].w;
+      Ws[buf][lk + 0][r] = rw[h].x, Ws[buf][lk + 1][r] = rw[h].y, Ws[buf][lk + 2][r] = rw[h].z,
+      Ws[buf][lk + 3][r] = rw[h].w;
+    }
+  };
+
+  load(0);
+  stash(0);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = 0; k0 < K; k0 += SG_BK) {
+    const bool more = k0 + SG_BK < K;
+    if (more) load(k0 + SG_BK);
+#pragma unroll
+    for (int k = 0; k < SG_BK; ++k) {
+      float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+      float4 w0 = *reinterpret_cast<const float4*>(&Ws[buf][k][tx * 4]);
+      float4 w1 = *reinterpret_cast<const float4*>(&Ws[buf][k][64 + tx * 4]);
+      float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
+    }
+    if (more) {
+      stash(buf ^ 1);
+      __syncthreads();
+      buf ^= 1;
+    }
+  }
+
+  if (e.kind == TB_EPI_ARGMAX) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+      ArgmaxAcc am;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) am.add(e, n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4), acc[i][j]);
+      // Reduce over the 16 threads sharing this row (same ty, a half warp).
+#pragma unroll
+      for (int o = 8; o; o >>= 1) {
+        unsigned long long t1 = __shfl_xor_sync(0xffffffffu, am.tok, o), t2 = __shfl_xor_sync(0xffffffffu, am.dur, o);
+        am.tok = t1 > am.tok ? t1 : am.tok;
+        am.dur = t2 > am.dur ? t2 : am.dur;
+      }
+      if (tx == 0 && m < M) am.flush(e, m);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (m >= M) continue;
+    epi_group(e, m, n0 + tx * 4, acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    epi_group(e, m, n0 + 64 + tx * 4, acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+static bool encode_tmap(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
+                        int box_rows) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN>
+static int launch_tc(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
+                     cudaStream_t stream) {
+  using C = TcCfg<BN>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return fail_cuda();
+    configured = true;
+  }
+  CUtensorMap ta, tw;
+  if (!encode_tmap(&ta, a, m, k, lda, C::BM) || !encode_tmap(&tw, w, n, k, k, BN)) return TB_ERR_CUDA;
+  int tiles = ((m + C::BM - 1) / C::BM) * (n / BN);
+  int grid = tiles < sm_count() ? tiles : sm_count();
+  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, stream>>>(ta, tw, m, n, k, e, err);
+  return check_launch();
+}
+
+int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
+         cudaStream_t stream) {
+  if (m <= 0) return TB_OK;
+  if (n <= 0 || k <= 0 || !a || !w) return TB_ERR_ARG;
+  if (e.kind == TB_EPI_ARGMAX && (!e.keys || !e.keys2 || !e.bias)) return TB_ERR_ARG;
+  if (dtype == TB_BF16) {
+    if (k % 64 || lda % 8 || (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+      return TB_ERR_UNSUPPORTED;
+    if (n % 256 == 0) return launch_tc<256>(a, lda, w, m, n, k, e, err, stream);
+    if (n % 128 == 0) return launch_tc<128>(a, lda, w, m, n, k, e, err, stream);
+    return TB_ERR_UNSUPPORTED;
+  }
+  if (dtype != TB_F32) return TB_ERR_ARG;
+  if (k % SG_BK || n % SG_BN || lda % 4) return TB_ERR_UNSUPPORTED;
+  dim3 grid(n / SG_BN, (m + SG_BM - 1) / SG_BM);
+  gemm_f32_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(w),
+                                            m, n, k, e);
+  return check_launch();
+}
+
+}  // namespace tb

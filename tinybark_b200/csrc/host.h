@@ -1,0 +1,35 @@
+// Host-side helpers shared by the .cu files of libtbcuda.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/tbcuda.h"
+
+namespace tb {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn tensor_map_encoder();
+int sm_count();
+int fail_cuda();     // records cudaGetLastError() and returns TB_ERR_CUDA
+int check_launch();  // TB_OK, or fail_cuda() if the last launch failed
+
+int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
+         cudaStream_t stream);
+int layernorm(const float* x, const float* w, const float* b, float* x_out, const float* w2, const float* b2, void* y,
+              int y_dtype, int rows, cudaStream_t stream);
+int relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
+                     int max_len, const tb_batch& batch, void* out, int* err, cudaStream_t stream);
+int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch& batch, void* out,
+                   cudaStream_t stream);
+int subsample(const tb_model& m, const tb_batch& batch, const float* feats, float* x, void* ws, size_t ws_bytes,
+              int* err, cudaStream_t stream);
+size_t subsample_ws(int dtype, int t2_total, int t3_total);
+int attention_tile_rows(int dtype);
+
+inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+inline size_t dsize(int dtype) { return dtype == TB_BF16 ? 2 : 4; }
+
+}  // namespace tb

@@ -1,0 +1,316 @@
+"""Host side of the cuda backend: the converted weights repacked on the GPU for the
+kernels, batch planning, and the front-end -> encoder -> TDT decode pipeline, all
+through libtbcuda's C ABI. torch only allocates device memory and supplies the stream.
+
+Clips of a batch are packed end to end at every stage (no padding): the reference pads
+to multiples of 2.56 s and masks (tinybark/tinygrad/model.py:15-20,140-158), and on
+valid frames both give the same values, since every masked position the reference
+zeroes is a zero-padding position here.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from . import lengths, tables
+
+DTYPES = {"fp32": L.F32, "bf16": L.BF16}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def positions(length: int) -> torch.Tensor:
+    """(2*length-1, 1024) float32: row n is relative position length-1-n as interleaved
+    [sin, cos] (tinybark/tinygrad/model.py:30-34), computed in float32 as
+    transformers' ParakeetEncoderRelPositionalEncoding does."""
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, L.HIDDEN, 2, dtype=torch.int64).float() / L.HIDDEN))
+    pos = torch.arange(length - 1, -length, -1).float()
+    freqs = pos[:, None] * inv_freq[None, :]
+    return torch.stack([freqs.sin(), freqs.cos()], -1).reshape(2 * length - 1, L.HIDDEN)
+
+
+@dataclass
+class Plan:
+    """Offsets and work lists of one batch, on the device, behind a tb_batch."""
+
+    frames: np.ndarray
+    t3: np.ndarray
+    batch: L.Batch
+    meta: torch.Tensor
+    t3_off: torch.Tensor
+    frame_off: torch.Tensor
+    caps: torch.Tensor
+    max_cap: int
+
+
+def plan_arrays(frames, sub_rows: int, attn_rows: int) -> dict[str, np.ndarray]:
+    """Host-side metadata of a packed batch: cumulative row offsets at each subsampling
+    stage, the clip of every row, the (clip, first row) work items of the subsampling
+    and attention kernels (longest clips first) and each clip's greedy-loop cap."""
+    f = np.asarray(frames, np.int64)
+    if len(f) == 0 or f.min() < 2:
+        raise ValueError("every clip needs at least 2 feature frames")
+    t1 = (f - 1) // 2 + 1
+    t2 = (t1 - 1) // 2 + 1
+    t3 = (t2 - 1) // 2 + 1
+    off = lambda n: np.concatenate([[0], np.cumsum(n)]).astype(np.int32)
+    ids = np.arange(len(f), dtype=np.int32)
+    order = np.argsort(-t3, kind="stable")
+    tiles = lambda n, step: np.array([(c, r) for c in order for r in range(0, int(n[c]), step)], np.int32).reshape(-1)
+    return {
+        "frames": f, "t3": t3,
+        "frame_off": off(f), "t1_off": off(t1), "t2_off": off(t2), "t3_off": off(t3),
+        "t2_clip": np.repeat(ids, t2), "t3_clip": np.repeat(ids, t3),
+        "sub_tiles": tiles(t2, sub_rows), "attn_tiles": tiles(t3, attn_rows),
+        "caps": np.array([lengths.decode_cap(int(n)) for n in f], np.int32),
+    }
+
+
+class Engine:
+    """The model on one GPU. `tensors` is the converted layout (tinybark/weights.py:62-89)
+    as float32 arrays; `dtype` is "fp32" (parity) or "bf16" (throughput)."""
+
+    def __init__(self, tensors: dict[str, np.ndarray], config: dict, dtype: str = "bf16", device="cuda",
+                 max_len: int = 512):
+        if not torch.cuda.is_available():
+            raise RuntimeError("the cuda backend needs a CUDA GPU")
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.dtype = DTYPES[dtype]
+        self.tdtype = torch.bfloat16 if self.dtype == L.BF16 else torch.float32
+        self.layers = config["encoder_config"]["num_hidden_layers"]
+        self.sub_rows, self.attn_rows = L.tile_rows(self.dtype)
+        self._keep: list[torch.Tensor] = []
+        with torch.cuda.device(self.device):
+            self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.host_flag = torch.zeros(4, dtype=torch.int32).pin_memory()
+            self._pack(tensors)
+            self.max_len = 0
+            self.ensure_len(max_len)
+
+    # ------------------------------------------------------------------ weights
+
+    def _mat(self, a: np.ndarray) -> torch.Tensor:
+        t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(self.device, self.tdtype).contiguous()
+        self._keep.append(t)
+        return t
+
+    def _vec(self, a: np.ndarray, dtype=torch.float32) -> torch.Tensor:
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device, dtype).contiguous()
+        self._keep.append(t)
+        return t
+
+    def _pack(self, w: dict[str, np.ndarray]) -> None:
+        m = L.Model()
+        m.dtype, m.layers = self.dtype, self.layers
+        p = "encoder.subsampling."
+        m.sub0_w = _ptr(self._vec(w[p + "layers.0.weight"].reshape(L.CHANNELS, 9)))
+        m.sub0_b = _ptr(self._vec(w[p + "layers.0.bias"]))
+        for i, (dw, pw) in enumerate(((2, 3), (5, 6))):
+            m.sub_dw_w[i] = _ptr(self._vec(w[p + f"layers.{dw}.weight"].reshape(L.CHANNELS, 9)))
+            m.sub_dw_b[i] = _ptr(self._vec(w[p + f"layers.{dw}.bias"]))
+            m.sub_pw_w[i] = _ptr(self._mat(w[p + f"layers.{pw}.weight"].reshape(L.CHANNELS, L.CHANNELS)))
+            m.sub_pw_b[i] = _ptr(self._vec(w[p + f"layers.{pw}.bias"]))
+        # Linear input columns: the reference's (channel, frequency) to (frequency, channel).
+        lin = w[p + "linear.weight"].reshape(L.HIDDEN, L.CHANNELS, 16).transpose(0, 2, 1).reshape(L.HIDDEN, -1)
+        m.sub_linear_w = _ptr(self._mat(lin))
+        m.sub_linear_b = _ptr(self._vec(w[p + "linear.bias"]))
+
+        self._layer_arr = (L.Layer * self.layers)()
+        self._rel_w: list[torch.Tensor] = []
+        norms = ("norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2", "norm_out")
+        for i in range(self.layers):
+            q = f"encoder.layers.{i}."
+            lay = self._layer_arr[i]
+            for j, n in enumerate(norms):
+                lay.norm_w[j] = _ptr(self._vec(w[q + n + ".weight"]))
+                lay.norm_b[j] = _ptr(self._vec(w[q + n + ".bias"]))
+            lay.ff1_w1 = _ptr(self._mat(w[q + "feed_forward1.linear1.weight"]))
+            lay.ff1_w2 = _ptr(self._mat(w[q + "feed_forward1.linear2.weight"]))
+            lay.ff2_w1 = _ptr(self._mat(w[q + "feed_forward2.linear1.weight"]))
+            lay.ff2_w2 = _ptr(self._mat(w[q + "feed_forward2.linear2.weight"]))
+            a = q + "self_attn."
+            lay.qkv = _ptr(self._mat(w[a + "qkv"]))
+            lay.o_proj = _ptr(self._mat(w[a + "o_proj.weight"]))
+            lay.bias_u = _ptr(self._vec(w[a + "bias_u"].reshape(-1)))
+            lay.bias_v = _ptr(self._vec(w[a + "bias_v"].reshape(-1)))
+            self._rel_w.append(self._mat(w[a + "relative_k_proj.weight"]))
+            c = q + "conv."
+            pw1 = w[c + "pointwise_conv1.weight"].reshape(2 * L.HIDDEN, L.HIDDEN)
+            # GLU pairs side by side: row 2c is a_c, row 2c+1 is its gate g_c.
+            lay.pw1 = _ptr(self._mat(np.stack([pw1[: L.HIDDEN], pw1[L.HIDDEN :]], 1).reshape(2 * L.HIDDEN, L.HIDDEN)))
+            lay.pw2 = _ptr(self._mat(w[c + "pointwise_conv2.weight"].reshape(L.HIDDEN, L.HIDDEN)))
+            lay.dw_w = _ptr(self._vec(w[c + "depthwise.weight"].reshape(L.HIDDEN, L.KERNEL)))
+            lay.dw_b = _ptr(self._vec(w[c + "depthwise.bias"]))
+        m.layer = C.cast(self._layer_arr, C.POINTER(L.Layer))
+        m.enc_proj_w = _ptr(self._mat(w["encoder_projector.weight"]))
+        m.enc_proj_b = _ptr(self._vec(w["encoder_projector.bias"]))
+
+        m.embedding = _ptr(self._mat(w["decoder.embedding.weight"]))
+        for l in range(2):
+            # Gates side by side per unit: row 4u+g is gate g (i, f, g, o) of unit u.
+            wl = w[f"decoder.lstm.weight_l{l}"].reshape(4, L.PRED, 2 * L.PRED).transpose(1, 0, 2).reshape(4 * L.PRED, -1)
+            bl = w[f"decoder.lstm.bias_l{l}"].reshape(4, L.PRED).T.reshape(-1)
+            m.lstm_w[l] = _ptr(self._mat(wl))
+            m.lstm_b[l] = _ptr(self._vec(bl))
+        m.dec_proj_w = _ptr(self._mat(w["decoder.decoder_projector.weight"]))
+        m.dec_proj_b = _ptr(self._vec(w["decoder.decoder_projector.bias"]))
+        joint = np.zeros((L.JOINT_ROWS, L.PRED), np.float32)
+        bias = np.full(L.JOINT_ROWS, -np.inf, np.float32)
+        joint[: L.TOKEN_ROWS] = w["joint.token_head.weight"]
+        bias[: L.TOKEN_ROWS] = w["joint.token_head.bias"]
+        joint[L.TOKEN_ROWS : L.TOKEN_ROWS + L.DURATIONS] = w["joint.duration_head.weight"]
+        bias[L.TOKEN_ROWS : L.TOKEN_ROWS + L.DURATIONS] = w["joint.duration_head.bias"]
+        m.joint_w = _ptr(self._mat(joint))
+        m.joint_b = _ptr(self._vec(bias))
+
+        mel_w, mel_start, mel_off = tables.sparse_mel()
+        m.window = _ptr(self._vec(tables.window()))
+        m.mel_w = _ptr(self._vec(mel_w))
+        m.mel_start = _ptr(self._vec(mel_start, torch.int32))
+        m.mel_off = _ptr(self._vec(mel_off, torch.int32))
+        self.model = m
+
+    def ensure_len(self, t3: int) -> None:
+        """Projected position tables (pos @ relative_k_proj^T, one per layer) covering
+        clips of up to `t3` encoder frames; computed once per length, off the per-clip
+        path, as tinybark/tinygrad/model.py:130-138 caches them per bucket."""
+        if t3 <= self.max_len:
+            return
+        n = max(-(-t3 // 128) * 128, 128)
+        pos = positions(n).to(self.device, self.tdtype).contiguous()
+        rows = 2 * n - 1
+        self._rel = []
+        for i in range(self.layers):
+            r = torch.empty(rows, L.HIDDEN, device=self.device, dtype=self.tdtype)
+            ep = L.Epilogue(kind=L.EPI_STORE, out_dtype=self.dtype, out=r.data_ptr(), ldo=L.HIDDEN)
+            self._gemm(pos, self._rel_w[i], ep)
+            self._rel.append(r)
+            self._layer_arr[i].rel = r.data_ptr()
+        self.max_len = n
+        self.model.max_len = n
+        self.check()
+
+    def _gemm(self, a: torch.Tensor, w: torch.Tensor, ep: L.Epilogue) -> None:
+        L.check(L.lib.tb_gemm(self.dtype, a.data_ptr(), a.stride(0), w.data_ptr(), a.shape[0], w.shape[0], a.shape[1],
+                              C.byref(ep), self.err.data_ptr(), _stream(self.device)), "tb_gemm")
+
+    def check(self) -> None:
+        """Synchronises and raises if a kernel reported a device-side timeout."""
+        torch.cuda.synchronize(self.device)
+        code = int(self.err.item())
+        if code:
+            self.err.zero_()
+            names = [v for k, v in L.DEVICE_ERRORS.items() if code & k]
+            raise RuntimeError("device error: " + ", ".join(names or [str(code)]))
+
+    # ------------------------------------------------------------------ batches
+
+    def plan(self, frames: list[int] | np.ndarray) -> Plan:
+        """Packed offsets and work lists for clips of the given feature-frame counts
+        (each at least 2), uploaded in one copy."""
+        parts = plan_arrays(frames, self.sub_rows, self.attn_rows)
+        self.ensure_len(int(parts["t3"].max()))
+        names = ("frame_off", "t1_off", "t2_off", "t3_off", "t2_clip", "t3_clip", "sub_tiles", "attn_tiles", "caps")
+        host = np.concatenate([parts[n] for n in names]).astype(np.int32)
+        meta = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
+        views, start = {}, 0
+        for n in names:
+            views[n] = meta[start : start + len(parts[n])]
+            start += len(parts[n])
+        b = L.Batch()
+        b.clips = len(parts["frames"])
+        b.frames_total, b.t1_total = int(parts["frame_off"][-1]), int(parts["t1_off"][-1])
+        b.t2_total, b.t3_total = int(parts["t2_off"][-1]), int(parts["t3_off"][-1])
+        for n in names[:6]:
+            setattr(b, n, views[n].data_ptr())
+        b.sub_tiles, b.n_sub_tiles = views["sub_tiles"].data_ptr(), len(parts["sub_tiles"]) // 2
+        b.attn_tiles, b.n_attn_tiles = views["attn_tiles"].data_ptr(), len(parts["attn_tiles"]) // 2
+        b.max_t3 = int(parts["t3"].max())
+        return Plan(parts["frames"], parts["t3"], b, meta, views["t3_off"], views["frame_off"], views["caps"],
+                    int(parts["caps"].max()))
+
+    # ------------------------------------------------------------------ stages
+
+    def features(self, samples: torch.Tensor, sample_off: torch.Tensor, plan: Plan) -> torch.Tensor:
+        """Packed float32 samples (device) to packed normalised log-mel features [frames, 128]."""
+        b = plan.batch
+        feats = torch.empty(b.frames_total, L.MELS, device=self.device, dtype=torch.float32)
+        nbytes = L.lib.tb_frontend_workspace_bytes(b.clips, b.frames_total)
+        ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
+        L.check(L.lib.tb_frontend(C.byref(self.model), samples.data_ptr(), sample_off.data_ptr(),
+                                  plan.frame_off.data_ptr(), b.clips, b.frames_total, int(plan.frames.max()),
+                                  feats.data_ptr(), ws.data_ptr(), nbytes, _stream(self.device)), "tb_frontend")
+        return feats
+
+    def encode(self, feats: torch.Tensor, plan: Plan) -> torch.Tensor:
+        """Packed features to packed encoder frames projected for the joint, [t3_total, 640] float32."""
+        b = plan.batch
+        enc = torch.empty(b.t3_total, L.PRED, device=self.device, dtype=torch.float32)
+        nbytes = L.lib.tb_encoder_workspace_bytes(self.dtype, b.t2_total, b.t3_total)
+        ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
+        L.check(L.lib.tb_encoder_forward(C.byref(self.model), C.byref(b), feats.data_ptr(), enc.data_ptr(),
+                                         ws.data_ptr(), nbytes, self.err.data_ptr(), _stream(self.device)),
+                "tb_encoder_forward")
+        return enc
+
+    def decode(self, enc: torch.Tensor, plan: Plan, early_exit: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+        """Greedy TDT decoding of every clip; returns device (tokens [clips, max_cap], counts [clips])."""
+        b = plan.batch
+        tokens = torch.empty(b.clips, plan.max_cap, device=self.device, dtype=torch.int32)
+        counts = torch.empty(b.clips, device=self.device, dtype=torch.int32)
+        nbytes = L.lib.tb_decode_workspace_bytes(self.dtype, b.clips)
+        ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
+        flag = self.host_flag.data_ptr() if early_exit else None
+        L.check(L.lib.tb_tdt_decode(C.byref(self.model), enc.data_ptr(), plan.t3_off.data_ptr(), plan.caps.data_ptr(),
+                                    b.clips, plan.max_cap, tokens.data_ptr(), counts.data_ptr(), ws.data_ptr(), nbytes,
+                                    flag, self.err.data_ptr(), _stream(self.device)), "tb_tdt_decode")
+        return tokens, counts
+
+    # ------------------------------------------------------------------ end to end
+
+    def upload(self, clips: list[np.ndarray]) -> tuple[torch.Tensor, torch.Tensor]:
+        """Packs float32 sample arrays into one pinned buffer and copies it to the device."""
+        sizes = np.array([len(c) for c in clips], np.int64)
+        off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+        host = torch.empty(int(off[-1]), dtype=torch.float32).pin_memory()
+        hv = host.numpy()
+        for c, s in zip(clips, off[:-1]):
+            hv[s : s + len(c)] = c
+        samples = host.to(self.device, non_blocking=True)
+        sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
+        return samples, sample_off
+
+    def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
+        """Token ids of every clip (16 kHz mono float32 samples), as the reference's
+        Bark.tokens returns them one clip at a time (tinybark/tinygrad/model.py:196-234)."""
+        clips = [np.asarray(c, np.float32).reshape(-1) for c in clips]
+        frames = [lengths.frames(len(c)) for c in clips]
+        keep = [i for i, f in enumerate(frames) if f >= 2]
+        out: list[list[int]] = [[] for _ in clips]
+        if not keep:
+            return out
+        with torch.cuda.device(self.device):
+            plan = self.plan([frames[i] for i in keep])
+            samples, sample_off = self.upload([clips[i] for i in keep])
+            feats = self.features(samples, sample_off, plan)
+            enc = self.encode(feats, plan)
+            tokens, counts = self.decode(enc, plan)
+            tok = tokens.cpu().numpy()
+            cnt = counts.cpu().numpy()
+            self.check()
+        for j, i in enumerate(keep):
+            out[i] = tok[j, : cnt[j]].tolist()
+        return out
