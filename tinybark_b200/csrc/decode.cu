@@ -174,6 +174,16 @@ __global__ void decode_publish_kernel(int* active, volatile int* host_flag) {
   active[1] = chunk + 1;
 }
 
+// A non-blocking stream per thread and device, used only to record graphs.
+static cudaStream_t capture_stream() {
+  static thread_local cudaStream_t streams[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
+    return nullptr;
+  return streams[dev];
+}
+
 template <typename T>
 static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                        int* tokens, int* counts, void* ws, int* host_flag, int* err, cudaStream_t stream) {
@@ -212,25 +222,25 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   jt.split = TB_TOKEN_ROWS;
   jt.split_end = TB_TOKEN_ROWS + TB_DURATIONS;
 
-  auto lstm_and_proj = [&]() -> int {
-    if (int rc = gemm(dt, w.x0, 2 * TB_PRED, m.lstm_w[0], lanes, 4 * TB_PRED, 2 * TB_PRED, l0, err, stream)) return rc;
-    if (int rc = gemm(dt, w.x1, 2 * TB_PRED, m.lstm_w[1], lanes, 4 * TB_PRED, 2 * TB_PRED, l1, err, stream)) return rc;
-    return gemm(dt, w.hp, TB_PRED, m.dec_proj_w, lanes, TB_PRED, TB_PRED, pj, err, stream);
+  auto lstm_and_proj = [&](cudaStream_t s) -> int {
+    if (int rc = gemm(dt, w.x0, 2 * TB_PRED, m.lstm_w[0], lanes, 4 * TB_PRED, 2 * TB_PRED, l0, err, s)) return rc;
+    if (int rc = gemm(dt, w.x1, 2 * TB_PRED, m.lstm_w[1], lanes, 4 * TB_PRED, 2 * TB_PRED, l1, err, s)) return rc;
+    return gemm(dt, w.hp, TB_PRED, m.dec_proj_w, lanes, TB_PRED, TB_PRED, pj, err, s);
   };
 
   if (cudaMemsetAsync(tokens, 0xff, (size_t)lanes * max_cap * sizeof(int), stream) != cudaSuccess) return fail_cuda();
   if (cudaMemsetAsync(w.active, 0, 2 * sizeof(int), stream) != cudaSuccess) return fail_cuda();
   decode_init_kernel<T><<<lane_blocks, 256, 0, stream>>>(w, emb, enc_off, cap, lanes);
   if (int rc = check_launch()) return rc;
-  if (int rc = lstm_and_proj()) return rc;
+  if (int rc = lstm_and_proj(stream)) return rc;
 
-  auto iteration = [&]() -> int {
-    decode_prep_kernel<T><<<lane_blocks, 256, 0, stream>>>(w, enc, enc_off, lanes);
+  auto iteration = [&](cudaStream_t s) -> int {
+    decode_prep_kernel<T><<<lane_blocks, 256, 0, s>>>(w, enc, enc_off, lanes);
     if (int rc = check_launch()) return rc;
-    if (int rc = gemm(dt, w.z, TB_PRED, m.joint_w, lanes, TB_JOINT_ROWS, TB_PRED, jt, err, stream)) return rc;
-    decode_step_kernel<T><<<lane_blocks, 256, 0, stream>>>(w, emb, enc_off, cap, lanes, max_cap, tokens);
+    if (int rc = gemm(dt, w.z, TB_PRED, m.joint_w, lanes, TB_JOINT_ROWS, TB_PRED, jt, err, s)) return rc;
+    decode_step_kernel<T><<<lane_blocks, 256, 0, s>>>(w, emb, enc_off, cap, lanes, max_cap, tokens);
     if (int rc = check_launch()) return rc;
-    return lstm_and_proj();
+    return lstm_and_proj(s);
   };
 
   // Early exit: the device publishes per chunk into pinned host memory.
@@ -241,18 +251,22 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   }
 
   // Every iteration launches the same kernels on the same buffers (the loop state is
-  // in device memory), so one chunk of iterations is captured once and replayed.
+  // in device memory), so one chunk of iterations is captured once and replayed on the
+  // caller's stream. Capture runs nothing, so it uses a stream of its own: the
+  // caller's may be the legacy default stream, which cannot be captured.
   constexpr int CHUNK = 32, AHEAD = 3;
+  const cudaStream_t cap_stream = capture_stream();
+  if (!cap_stream) return fail_cuda();
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
-  if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return fail_cuda();
+  if (cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return fail_cuda();
   int rc = TB_OK;
-  for (int i = 0; i < CHUNK && rc == TB_OK; ++i) rc = iteration();
+  for (int i = 0; i < CHUNK && rc == TB_OK; ++i) rc = iteration(cap_stream);
   if (rc == TB_OK && flag_dev) {
-    decode_publish_kernel<<<1, 1, 0, stream>>>(w.active, flag_dev);
+    decode_publish_kernel<<<1, 1, 0, cap_stream>>>(w.active, flag_dev);
     rc = check_launch();
   }
-  const cudaError_t captured = cudaStreamEndCapture(stream, &graph);
+  const cudaError_t captured = cudaStreamEndCapture(cap_stream, &graph);
   if (rc != TB_OK || captured != cudaSuccess) {
     if (graph) cudaGraphDestroy(graph);
     return rc != TB_OK ? rc : fail_cuda();
