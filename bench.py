@@ -48,6 +48,12 @@ def args_parser():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
+    p.add_argument("--only", default="", help="--micro: comma-separated kernels (layernorm,ffn,conv,mhsa)")
+    p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
+    p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
+    p.add_argument("--micro-dtypes", default="bf16,fp32")
+    p.add_argument("--profile", action="store_true", help="one step of the pipeline, for a profiler")
     return p
 
 
@@ -271,6 +277,7 @@ def run_ours(args):
     eng.check()
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
     barrier()
+    stages = stage_split(eng, samples, sample_off, plan)
     total_audio = audio_rank
     if world > 1:
         t = torch.tensor([audio_rank], device=dev, dtype=torch.float64)
@@ -353,6 +360,7 @@ def run_ours(args):
                        "encoder_frames_per_rank": int(M), "layers": args.layers, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (samples and weights, >126 MB per step)"},
             "encoder_ms_per_10s_clip": enc10_ms,
+            "stages_ms_rank0": stages,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
                          "frac": achieved / tflops, "traffic": traffic,
                          "kernel": f"gemm_tc_kernel<256> FFN up M={M} N=4096 K=1024, timed alone",
@@ -369,9 +377,150 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def timed(fn, iters: int = 10, flush=None) -> float:
+    """Median seconds of fn() over `iters` launches, each timed alone with CUDA events on
+    the current stream, L2 flushed before each (a write larger than L2)."""
+    import torch
+
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) / 1000)
+    return statistics.median(times)
+
+
+def run_micro(args):
+    """Per-kernel microbenchmarks at encoder shapes, inputs N(0, 1) from a seed: LayerNorm
+    over [B*T, 1024]; the SiLU FFN 1024->4096->1024; the conv module (pointwise 1024->2048
+    + GLU, depthwise k=9 + SiLU, pointwise 1024->1024); rel-pos MHSA with q/k/v
+    [B, 8, T, 128] and positions [2T-1, 1024]. One JSON line per case."""
+    import torch
+
+    from tinybark_b200 import _lib as L
+    from tinybark_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    hbm, tflops, kind = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    only = set(filter(None, args.only.split(",")))
+    want = lambda k: not only or k in only
+    g = torch.Generator(device=dev).manual_seed(0)
+    rnd = lambda *s, dt=torch.float32: torch.randn(*s, device=dev, generator=g).to(dt)
+
+    def emit(**kw):
+        print(json.dumps(kw), flush=True)
+
+    for dt_name in args.micro_dtypes.split(","):
+        dt = torch.bfloat16 if dt_name == "bf16" else torch.float32
+        esz = 2 if dt == torch.bfloat16 else 4
+        code = L.BF16 if dt == torch.bfloat16 else L.F32
+        for bt in map(int, filter(None, args.rows.split(","))):
+            if want("layernorm"):
+                x, w, b = rnd(bt, 1024), rnd(1024), rnd(1024)
+                y = torch.empty(bt, 1024, device=dev, dtype=dt)
+                s = timed(lambda: K.layernorm(x, w, b, y), flush=flush)
+                nbytes = bt * 1024 * (4 + esz)
+                emit(kernel="layernorm", dtype=dt_name, rows=bt, us=s * 1e6, gbs=nbytes / s / 1e9,
+                     frac=nbytes / s / 1e9 / hbm, bound="hbm")
+            if want("ffn"):
+                x = rnd(bt, 1024, dt=dt)
+                w1, w2 = rnd(4096, 1024, dt=dt) / 32, rnd(1024, 4096, dt=dt) / 64
+                h = torch.empty(bt, 4096, device=dev, dtype=dt)
+                res = rnd(bt, 1024)
+                e1 = L.Epilogue(kind=L.EPI_SILU, out_dtype=code, out=h.data_ptr(), ldo=4096)
+                e2 = L.Epilogue(kind=L.EPI_RESIDUAL, out=res.data_ptr(), ldo=1024, alpha=0.5)
+                s1 = timed(lambda: K.gemm(x, w1, e1), flush=flush)
+                s2 = timed(lambda: K.gemm(h, w2, e2), flush=flush)
+                fl = 2 * bt * 1024 * 4096
+                for name, s in (("ffn_up_silu", s1), ("ffn_down_residual", s2)):
+                    emit(kernel=name, dtype=dt_name, rows=bt, us=s * 1e6, tflops=fl / s / 1e12,
+                         frac=fl / s / 1e12 / tflops, bound="tensor" if code == L.BF16 else "fma")
+            if want("conv"):
+                x = rnd(bt, 1024, dt=dt)
+                pw1, pw2 = rnd(2048, 1024, dt=dt) / 32, rnd(1024, 1024, dt=dt) / 32
+                glu = torch.empty(bt, 1024, device=dev, dtype=dt)
+                dwo = torch.empty(bt, 1024, device=dev, dtype=dt)
+                res = rnd(bt, 1024)
+                frames = K.Frames([bt], code, dev)
+                dww, dwb = rnd(1024, 9), rnd(1024)
+                e1 = L.Epilogue(kind=L.EPI_GLU, out_dtype=code, out=glu.data_ptr(), ldo=1024)
+                e2 = L.Epilogue(kind=L.EPI_RESIDUAL, out=res.data_ptr(), ldo=1024, alpha=1.0)
+                s1 = timed(lambda: K.gemm(x, pw1, e1), flush=flush)
+                s2 = timed(lambda: K.depthwise(glu, dww, dwb, frames, dwo), flush=flush)
+                s3 = timed(lambda: K.gemm(dwo, pw2, e2), flush=flush)
+                emit(kernel="conv_pw1_glu", dtype=dt_name, rows=bt, us=s1 * 1e6,
+                     tflops=2 * bt * 1024 * 2048 / s1 / 1e12)
+                nbytes = 2 * bt * 1024 * esz
+                emit(kernel="conv_depthwise_silu", dtype=dt_name, rows=bt, us=s2 * 1e6, gbs=nbytes / s2 / 1e9,
+                     frac=nbytes / s2 / 1e9 / hbm, bound="hbm")
+                emit(kernel="conv_pw2_residual", dtype=dt_name, rows=bt, us=s3 * 1e6,
+                     tflops=2 * bt * 1024 * 1024 / s3 / 1e12)
+            if want("mhsa"):
+                for t in map(int, filter(None, args.lengths.split(","))):
+                    if t > bt and bt != min(map(int, args.rows.split(","))):
+                        continue
+                    clips = max(1, bt // t)
+                    rows = clips * t
+                    qu, qv, k, v = (rnd(rows, 1024, dt=dt) for _ in range(4))
+                    rel = rnd(2 * t - 1, 1024, dt=dt)
+                    out = torch.empty(rows, 1024, device=dev, dtype=dt)
+                    frames = K.Frames([t] * clips, code, dev)
+                    s = timed(lambda: K.attention(qu, qv, k, v, rel, t, frames, out), flush=flush)
+                    fl = 6.0 * t * t * 1024 * clips
+                    emit(kernel="relpos_attention", dtype=dt_name, rows=rows, T=t, clips=clips, us=s * 1e6,
+                         tflops=fl / s / 1e12, frac=fl / s / 1e12 / tflops)
+    K.check(dev)
+
+
+def stage_split(eng, samples, sample_off, plan):
+    """Milliseconds of front-end, encoder and decode in one untimed extra step."""
+    import torch
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record()
+    feats = eng.features(samples, sample_off, plan)
+    ev[1].record()
+    enc = eng.encode(feats, plan)
+    ev[2].record()
+    eng.decode(enc, plan)
+    ev[3].record()
+    torch.cuda.synchronize()
+    return {k: ev[i].elapsed_time(ev[i + 1]) for i, k in enumerate(("frontend", "encoder", "decode"))}
+
+
+def run_profile(args):
+    """One pipeline step on this rank's shard after one warm-up step: for ncu."""
+    import torch
+
+    import tinybark_b200
+
+    torch.cuda.set_device(0)
+    clips, durs = shard(0, args.clips_per_rank)
+    tensors, cfg = weights(args.layers)
+    bark = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg))
+    eng = bark.engine
+    plan = eng.plan([len(c) // 160 for c in clips])
+    samples, sample_off = eng.upload(clips)
+    for _ in range(args.steps):
+        split = stage_split(eng, samples, sample_off, plan)
+    eng.check()
+    print(json.dumps({"profile_step_ms": split, "clips": len(clips), "audio_s": float(np.sum(durs))}), flush=True)
+
+
 def main():
     args = args_parser().parse_args()
-    if args.impl == "reference":
+    if args.micro:
+        run_micro(args)
+    elif args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

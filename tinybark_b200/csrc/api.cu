@@ -27,6 +27,9 @@ int fail_cuda() {
 
 static std::atomic<long long> g_launches{0};
 
+void count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(); }
+
 int check_launch() {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();

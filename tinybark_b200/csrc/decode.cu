@@ -259,6 +259,7 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   if (!cap_stream) return fail_cuda();
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  const long long launches_before = launch_count();
   if (cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return fail_cuda();
   int rc = TB_OK;
   for (int i = 0; i < CHUNK && rc == TB_OK; ++i) rc = iteration(cap_stream);
@@ -267,6 +268,7 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
     rc = check_launch();
   }
   const cudaError_t captured = cudaStreamEndCapture(cap_stream, &graph);
+  count_launches(launches_before - launch_count());  // recorded, not run
   if (rc != TB_OK || captured != cudaSuccess) {
     if (graph) cudaGraphDestroy(graph);
     return rc != TB_OK ? rc : fail_cuda();
@@ -275,6 +277,8 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
     cudaGraphDestroy(graph);
     return fail_cuda();
   }
+  size_t nodes = 0;
+  cudaGraphGetNodes(graph, nullptr, &nodes);
   const int chunks = (max_cap + CHUNK - 1) / CHUNK;
   if (flag_dev) host_flag[0] = 1, host_flag[1] = -1;
   for (int c = 0; c < chunks && rc == TB_OK; ++c) {
@@ -300,6 +304,7 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
       if (stop || rc != TB_OK) break;
     }
     if (cudaGraphLaunch(exec, stream) != cudaSuccess) rc = fail_cuda();
+    count_launches((long long)nodes);
   }
   cudaGraphExecDestroy(exec);
   cudaGraphDestroy(graph);

@@ -14,7 +14,9 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 EncodeTiledFn tensor_map_encoder();
 int sm_count();
 int fail_cuda();     // records cudaGetLastError() and returns TB_ERR_CUDA
-int check_launch();  // TB_OK, or fail_cuda() if the last launch failed
+int check_launch();  // TB_OK, or fail_cuda() if the last launch failed; counts the launch
+void count_launches(long long n);  // adds kernels run by a graph replay (or removes captured ones)
+long long launch_count();
 
 int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
          cudaStream_t stream);
