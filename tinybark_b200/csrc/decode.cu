@@ -153,13 +153,26 @@ __global__ void decode_step_kernel(DecodeWs w, const T* __restrict__ emb, const 
   tok = __shfl_sync(0xffffffffu, tok, 0);
   if (!step) return;
   const long long L = lanes;
-  T* x0 = reinterpret_cast<T*>(w.x0) + (long long)l * 2 * TB_PRED;
-  T* x1 = reinterpret_cast<T*>(w.x1) + (long long)l * 2 * TB_PRED;
-  const T* er = emb + (long long)tok * TB_PRED;
-  for (int j = lane; j < TB_PRED; j += 32) {
-    x0[j] = er[j];
-    x0[TB_PRED + j] = from_f<T>(w.h[l * TB_PRED + j]);
-    x1[TB_PRED + j] = from_f<T>(w.h[(L + l) * TB_PRED + j]);
+  T* __restrict__ x0 = reinterpret_cast<T*>(w.x0) + (long long)l * 2 * TB_PRED;
+  T* __restrict__ x1 = reinterpret_cast<T*>(w.x1) + (long long)l * 2 * TB_PRED;
+  const T* __restrict__ er = emb + (long long)tok * TB_PRED;
+  const float* __restrict__ h0 = w.h + (long long)l * TB_PRED;
+  const float* __restrict__ h1 = w.h + (L + l) * TB_PRED;
+  // 640 = 5 x 32 lanes x 4 values; all loads first, then the stores.
+  float4 e4[5], a4[5], b4[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int j = (i * 32 + lane) * 4;
+    e4[i] = load4(er + j);
+    a4[i] = load4(h0 + j);
+    b4[i] = load4(h1 + j);
+  }
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int j = (i * 32 + lane) * 4;
+    store4(x0 + j, e4[i].x, e4[i].y, e4[i].z, e4[i].w);
+    store4(x0 + TB_PRED + j, a4[i].x, a4[i].y, a4[i].z, a4[i].w);
+    store4(x1 + TB_PRED + j, b4[i].x, b4[i].y, b4[i].z, b4[i].w);
   }
 }
 

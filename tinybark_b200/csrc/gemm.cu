@@ -6,7 +6,11 @@
 // into a STAGES-deep shared-memory ring, warp 1 issues tcgen05.mma (128 x BN x 16 per
 // instruction) into one of two tensor-memory accumulators, warps 2-5 drain the other
 // accumulator through the epilogue, so a tile's epilogue overlaps the next tile's
-// main loop.
+// main loop. The epilogue is a template parameter; each warp moves its 32 rows x 32
+// columns from tensor memory through a shared-memory transpose, so global loads and
+// stores are whole row segments (8 lanes per row) instead of one row per lane.
+// BN is 256, 128 or 64: small-M GEMMs (the decoder's) take narrow tiles to spread
+// over more SMs.
 // fp32: a CUDA-core kernel, 128 x 128 tiles, 8 x 8 outputs per thread, for the fp32
 // parity path.
 #include "epilogue.cuh"
@@ -20,13 +24,15 @@ namespace tb {
 template <int BN>
 struct TcCfg {
   static constexpr int BM = 128, BK = 64;
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int OUT_STRIDE = 36;  // floats per staged row: 16-byte aligned, conflict-free
+  static constexpr int OUT_BYTES = 4 * 32 * OUT_STRIDE * 4;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES;
 };
 
 struct TcBars {
@@ -49,14 +55,110 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-template <int BN>
+__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+__device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// The epilogue of one warp's 32 x 32 chunk, staged row-major (stride OUT_STRIDE) in
+// `stage`: lane reads rows 4*it + lane/8 (it = 0..7), columns 4*(lane%8) .. +3.
+// row0: global row of the chunk's first row; n0: global column of its first column.
+template <int EPI>
+__device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* stage, int row0, int n0, int lane, int M) {
+  constexpr int S = 36;
+  const int sub = lane >> 3, col = (lane & 7) * 4, n = n0 + col;
+  float4 v[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) v[it] = *reinterpret_cast<const float4*>(stage + (it * 4 + sub) * S + col);
+  if constexpr (EPI == TB_EPI_RESIDUAL) {
+    float* out = reinterpret_cast<float*>(e.out);
+    float4 x[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      x[it] = m < M ? load4(out + (long long)m * e.ldo + n) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M)
+        store4(out + (long long)m * e.ldo + n, x[it].x + e.alpha * v[it].x, x[it].y + e.alpha * v[it].y,
+               x[it].z + e.alpha * v[it].z, x[it].w + e.alpha * v[it].w);
+    }
+  } else if constexpr (EPI == TB_EPI_STORE || EPI == TB_EPI_BIAS_RELU) {
+    const float4 b = e.bias ? load4(e.bias + n) : make_float4(0, 0, 0, 0);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m >= M) continue;
+      float a0 = v[it].x + b.x, a1 = v[it].y + b.y, a2 = v[it].z + b.z, a3 = v[it].w + b.w;
+      if constexpr (EPI == TB_EPI_BIAS_RELU) a0 = fmaxf(a0, 0.f), a1 = fmaxf(a1, 0.f), a2 = fmaxf(a2, 0.f), a3 = fmaxf(a3, 0.f);
+      store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, a0, a1, a2, a3);
+    }
+  } else if constexpr (EPI == TB_EPI_SILU) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M)
+        store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, fast_silu(v[it].x), fast_silu(v[it].y),
+                  fast_silu(v[it].z), fast_silu(v[it].w));
+    }
+  } else if constexpr (EPI == TB_EPI_GLU) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M)
+        store2_dt(e.out, (long long)m * e.ldo + (n >> 1), e.out_dtype, v[it].x * fast_sigmoid(v[it].y),
+                  v[it].z * fast_sigmoid(v[it].w));
+    }
+  } else if constexpr (EPI == TB_EPI_QKV) {
+    const int sec = n >> 10, c = n & 1023;
+    void* dst = sec == 0 ? e.out : (sec == 1 ? e.out3 : e.out4);
+    const float4 u = sec == 0 ? load4(e.bias_u + c) : make_float4(0, 0, 0, 0);
+    const float4 w = sec == 0 ? load4(e.bias_v + c) : make_float4(0, 0, 0, 0);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m >= M) continue;
+      const long long off = (long long)m * e.ldo + c;
+      store4_dt(dst, off, e.out_dtype, v[it].x + u.x, v[it].y + u.y, v[it].z + u.z, v[it].w + u.w);
+      if (sec == 0) store4_dt(e.out2, off, e.out_dtype, v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
+    }
+  } else if constexpr (EPI == TB_EPI_LSTM) {
+    // Columns n..n+3 are the gates i, f, g, o of unit n / 4.
+    const int u = n >> 2;
+    const float4 b = load4(e.bias + n);
+    float cp[8];
+    int step[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      step[it] = m < M && (!e.mask || e.mask[m] != 0);
+      cp[it] = step[it] ? e.c[(long long)m * TB_PRED + u] : 0.f;
+    }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      if (!step[it]) continue;
+      const int m = row0 + it * 4 + sub;
+      const float ig = fast_sigmoid(v[it].x + b.x), fg = fast_sigmoid(v[it].y + b.y);
+      const float gg = tanhf(v[it].z + b.z), og = fast_sigmoid(v[it].w + b.w);
+      const float c = fg * cp[it] + ig * gg;
+      const float h = og * tanhf(c);
+      e.c[(long long)m * TB_PRED + u] = c;
+      e.h[(long long)m * TB_PRED + u] = h;
+      if (e.out) store1_dt(e.out, (long long)m * e.ldo + u, e.out_dtype, h);
+      if (e.out2) store1_dt(e.out2, (long long)m * e.ldo2 + u, e.out_dtype, h);
+    }
+  }
+}
+
+template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
                    const tb_epilogue e, int* err) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  TcBars* bars = reinterpret_cast<TcBars*>(smem + C::STAGES * C::STAGE_BYTES);
+  float* out_stage = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+  TcBars* bars = reinterpret_cast<TcBars*>(smem + C::STAGES * C::STAGE_BYTES + C::OUT_BYTES);
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -146,35 +248,45 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int q = warp & 3;  // tensor-memory lane quarter this warp may access
-    const int row = q * 32 + lane;
+    float* stage = out_stage + q * 32 * C::OUT_STRIDE;
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       const int mt = t / n_tiles, nt = t % n_tiles;
       if (!warp_wait(&bars->tfull[acc], acc_ph, err, abort)) break;
       tc_fence_after();
-      const int m = mt * C::BM + row;
+      const int row0 = mt * C::BM + q * 32;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-      ArgmaxAcc am;
+      if constexpr (EPI == TB_EPI_ARGMAX) {
+        const int m = row0 + lane;
+        ArgmaxAcc am;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
-        tmem_wait_ld();
-        if (m < M) {
-          const int n0 = nt * BN + c;
-          if (e.kind == TB_EPI_ARGMAX) {
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          tmem_wait_ld();
+          if (m < M) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) am.add(e, n0 + j, __uint_as_float(r[j]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              epi_group(e, m, n0 + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                        __uint_as_float(r[j + 3]));
+            for (int j = 0; j < 32; ++j) am.add(e, nt * BN + c + j, __uint_as_float(r[j]));
           }
         }
+        if (m < M) am.flush(e, m);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          tmem_wait_ld();
+          float4* srow = reinterpret_cast<float4*>(stage + lane * C::OUT_STRIDE);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            srow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          __syncwarp();
+          epi_chunk<EPI>(e, stage, row0, nt * BN + c, lane, M);
+          __syncwarp();
+        }
       }
-      if (e.kind == TB_EPI_ARGMAX && m < M) am.flush(e, m);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[acc]);
@@ -303,35 +415,67 @@ static bool encode_tmap(CUtensorMap* map, const void* ptr, long long rows, long 
   return r == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int EPI>
 static int launch_tc(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
                      cudaStream_t stream) {
   using C = TcCfg<BN>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
       return fail_cuda();
     configured = true;
   }
   CUtensorMap ta, tw;
   if (!encode_tmap(&ta, a, m, k, lda, C::BM) || !encode_tmap(&tw, w, n, k, k, BN)) return TB_ERR_CUDA;
-  int tiles = ((m + C::BM - 1) / C::BM) * (n / BN);
-  int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tc_kernel<BN><<<grid, 192, C::SMEM, stream>>>(ta, tw, m, n, k, e, err);
+  const int tiles = ((m + C::BM - 1) / C::BM) * (n / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  gemm_tc_kernel<BN, EPI><<<grid, 192, C::SMEM, stream>>>(ta, tw, m, n, k, e, err);
   return check_launch();
+}
+
+template <int BN>
+static int launch_tc_kind(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e,
+                          int* err, cudaStream_t s) {
+  switch (e.kind) {
+    case TB_EPI_STORE: return launch_tc<BN, TB_EPI_STORE>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_SILU: return launch_tc<BN, TB_EPI_SILU>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_RESIDUAL: return launch_tc<BN, TB_EPI_RESIDUAL>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_BIAS_RELU: return launch_tc<BN, TB_EPI_BIAS_RELU>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_GLU: return launch_tc<BN, TB_EPI_GLU>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_QKV: return launch_tc<BN, TB_EPI_QKV>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_ARGMAX: return launch_tc<BN, TB_EPI_ARGMAX>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_LSTM: return launch_tc<BN, TB_EPI_LSTM>(a, lda, w, m, n, k, e, err, s);
+    default: return TB_ERR_ARG;
+  }
+}
+
+// The widest tile (fewest operand re-reads) that still gives every SM a tile; when none
+// does, the narrowest, for the most parallelism.
+static int pick_bn(int m, int n) {
+  const int m_tiles = (m + 127) / 128, sms = sm_count();
+  for (int bn : {256, 128, 64})
+    if (n % bn == 0 && m_tiles * (n / bn) >= sms) return bn;
+  for (int bn : {64, 128, 256})
+    if (n % bn == 0) return bn;
+  return 0;
 }
 
 int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
          cudaStream_t stream) {
   if (m <= 0) return TB_OK;
   if (n <= 0 || k <= 0 || !a || !w) return TB_ERR_ARG;
+  if (e.kind < TB_EPI_STORE || e.kind > TB_EPI_LSTM) return TB_ERR_ARG;
   if (e.kind == TB_EPI_ARGMAX && (!e.keys || !e.keys2 || !e.bias)) return TB_ERR_ARG;
   if (dtype == TB_BF16) {
     if (k % 64 || lda % 8 || (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
       return TB_ERR_UNSUPPORTED;
-    if (n % 256 == 0) return launch_tc<256>(a, lda, w, m, n, k, e, err, stream);
-    if (n % 128 == 0) return launch_tc<128>(a, lda, w, m, n, k, e, err, stream);
-    return TB_ERR_UNSUPPORTED;
+    switch (pick_bn(m, n)) {
+      case 256: return launch_tc_kind<256>(a, lda, w, m, n, k, e, err, stream);
+      case 128: return launch_tc_kind<128>(a, lda, w, m, n, k, e, err, stream);
+      case 64: return launch_tc_kind<64>(a, lda, w, m, n, k, e, err, stream);
+      default: return TB_ERR_UNSUPPORTED;
+    }
   }
   if (dtype != TB_F32) return TB_ERR_ARG;
   if (k % SG_BK || n % SG_BN || lda % 4) return TB_ERR_UNSUPPORTED;
