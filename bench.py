@@ -470,9 +470,10 @@ def run_micro(args):
                     rows = clips * t
                     qu, qv, k, v = (rnd(rows, 1024, dt=dt) for _ in range(4))
                     rel = rnd(2 * t - 1, 1024, dt=dt)
+                    rel_c = K.rel_bias(rel, rnd(1024), rnd(1024)) if code == L.BF16 else None
                     out = torch.empty(rows, 1024, device=dev, dtype=dt)
                     frames = K.Frames([t] * clips, code, dev)
-                    s = timed(lambda: K.attention(qu, qv, k, v, rel, t, frames, out), flush=flush)
+                    s = timed(lambda: K.attention(qu, qv, k, v, rel, t, frames, out, rel_c), flush=flush)
                     fl = 6.0 * t * t * 1024 * clips
                     emit(kernel="relpos_attention", dtype=dt_name, rows=rows, T=t, clips=clips, us=s * 1e6,
                          tflops=fl / s / 1e12, frac=fl / s / 1e12 / tflops)

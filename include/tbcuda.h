@@ -110,6 +110,7 @@ typedef struct tb_layer {
   const float* dw_w;  /* [1024, 9] depthwise taps with BatchNorm folded in */
   const float* dw_b;  /* [1024] */
   const void* rel;    /* [2*max_len-1, 1024]: positions(max_len) @ relative_k_proj^T */
+  const float* rel_c; /* [2*max_len-1, 128]: column h < 8 = (bias_v - bias_u)_h . rel (bf16 attention) */
 } tb_layer;
 
 typedef struct tb_model {
@@ -200,9 +201,12 @@ int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n
 /* ---- relative-position MHSA core: tinybark/tinygrad/model.py:99-116 (_attention),
  * tinybark/mojo/bark/gpu.mojo:202-224 (softmax_kernel) ----
  * qu = q + bias_u, qv = q + bias_v, k, v: [t3_total, 1024] (dtype) packed by clip;
- * rel: [2*max_len-1, 1024]; out: [t3_total, 1024] (dtype), heads side by side. */
+ * rel: [2*max_len-1, 1024]; out: [t3_total, 1024] (dtype), heads side by side.
+ * fp32 reads qv; bf16 (tensor cores) reads rel_c instead: [2*max_len-1, 128] fp32,
+ * column h < 8 = (bias_v - bias_u)_h . rel[row, head h] (qv may then be NULL).
+ * tb_batch.attn_tiles must use tb_tile_rows(dtype) query rows per item. */
 int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
-                        int max_len, const tb_batch* batch, void* out, int* err, void* stream);
+                        const float* rel_c, int max_len, const tb_batch* batch, void* out, int* err, void* stream);
 
 /* ---- conv module middle: tinybark/tinygrad/model.py:121-124 (_conv: GLU output,
  * depthwise k=9 with folded BatchNorm, SiLU) ----

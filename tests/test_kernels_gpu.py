@@ -189,27 +189,35 @@ def batch_for(L, t3_list, attn_rows):
 
 
 @pytest.mark.parametrize("dtype", [0, 1])
-def test_relpos_attention(L, dtype, err):
-    t3 = [1, 2, 7, 33, 130, 64]
-    max_len = 256
+@pytest.mark.parametrize("t3,max_len", [([1, 2, 7, 33, 130, 64], 256), ([300, 65, 128, 129], 384), ([250], 250)])
+def test_relpos_attention(L, dtype, t3, max_len, err):
+    from tinybark_b200 import kernels
+
     _, attn_rows = L.tile_rows(dtype)
     b, keep, off = batch_for(L, t3, attn_rows)
     R = off[-1]
     g = torch.Generator(device="cuda").manual_seed(7)
-    qu, qv, k, v = (torch.randn(R, 1024, device="cuda", generator=g).to(tdt(dtype)) for _ in range(4))
+    q, k, v = (torch.randn(R, 1024, device="cuda", generator=g) for _ in range(3))
+    bu, bv = torch.randn(1024, device="cuda", generator=g), torch.randn(1024, device="cuda", generator=g)
+    qu, qv, k, v = (x.to(tdt(dtype)) for x in (q + bu, q + bv, k, v))
     rel = torch.randn(2 * max_len - 1, 1024, device="cuda", generator=g).to(tdt(dtype))
+    rel_c = kernels.rel_bias(rel, bu, bv) if dtype == 1 else None
     out = torch.empty(R, 1024, device="cuda", dtype=tdt(dtype))
     L.check(L.lib.tb_relpos_attention(dtype, qu.data_ptr(), qv.data_ptr(), k.data_ptr(), v.data_ptr(), rel.data_ptr(),
-                                      max_len, ctypes.byref(b), out.data_ptr(), err.data_ptr(), stream()),
-            "tb_relpos_attention")
+                                      None if rel_c is None else rel_c.data_ptr(), max_len, ctypes.byref(b),
+                                      out.data_ptr(), err.data_ptr(), stream()), "tb_relpos_attention")
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    # bf16 computes (q+u).r + (v-u).r with both operands rounded to bf16: the reference
+    # uses the same rounded operands.
+    qpos = qv.double() if dtype == 0 else qu.double() + (bv - bu).to(tdt(dtype)).double()
     for c, T in enumerate(t3):
         s = slice(off[c], off[c + 1])
         hq = lambda x: x[s].double().view(T, 8, 128).transpose(0, 1)
         i = torch.arange(T, device="cuda")[:, None]
         j = torch.arange(T, device="cuda")[None, :]
         r = rel.double()[max_len - 1 - i + j].view(T, T, 8, 128).permute(2, 0, 1, 3)  # (H, i, j, d)
-        scores = hq(qu) @ hq(k).transpose(1, 2) + (hq(qv)[:, :, None, :] * r).sum(-1)
+        scores = hq(qu) @ hq(k).transpose(1, 2) + (hq(qpos)[:, :, None, :] * r).sum(-1)
         p = torch.softmax(scores / 128**0.5, -1)
         ref = (p @ hq(v)).transpose(0, 1).reshape(T, 1024)
         assert max_rel(out[s].float().cpu(), ref.cpu()) < TOL[dtype], (c, T)

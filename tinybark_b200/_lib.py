@@ -32,7 +32,7 @@ class Layer(C.Structure):
     _fields_ = [
         ("norm_w", vp * 5), ("norm_b", vp * 5), ("ff1_w1", vp), ("ff1_w2", vp), ("ff2_w1", vp), ("ff2_w2", vp),
         ("qkv", vp), ("o_proj", vp), ("pw1", vp), ("pw2", vp), ("bias_u", vp), ("bias_v", vp),
-        ("dw_w", vp), ("dw_b", vp), ("rel", vp),
+        ("dw_w", vp), ("dw_b", vp), ("rel", vp), ("rel_c", vp),
     ]
 
 
@@ -75,7 +75,7 @@ def _load() -> C.CDLL:
         "tb_frontend": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, sz, vp]),
         "tb_layernorm": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
         "tb_gemm": (i32, [i32, vp, ll, vp, i32, i32, i32, P(Epilogue), vp, vp]),
-        "tb_relpos_attention": (i32, [i32, vp, vp, vp, vp, vp, i32, P(Batch), vp, vp, vp]),
+        "tb_relpos_attention": (i32, [i32, vp, vp, vp, vp, vp, vp, i32, P(Batch), vp, vp, vp]),
         "tb_conv_depthwise": (i32, [i32, vp, vp, vp, P(Batch), vp, vp]),
         "tb_subsample_workspace_bytes": (sz, [i32, i32, i32]),
         "tb_subsample": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),

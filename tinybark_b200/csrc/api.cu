@@ -136,7 +136,7 @@ static int encoder_forward(const tb_model& m, const tb_batch& b, const float* fe
   qkv.kind = TB_EPI_QKV;
   qkv.out_dtype = dt;
   qkv.out = w.qu;
-  qkv.out2 = w.qv;
+  qkv.out2 = dt == TB_F32 ? w.qv : nullptr;  // the bf16 attention takes the bias_v term from rel_c
   qkv.out3 = w.k;
   qkv.out4 = w.v;
   qkv.ldo = TB_HIDDEN;
@@ -153,7 +153,7 @@ static int encoder_forward(const tb_model& m, const tb_batch& b, const float* fe
     qkv.bias_u = L.bias_u;
     qkv.bias_v = L.bias_v;
     if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.qkv, R, 3 * TB_HIDDEN, TB_HIDDEN, qkv, err, s)) return rc;
-    if (int rc = relpos_attention(dt, w.qu, w.qv, w.k, w.v, L.rel, m.max_len, b, w.att, err, s)) return rc;
+    if (int rc = relpos_attention(dt, w.qu, w.qv, w.k, w.v, L.rel, L.rel_c, m.max_len, b, w.att, err, s)) return rc;
     if (int rc = gemm(dt, w.att, TB_HIDDEN, L.o_proj, R, TB_HIDDEN, TB_HIDDEN, full, err, s)) return rc;
     // x += Conv(LN(x))
     if (int rc = layernorm(w.x, L.norm_w[2], L.norm_b[2], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
@@ -235,9 +235,9 @@ int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n
 }
 
 int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
-                        int max_len, const tb_batch* batch, void* out, int* err, void* stream) {
+                        const float* rel_c, int max_len, const tb_batch* batch, void* out, int* err, void* stream) {
   if (!batch) return TB_ERR_ARG;
-  return relpos_attention(dtype, qu, qv, k, v, rel, max_len, *batch, out, err, as_stream(stream));
+  return relpos_attention(dtype, qu, qv, k, v, rel, rel_c, max_len, *batch, out, err, as_stream(stream));
 }
 
 int tb_conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch* batch, void* out,

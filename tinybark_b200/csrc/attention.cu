@@ -143,6 +143,317 @@ __global__ void __launch_bounds__(256) relpos_attention_simt(const T* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 form (bf16): one CTA per (clip, head, 128 queries), key tiles of 64.
+//
+// Warp 0 loads tiles with TMA, warp 1 issues the MMAs, warps 2-5 (one query row per
+// thread) run the softmax. Per key tile, into tensor memory:
+//   S  = Qu K^T          (128 x 64)
+//   BD = Qu R_band^T     (128 x 192), R_band the 192 table rows the tile's relative
+//                        positions span (191 used)
+// The positional term of the reference, (q + bias_v) . r, is computed as
+// (q + bias_u) . r + (bias_v - bias_u) . r: the second product depends only on the
+// head and the relative position and comes precomputed per layer (rel_c), so Qu is the
+// only query operand. Each softmax warp copies the 96 BD columns its 32 rows need into
+// shared memory and reads its row's window shifted by its row index (the relative
+// shift). P (bf16) is written back into the tensor memory of S and the PV MMA reads
+// it from there; V is an MN-major operand straight from the [frames, 1024] V tensor.
+// O accumulates in tensor memory, rescaled by the softmax threads when the row max
+// grows.
+
+namespace att {
+constexpr int TQ = 128, TK = 64, D = 128, BAND = 192;
+constexpr int Q_BYTES = TQ * D * 2, K_BYTES = TK * D * 2, R_BYTES = BAND * D * 2, V_BYTES = TK * D * 2;
+constexpr int Q_SUB = TQ * 128, K_SUB = TK * 128, R_SUB = BAND * 128, V_SUB = TK * 128;  // 64-column halves
+constexpr int ST_STRIDE = 100, WIN = 96;
+constexpr int ST_BYTES = 4 * 32 * ST_STRIDE * 4, C_BYTES = 4 * WIN * 4;
+constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_R = OFF_K + K_BYTES, OFF_V = OFF_R + R_BYTES,
+              OFF_ST = OFF_V + V_BYTES, OFF_C = OFF_ST + ST_BYTES, OFF_BAR = OFF_C + C_BYTES;
+constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, TMEM_COLS = 512;
+// log2(e) / sqrt(128): scores are kept in the base-2 exponent domain.
+constexpr float SCALE_LOG2 = 0.12751743074f;
+
+struct Bars {
+  uint64_t q_full, kr_full, kr_empty, v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, done;
+  uint32_t tmem;
+  int abort;
+};
+}  // namespace att
+
+__device__ __forceinline__ void att_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - start > TB_WAIT_NS) break;
+}
+
+__device__ __forceinline__ bool att_warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, TB_DEV_ATTN_TIMEOUT, abort);
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__global__ void __launch_bounds__(192, 1)
+    relpos_attention_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tr,
+                        const float* __restrict__ rel_c, int max_len, const int* __restrict__ t3_off,
+                        const int* __restrict__ tiles, __nv_bfloat16* __restrict__ out, int* err) {
+  using namespace att;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int clip = tiles[2 * blockIdx.x], q0 = tiles[2 * blockIdx.x + 1], head = blockIdx.y;
+  const int base = t3_off[clip], T_ = t3_off[clip + 1] - base;
+  const int nk = (T_ + TK - 1) / TK;
+  const int col0 = head * D;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->kr_full, 1);
+    mbar_init(&bars->kr_empty, 1);
+    mbar_init(&bars->v_full, 1);
+    mbar_init(&bars->v_empty, 1);
+    mbar_init(&bars->sbd_full, 1);
+    mbar_init(&bars->sbd_empty, 4);
+    mbar_init(&bars->p_full, 4);
+    mbar_init(&bars->o_done, 1);
+    mbar_init(&bars->done, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      prefetch_tmap(&tr);
+      int kr_issued = 0, v_issued = 0;
+      bool ok = true;
+      mbar_expect_tx(&bars->q_full, Q_BYTES);
+      tma_load_2d(smem + OFF_Q, &tq, &bars->q_full, col0, base + q0);
+      tma_load_2d(smem + OFF_Q + Q_SUB, &tq, &bars->q_full, col0 + 64, base + q0);
+      for (int j = 0; j < nk; ++j) {
+        const int k0 = j * TK;
+        const int band0 = max_len - TQ - q0 + k0;  // may be negative: TMA fills zeros
+        if (!mbar_wait(&bars->kr_empty, (j & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&bars->kr_full, K_BYTES + R_BYTES);
+        tma_load_2d(smem + OFF_K, &tk, &bars->kr_full, col0, base + k0);
+        tma_load_2d(smem + OFF_K + K_SUB, &tk, &bars->kr_full, col0 + 64, base + k0);
+        tma_load_2d(smem + OFF_R, &tr, &bars->kr_full, col0, band0);
+        tma_load_2d(smem + OFF_R + R_SUB, &tr, &bars->kr_full, col0 + 64, band0);
+        ++kr_issued;
+        if (!mbar_wait(&bars->v_empty, (j & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&bars->v_full, V_BYTES);
+        tma_load_2d(smem + OFF_V, &tv, &bars->v_full, col0, base + k0);
+        tma_load_2d(smem + OFF_V + V_SUB, &tv, &bars->v_full, col0 + 64, base + k0);
+        ++v_issued;
+      }
+      if (!ok) {
+        // Let the copies in flight land before the CTA exits.
+        att_drain(&bars->q_full, 0);
+        if (kr_issued) att_drain(&bars->kr_full, (kr_issued - 1) & 1);
+        if (v_issued) att_drain(&bars->v_full, (v_issued - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16(TQ, TK), id_bd = idesc_bf16(TQ, BAND), id_pv = idesc_bf16_bmn(TQ, D);
+      const uint32_t qa = smem_u32(smem + OFF_Q), ka = smem_u32(smem + OFF_K), ra = smem_u32(smem + OFF_R),
+                     va = smem_u32(smem + OFF_V);
+      bool ok = mbar_wait(&bars->q_full, 0, err, TB_DEV_ATTN_TIMEOUT, abort);
+      for (int j = 0; j < nk && ok; ++j) {
+        if (!mbar_wait(&bars->kr_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+        if (j > 0) {
+          // S and BD of the previous tile read, and P (in S's columns) consumed.
+          if (!mbar_wait(&bars->sbd_empty, (j - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+          if (!mbar_wait(&bars->o_done, (j - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + COL_S, sdesc_sw128(qa + s * Q_SUB) + 2 * k, sdesc_sw128(ka + s * K_SUB) + 2 * k, id_s,
+                     (s | k) != 0);
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + COL_BD, sdesc_sw128(qa + s * Q_SUB) + 2 * k, sdesc_sw128(ra + s * R_SUB) + 2 * k, id_bd,
+                     (s | k) != 0);
+        umma_commit(&bars->sbd_full);
+        umma_commit(&bars->kr_empty);
+        if (!mbar_wait(&bars->p_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+        if (!mbar_wait(&bars->v_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk)
+          umma_f16_ts(tmem + COL_O, tmem + COL_S + 8 * kk, sdesc_sw128_mn(va + 2048 * kk, V_SUB), id_pv,
+                      (j | kk) != 0);
+        umma_commit(&bars->o_done);
+        umma_commit(&bars->v_empty);
+      }
+      umma_commit(&bars->done);
+      att_drain(&bars->done, 0);
+    }
+  } else {
+    const int q = warp & 3;  // tensor-memory lane quarter: query rows 32q .. 32q+31
+    const int il = q * 32 + lane;
+    float* stage = reinterpret_cast<float*>(smem + OFF_ST) + q * 32 * ST_STRIDE;
+    float* cband = reinterpret_cast<float*>(smem + OFF_C) + q * WIN;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+    const int wcol = 96 - 32 * q;  // first BD column this warp's rows need
+    const int rel_rows = 2 * max_len - 1;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    uint32_t r[32];
+    for (int j = 0; j < nk; ++j) {
+      const int k0 = j * TK;
+      const int band0 = max_len - TQ - q0 + k0;
+      __syncwarp();  // every lane is done with the previous tile's cband
+      for (int t = lane; t < WIN; t += 32) {
+        const int n = band0 + wcol + t;
+        cband[t] = (n >= 0 && n < rel_rows) ? rel_c[(long long)n * 128 + head] : 0.f;
+      }
+      __syncwarp();
+      if (!att_warp_wait(&bars->sbd_full, j & 1, err, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sc[TK];
+      tmem_ld32(tl + COL_S, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 32; ++k) sc[k] = __uint_as_float(r[k]);
+      tmem_ld32(tl + COL_S + 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(r[k]);
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
+        tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(stage + lane * ST_STRIDE + 32 * c);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          dst[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]), __uint_as_float(r[4 * k + 2]),
+                               __uint_as_float(r[4 * k + 3]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sbd_empty);
+      // Scores: content + shifted position term, scaled into the base-2 domain.
+      const float* srow = stage + lane * ST_STRIDE + (31 - lane);
+      const float* crow = cband + (31 - lane);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int jj = 0; jj < TK; ++jj) {
+        const float v = (sc[jj] + srow[jj] + crow[jj]) * SCALE_LOG2;
+        sc[jj] = k0 + jj < T_ ? v : -INFINITY;
+        mx = fmaxf(mx, sc[jj]);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float corr = exp2f(m_run - m_new);
+      float sum = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < TK; jj += 2) {
+        const float p0 = exp2f(sc[jj] - m_new), p1 = exp2f(sc[jj + 1] - m_new);
+        sum += p0 + p1;
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+        r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      l_run = l_run * corr + sum;
+      m_run = m_new;
+      if (j > 0) {
+        if (!att_warp_wait(&bars->o_done, (j - 1) & 1, err, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, corr != 1.0f)) {
+          uint32_t o[32];
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(tl + COL_O + 32 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * corr);
+            tmem_st32(tl + COL_O + 32 * c, o);
+          }
+        }
+      }
+      tmem_st32(tl + COL_S, r);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full);
+    }
+    if (ok && nk > 0 && att_warp_wait(&bars->o_done, (nk - 1) & 1, err, abort)) {
+      tc_fence_after();
+      const float inv = 1.0f / l_run;
+      const bool valid = q0 + il < T_;
+      __nv_bfloat16* dst = out + (long long)(base + q0 + il) * TB_HIDDEN + col0;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(tl + COL_O + 32 * c, r);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int k = 0; k < 32; k += 4)
+            store4(dst + 32 * c + k, __uint_as_float(r[k]) * inv, __uint_as_float(r[k + 1]) * inv,
+                   __uint_as_float(r[k + 2]) * inv, __uint_as_float(r[k + 3]) * inv);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, att::TMEM_COLS);
+  }
+}
+
+static int launch_attn_tc(const void* qu, const void* k, const void* v, const void* rel, const float* rel_c,
+                          int max_len, const tb_batch& b, void* out, int* err, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(relpos_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, att::SMEM) !=
+        cudaSuccess)
+      return fail_cuda();
+    configured = true;
+  }
+  for (const void* p : {qu, k, v, rel})
+    if (reinterpret_cast<uintptr_t>(p) & 15) return TB_ERR_UNSUPPORTED;
+  CUtensorMap mq, mk, mv, mr;
+  const long long rows = b.t3_total;
+  if (!encode_tmap_2d(&mq, qu, rows, TB_HIDDEN, TB_HIDDEN, 64, att::TQ) ||
+      !encode_tmap_2d(&mk, k, rows, TB_HIDDEN, TB_HIDDEN, 64, att::TK) ||
+      !encode_tmap_2d(&mv, v, rows, TB_HIDDEN, TB_HIDDEN, 64, att::TK) ||
+      !encode_tmap_2d(&mr, rel, 2LL * max_len - 1, TB_HIDDEN, TB_HIDDEN, 64, att::BAND))
+    return TB_ERR_CUDA;
+  dim3 grid(b.n_attn_tiles, TB_HEADS);
+  relpos_attention_tc<<<grid, 192, att::SMEM, stream>>>(mq, mk, mv, mr, rel_c, max_len, b.t3_off, b.attn_tiles,
+                                                        reinterpret_cast<__nv_bfloat16*>(out), err);
+  return check_launch();
+}
+
 template <typename T>
 static int launch_attn_simt(const void* qu, const void* qv, const void* k, const void* v, const void* rel, int max_len,
                             const tb_batch& b, void* out, cudaStream_t stream) {
@@ -161,18 +472,20 @@ static int launch_attn_simt(const void* qu, const void* qv, const void* k, const
   return check_launch();
 }
 
-int attention_tile_rows(int dtype) {
-  (void)dtype;
-  return AQ;
-}
+int attention_tile_rows(int dtype) { return dtype == TB_BF16 ? att::TQ : AQ; }
 
 int relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
-                     int max_len, const tb_batch& b, void* out, int* err, cudaStream_t stream) {
-  (void)err;
+                     const float* rel_c, int max_len, const tb_batch& b, void* out, int* err, cudaStream_t stream) {
   if (b.n_attn_tiles <= 0) return TB_OK;
-  if (!qu || !qv || !k || !v || !rel || !out || !b.attn_tiles || !b.t3_off || b.max_t3 > max_len) return TB_ERR_ARG;
-  if (dtype == TB_BF16) return launch_attn_simt<__nv_bfloat16>(qu, qv, k, v, rel, max_len, b, out, stream);
-  if (dtype == TB_F32) return launch_attn_simt<float>(qu, qv, k, v, rel, max_len, b, out, stream);
+  if (!qu || !k || !v || !rel || !out || !b.attn_tiles || !b.t3_off || b.max_t3 > max_len) return TB_ERR_ARG;
+  if (dtype == TB_BF16) {
+    if (!rel_c || !err) return TB_ERR_ARG;
+    return launch_attn_tc(qu, k, v, rel, rel_c, max_len, b, out, err, stream);
+  }
+  if (dtype == TB_F32) {
+    if (!qv) return TB_ERR_ARG;
+    return launch_attn_simt<float>(qu, qv, k, v, rel, max_len, b, out, stream);
+  }
   return TB_ERR_ARG;
 }
 

@@ -158,6 +158,18 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem desc]^T: the A operand (K-major, bf16 pairs packed in
+// 32-bit columns, one row per lane) read from tensor memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -183,6 +195,37 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
          | ((uint64_t)1 << 46)                 // descriptor version for sm_100
          | ((uint64_t)2 << 61);                // layout: 128-byte swizzle
 }
+
+// Descriptor for an MN-major operand written by TMA with 128-byte swizzling: each row
+// (one K index) holds 64 consecutive MN elements; 8-row K groups are 1024 bytes apart
+// and consecutive 64-element MN chunks `mn_chunk_bytes` apart.
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr, uint32_t mn_chunk_bytes) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4)                 // start address
+         | ((uint64_t)((mn_chunk_bytes >> 4) & 0x3FFFu) << 16)  // leading byte offset: next MN chunk
+         | ((uint64_t)(1024 >> 4) << 32)                     // stride byte offset: next 8 K rows
+         | ((uint64_t)1 << 46)
+         | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor for kind::f16, bf16 inputs, f32 accumulator, K-major A and
+// MN-major B.
+__host__ __device__ constexpr uint32_t idesc_bf16_bmn(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// 32 lanes x 32 consecutive 32-bit columns to tensor memory; one row per thread.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 consecutive 32-bit columns from tensor memory; one row per thread.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -60,7 +60,7 @@ __device__ __forceinline__ void epi_group(const tb_epilogue& e, int m, int n, fl
       if (sec == 0) {
         float4 u = load4(e.bias_u + c), w = load4(e.bias_v + c);
         store4_dt(e.out, off, e.out_dtype, v0 + u.x, v1 + u.y, v2 + u.z, v3 + u.w);
-        store4_dt(e.out2, off, e.out_dtype, v0 + w.x, v1 + w.y, v2 + w.z, v3 + w.w);
+        if (e.out2) store4_dt(e.out2, off, e.out_dtype, v0 + w.x, v1 + w.y, v2 + w.z, v3 + w.w);
       } else {
         store4_dt(sec == 1 ? e.out3 : e.out4, off, e.out_dtype, v0, v1, v2, v3);
       }

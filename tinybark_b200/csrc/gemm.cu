@@ -120,7 +120,8 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
       if (m >= M) continue;
       const long long off = (long long)m * e.ldo + c;
       store4_dt(dst, off, e.out_dtype, v[it].x + u.x, v[it].y + u.y, v[it].z + u.z, v[it].w + u.w);
-      if (sec == 0) store4_dt(e.out2, off, e.out_dtype, v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
+      if (sec == 0 && e.out2)
+        store4_dt(e.out2, off, e.out_dtype, v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
     }
   } else if constexpr (EPI == TB_EPI_LSTM) {
     // Columns n..n+3 are the gates i, f, g, o of unit n / 4.
@@ -401,18 +402,23 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 // ---------------------------------------------------------------------------
 // Host side
 
-static bool encode_tmap(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
-                        int box_rows) {
+bool encode_tmap_2d(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
+                    int box_cols, int box_rows) {
   auto fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * 2)};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+static bool encode_tmap(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
+                        int box_rows) {
+  return encode_tmap_2d(map, ptr, rows, cols, ld_elems, 64, box_rows);
 }
 
 template <int BN, int EPI>

@@ -12,6 +12,9 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn tensor_map_encoder();
+// 2-D bf16 tensor map, 128-byte swizzle, box of box_cols x box_rows (box_cols * 2 <= 128).
+bool encode_tmap_2d(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
+                    int box_cols, int box_rows);
 int sm_count();
 int fail_cuda();     // records cudaGetLastError() and returns TB_ERR_CUDA
 int check_launch();  // TB_OK, or fail_cuda() if the last launch failed; counts the launch
@@ -23,7 +26,7 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
 int layernorm(const float* x, const float* w, const float* b, float* x_out, const float* w2, const float* b2, void* y,
               int y_dtype, int rows, cudaStream_t stream);
 int relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
-                     int max_len, const tb_batch& batch, void* out, int* err, cudaStream_t stream);
+                     const float* rel_c, int max_len, const tb_batch& batch, void* out, int* err, cudaStream_t stream);
 int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch& batch, void* out,
                    cudaStream_t stream);
 int subsample(const tb_model& m, const tb_batch& batch, const float* feats, float* x, void* ws, size_t ws_bytes,

@@ -130,6 +130,7 @@ class Engine:
 
         self._layer_arr = (L.Layer * self.layers)()
         self._rel_w: list[torch.Tensor] = []
+        self._pos_bias: list[tuple[torch.Tensor, torch.Tensor]] = []
         norms = ("norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2", "norm_out")
         for i in range(self.layers):
             q = f"encoder.layers.{i}."
@@ -144,8 +145,9 @@ class Engine:
             a = q + "self_attn."
             lay.qkv = _ptr(self._mat(w[a + "qkv"]))
             lay.o_proj = _ptr(self._mat(w[a + "o_proj.weight"]))
-            lay.bias_u = _ptr(self._vec(w[a + "bias_u"].reshape(-1)))
-            lay.bias_v = _ptr(self._vec(w[a + "bias_v"].reshape(-1)))
+            bu, bv = self._vec(w[a + "bias_u"].reshape(-1)), self._vec(w[a + "bias_v"].reshape(-1))
+            lay.bias_u, lay.bias_v = _ptr(bu), _ptr(bv)
+            self._pos_bias.append((bu, bv))
             self._rel_w.append(self._mat(w[a + "relative_k_proj.weight"]))
             c = q + "conv."
             pw1 = w[c + "pointwise_conv1.weight"].reshape(2 * L.HIDDEN, L.HIDDEN)
@@ -192,13 +194,17 @@ class Engine:
         n = max(-(-t3 // 128) * 128, 128)
         pos = positions(n).to(self.device, self.tdtype).contiguous()
         rows = 2 * n - 1
+        from . import kernels
+
         self._rel = []
         for i in range(self.layers):
             r = torch.empty(rows, L.HIDDEN, device=self.device, dtype=self.tdtype)
             ep = L.Epilogue(kind=L.EPI_STORE, out_dtype=self.dtype, out=r.data_ptr(), ldo=L.HIDDEN)
             self._gemm(pos, self._rel_w[i], ep)
-            self._rel.append(r)
+            c = kernels.rel_bias(r, *self._pos_bias[i])
+            self._rel.append((r, c))
             self._layer_arr[i].rel = r.data_ptr()
+            self._layer_arr[i].rel_c = c.data_ptr()
         self.max_len = n
         self.model.max_len = n
         self.check()

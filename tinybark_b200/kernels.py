@@ -60,10 +60,24 @@ class Frames:
         self.batch = b
 
 
-def attention(qu, qv, k, v, rel, max_len: int, frames: Frames, out) -> None:
-    L.check(L.lib.tb_relpos_attention(dtype_of(qu), qu.data_ptr(), qv.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                      rel.data_ptr(), max_len, C.byref(frames.batch), out.data_ptr(),
-                                      _err(qu.device).data_ptr(), _stream()), "tb_relpos_attention")
+def rel_bias(rel: torch.Tensor, bias_u: torch.Tensor, bias_v: torch.Tensor) -> torch.Tensor:
+    """(bias_v - bias_u)_h . rel[n, head h] as [rows, 128] fp32 (columns 8.. zero): the
+    position term the bf16 attention adds to (q + bias_u) . rel, through tb_gemm."""
+    w = torch.zeros(128, L.HIDDEN, device=rel.device, dtype=torch.float32)
+    diff = (bias_v - bias_u).float().reshape(L.HEADS, L.HEAD_DIM)
+    for h in range(L.HEADS):
+        w[h, h * L.HEAD_DIM : (h + 1) * L.HEAD_DIM] = diff[h]
+    out = torch.empty(rel.shape[0], 128, device=rel.device, dtype=torch.float32)
+    ep = L.Epilogue(kind=L.EPI_STORE, out_dtype=L.F32, out=out.data_ptr(), ldo=128)
+    gemm(rel, w.to(rel.dtype).contiguous(), ep)
+    return out
+
+
+def attention(qu, qv, k, v, rel, max_len: int, frames: Frames, out, rel_c=None) -> None:
+    L.check(L.lib.tb_relpos_attention(dtype_of(qu), qu.data_ptr(), None if qv is None else qv.data_ptr(),
+                                      k.data_ptr(), v.data_ptr(), rel.data_ptr(),
+                                      None if rel_c is None else rel_c.data_ptr(), max_len, C.byref(frames.batch),
+                                      out.data_ptr(), _err(qu.device).data_ptr(), _stream()), "tb_relpos_attention")
 
 
 def depthwise(x, w, b, frames: Frames, y) -> None:
