@@ -69,7 +69,9 @@ def shard(rank: int, count: int):
     seeds = [SEED * 10_000_000 + rank * 100_000 + i for i in range(count)]
     with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as pool:
         pcm = list(pool.map(lambda a: synthetic.clip(*a), zip(durs, seeds)))
-    return [synthetic.to_float(p) for p in pcm], durs
+    # Longest first, as Bark.tokens_batch orders a batch.
+    order = np.argsort(-durs, kind="stable")
+    return [synthetic.to_float(pcm[i]) for i in order], durs[order]
 
 
 def weights(layers: int):

@@ -91,6 +91,7 @@ typedef struct tb_epilogue {
   float* c;
   float* h;
   const int* mask;
+  const int* rows; /* if not NULL: only rows below *rows (device int, read at run time) are computed */
 } tb_epilogue;
 
 /* One conformer layer, device pointers. Matrices are tb_model.dtype; vectors fp32. */

@@ -25,6 +25,7 @@ class Epilogue(C.Structure):
         ("kind", i32), ("out_dtype", i32), ("out", vp), ("ldo", ll), ("bias", vp), ("alpha", f32),
         ("out2", vp), ("ldo2", ll), ("out3", vp), ("out4", vp), ("bias_u", vp), ("bias_v", vp),
         ("keys", vp), ("keys2", vp), ("split", i32), ("split_end", i32), ("c", vp), ("h", vp), ("mask", vp),
+        ("rows", vp),
     ]
 
 

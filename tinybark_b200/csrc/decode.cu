@@ -15,19 +15,26 @@
 //   proj:  dec = h1 W_p^T + b_p
 // The LSTM inputs [embedding(token) | h] are assembled from the fp32 state by the step
 // kernel, so no GEMM reads a buffer that its own epilogue writes.
+#include <algorithm>
 #include <chrono>
 #include <thread>
+#include <vector>
 
 #include "epilogue.cuh"
 #include "host.h"
 
 namespace tb {
 
+constexpr int DECODE_CHUNK = 32;       // iterations per captured graph
+constexpr int DECODE_MAX_CHUNKS = 8192;  // so max_cap <= 262144
+
 struct DecodeWs {
   unsigned long long *keys, *keys2;
   void *z, *x0, *x1, *hp;
   float *h, *c, *dec;
   int *frame, *it, *done, *mask, *count, *active;
+  int* m_chunk;  // [DECODE_MAX_CHUNKS]: only lanes below this index can run in chunk c
+  int* m_cur;    // [0]: the current chunk's bound, [1]: the current chunk
 };
 
 static DecodeWs carve(void* ws, int dtype, int lanes) {
@@ -54,13 +61,15 @@ static DecodeWs carve(void* ws, int dtype, int lanes) {
   w.mask = (int*)take(L * 4);
   w.count = (int*)take(L * 4);
   w.active = (int*)take(256);
+  w.m_chunk = (int*)take(DECODE_MAX_CHUNKS * 4);
+  w.m_cur = (int*)take(256);
   return w;
 }
 
 size_t decode_ws(int dtype, int lanes) {
   uint8_t* base = nullptr;
   DecodeWs w = carve(base, dtype, lanes);
-  return (size_t)(reinterpret_cast<uint8_t*>(w.active) - base) + 256;
+  return (size_t)(reinterpret_cast<uint8_t*>(w.m_cur) - base) + 256;
 }
 
 // Lane state initialisation and the inputs of the first step (token = blank, zero state).
@@ -98,7 +107,7 @@ template <typename T>
 __global__ void decode_prep_kernel(DecodeWs w, const float* __restrict__ enc, const int* __restrict__ enc_off,
                                    int lanes) {
   const int l = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (l >= lanes) return;
+  if (l >= lanes || l >= w.m_cur[0]) return;
   T* z = reinterpret_cast<T*>(w.z) + (long long)l * TB_PRED;
   if (lane == 0) w.keys[l] = 0ull, w.keys2[l] = 0ull;
   if (w.done[l]) return;
@@ -115,7 +124,7 @@ template <typename T>
 __global__ void decode_step_kernel(DecodeWs w, const T* __restrict__ emb, const int* __restrict__ enc_off,
                                    const int* __restrict__ cap, int lanes, int max_cap, int* __restrict__ tokens) {
   const int l = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (l >= lanes) return;
+  if (l >= lanes || l >= w.m_cur[0]) return;  // lanes past the bound finished before this chunk
   int step = 0, tok = 0;
   if (lane == 0) {
     if (!w.done[l]) {
@@ -177,14 +186,19 @@ __global__ void decode_step_kernel(DecodeWs w, const T* __restrict__ emb, const 
 }
 
 // Ends a chunk of iterations: publishes (lanes still running, summed over the chunk's
-// iterations; chunk number) to pinned host memory and resets the count.
-__global__ void decode_publish_kernel(int* active, volatile int* host_flag) {
-  const int chunk = active[1];
-  host_flag[0] = active[0];
-  __threadfence_system();
-  host_flag[1] = chunk;
+// iterations; chunk number) to pinned host memory when asked, resets the count and
+// moves the GEMMs' row bound to the next chunk's.
+__global__ void decode_chunk_end_kernel(int* active, int* m_cur, const int* m_chunk, int chunks,
+                                        volatile int* host_flag) {
+  const int chunk = m_cur[1];
+  if (host_flag) {
+    host_flag[0] = active[0];
+    __threadfence_system();
+    host_flag[1] = chunk;
+  }
   active[0] = 0;
-  active[1] = chunk + 1;
+  m_cur[0] = chunk + 1 < chunks ? m_chunk[chunk + 1] : 0;
+  m_cur[1] = chunk + 1;
 }
 
 // A non-blocking stream per thread and device, used only to record graphs.
@@ -206,6 +220,26 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   const int lane_blocks = (lanes + 7) / 8;
   const long long L = lanes;
 
+  // Row bound per chunk: lane l runs iterations [0, cap[l]), so it can run in chunk c
+  // only if 32c < cap[l]. With lanes ordered by length the bound shrinks as clips finish
+  // and the GEMMs stop computing finished lanes.
+  const int chunks = (max_cap + DECODE_CHUNK - 1) / DECODE_CHUNK;
+  if (chunks > DECODE_MAX_CHUNKS) return TB_ERR_ARG;
+  std::vector<int> caps(lanes), bound(chunks, 0);
+  if (cudaMemcpyAsync(caps.data(), cap, (size_t)lanes * sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return fail_cuda();
+  for (int l = 0; l < lanes; ++l) {
+    const int last = std::min(chunks, (std::max(caps[l], 0) + DECODE_CHUNK - 1) / DECODE_CHUNK);
+    for (int c = 0; c < last; ++c) bound[c] = l + 1;
+  }
+  const int head[2] = {bound[0], 0};
+  if (cudaMemcpyAsync(w.m_chunk, bound.data(), (size_t)chunks * sizeof(int), cudaMemcpyHostToDevice, stream) !=
+          cudaSuccess ||
+      cudaMemcpyAsync(w.m_cur, head, sizeof(head), cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return fail_cuda();
+
   tb_epilogue l0 = {};
   l0.kind = TB_EPI_LSTM;
   l0.out_dtype = dt;
@@ -213,6 +247,7 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   l0.c = w.c;
   l0.h = w.h;
   l0.mask = w.mask;
+  l0.rows = w.m_cur;
   l0.out = w.x1;  // h0 -> first half of layer 1's input
   l0.ldo = 2 * TB_PRED;
   tb_epilogue l1 = l0;
@@ -227,7 +262,9 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   pj.out = w.dec;
   pj.ldo = TB_PRED;
   pj.bias = m.dec_proj_b;
+  pj.rows = w.m_cur;
   tb_epilogue jt = {};
+  jt.rows = w.m_cur;
   jt.kind = TB_EPI_ARGMAX;
   jt.bias = m.joint_b;
   jt.keys = w.keys;
@@ -267,7 +304,7 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   // in device memory), so one chunk of iterations is captured once and replayed on the
   // caller's stream. Capture runs nothing, so it uses a stream of its own: the
   // caller's may be the legacy default stream, which cannot be captured.
-  constexpr int CHUNK = 32, AHEAD = 3;
+  constexpr int AHEAD = 3;
   const cudaStream_t cap_stream = capture_stream();
   if (!cap_stream) return fail_cuda();
   cudaGraph_t graph = nullptr;
@@ -275,9 +312,9 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   const long long launches_before = launch_count();
   if (cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return fail_cuda();
   int rc = TB_OK;
-  for (int i = 0; i < CHUNK && rc == TB_OK; ++i) rc = iteration(cap_stream);
-  if (rc == TB_OK && flag_dev) {
-    decode_publish_kernel<<<1, 1, 0, cap_stream>>>(w.active, flag_dev);
+  for (int i = 0; i < DECODE_CHUNK && rc == TB_OK; ++i) rc = iteration(cap_stream);
+  if (rc == TB_OK) {
+    decode_chunk_end_kernel<<<1, 1, 0, cap_stream>>>(w.active, w.m_cur, w.m_chunk, chunks, flag_dev);
     rc = check_launch();
   }
   const cudaError_t captured = cudaStreamEndCapture(cap_stream, &graph);
@@ -292,7 +329,6 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   }
   size_t nodes = 0;
   cudaGraphGetNodes(graph, nullptr, &nodes);
-  const int chunks = (max_cap + CHUNK - 1) / CHUNK;
   if (flag_dev) host_flag[0] = 1, host_flag[1] = -1;
   for (int c = 0; c < chunks && rc == TB_OK; ++c) {
     if (flag_dev) {

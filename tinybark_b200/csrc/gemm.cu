@@ -182,6 +182,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
+  if (e.rows) M = min(M, *e.rows);
   const int m_tiles = (M + C::BM - 1) / C::BM, n_tiles = N / BN, tiles = m_tiles * n_tiles, kb_count = K / C::BK;
 
   if (warp == 0) {
@@ -315,6 +316,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   __shared__ __align__(16) float Ws[2][SG_BK][SG_BN + SG_PAD];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * SG_BM, n0 = blockIdx.x * SG_BN;
+  if (e.rows) M = min(M, *e.rows);
+  if (m0 >= M) return;
   // Loader mapping: rows lr and lr + 64, k offset lk.
   const int lr = tid >> 2, lk = (tid & 3) * 4;
 
@@ -456,15 +459,20 @@ static int launch_tc_kind(const void* a, long long lda, const void* w, int m, in
   }
 }
 
-// The widest tile (fewest operand re-reads) that still gives every SM a tile; when none
-// does, the narrowest, for the most parallelism.
-static int pick_bn(int m, int n) {
-  const int m_tiles = (m + 127) / 128, sms = sm_count();
-  for (int bn : {256, 128, 64})
-    if (n % bn == 0 && m_tiles * (n / bn) >= sms) return bn;
-  for (int bn : {64, 128, 256})
-    if (n % bn == 0) return bn;
-  return 0;
+static int pick_bn(int m, int n, int k) {
+  // Tile width with the least operand traffic into the busiest SM: waves x (A + B bytes
+  // per k-block), plus a per-wave allowance for the prologue and epilogue (about two
+  // k-blocks). Wide tiles re-read A less; narrow ones spread small-M GEMMs over more SMs.
+  const long long m_tiles = (m + 127) / 128, sms = sm_count(), kb = k / 64;
+  int best = 0;
+  long long best_cost = 0;
+  for (int bn : {256, 128, 64}) {
+    if (n % bn) continue;
+    const long long tiles = m_tiles * (n / bn), waves = (tiles + sms - 1) / sms;
+    const long long cost = waves * (kb + 2) * (128 * 128 + bn * 128);
+    if (!best || cost < best_cost) best = bn, best_cost = cost;
+  }
+  return best;
 }
 
 int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
@@ -476,7 +484,7 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
   if (dtype == TB_BF16) {
     if (k % 64 || lda % 8 || (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
       return TB_ERR_UNSUPPORTED;
-    switch (pick_bn(m, n)) {
+    switch (pick_bn(m, n, k)) {
       case 256: return launch_tc_kind<256>(a, lda, w, m, n, k, e, err, stream);
       case 128: return launch_tc_kind<128>(a, lda, w, m, n, k, e, err, stream);
       case 64: return launch_tc_kind<64>(a, lda, w, m, n, k, e, err, stream);

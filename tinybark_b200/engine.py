@@ -304,7 +304,9 @@ class Engine:
         Bark.tokens returns them one clip at a time (tinybark/tinygrad/model.py:196-234)."""
         clips = [np.asarray(c, np.float32).reshape(-1) for c in clips]
         frames = [lengths.frames(len(c)) for c in clips]
-        keep = [i for i, f in enumerate(frames) if f >= 2]
+        # Longest first: the decoder's lanes then finish from the end of the batch, and its
+        # GEMMs shrink to the lanes still running.
+        keep = sorted((i for i, f in enumerate(frames) if f >= 2), key=lambda i: -frames[i])
         out: list[list[int]] = [[] for _ in clips]
         if not keep:
             return out
