@@ -26,7 +26,8 @@ enum tb_status {
   TB_ERR_ARG = 1,         /* bad size, pointer or enum */
   TB_ERR_CUDA = 2,        /* a CUDA runtime call failed (see tb_last_cuda_error) */
   TB_ERR_UNSUPPORTED = 3, /* no kernel for this shape / dtype */
-  TB_ERR_WORKSPACE = 4    /* workspace smaller than *_workspace_bytes */
+  TB_ERR_WORKSPACE = 4,   /* workspace smaller than *_workspace_bytes */
+  TB_ERR_TOO_LARGE = 5    /* more than the library's own scratch holds (tb_frontend_static) */
 };
 
 /* Bits a kernel or-s into the device error word. */
@@ -184,6 +185,22 @@ int tb_sm_count(int device, int* out);
 size_t tb_frontend_workspace_bytes(int clips, int frames_total);
 int tb_frontend(const tb_model* m, const float* samples, const long long* sample_off, const int* frame_off,
                 int clips, int frames_total, int max_frames, float* feats, void* ws, size_t ws_bytes, void* stream);
+
+/* ---- front-end without a caller-supplied workspace (no counterpart in the reference) ----
+ * The same features as tb_frontend, for callers that cannot allocate device memory:
+ * a real-time audio thread, where cudaMalloc can synchronize the device and stall the
+ * stream, or a host whose device memory is all owned by another allocator. The scratch
+ * lives in a fixed device array inside the library (about 1.1 MB on every GPU that loads
+ * it, kept until the process exits), so at most TB_FRONTEND_STATIC_MAX_CLIPS clips per
+ * call; more returns TB_ERR_TOO_LARGE before anything runs. The caller still allocates
+ * samples, offsets and feats. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current: make it before any stream
+ * capture. All calls share the array: calls that can overlap on the GPU (other streams,
+ * other threads) race and must be serialized by the caller. Nothing in it needs to start
+ * at zero: every scratch value is written before it is read. Allocates nothing. */
+#define TB_FRONTEND_STATIC_MAX_CLIPS 64
+int tb_frontend_static(const tb_model* m, const float* samples, const long long* sample_off, const int* frame_off,
+                       int clips, int frames_total, float* feats, void* stream);
 
 /* ---- LayerNorm over 1024: tinybark/tinygrad/model.py:56-57 (layernorm) ----
  * y = LN(x) (y_dtype), fp32 statistics, eps 1e-5. If x_out != NULL, LN(x) is also

@@ -10,7 +10,9 @@ LIB_PATH = Path(__file__).resolve().parent / "libtbcuda.so"
 
 F32, BF16 = 0, 1
 EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_BIAS_RELU, EPI_GLU, EPI_QKV, EPI_ARGMAX, EPI_LSTM = range(8)
-STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or dtype", 4: "workspace too small"}
+STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or dtype", 4: "workspace too small",
+          5: "more clips than the library's own scratch holds"}
+FRONTEND_STATIC_MAX_CLIPS = 64
 DEVICE_ERRORS = {1: "GEMM barrier wait timed out", 2: "attention barrier wait timed out", 4: "decode wait timed out"}
 
 HIDDEN, HEADS, HEAD_DIM, FFN, KERNEL, CHANNELS, MELS = 1024, 8, 128, 4096, 9, 256, 128
@@ -74,6 +76,7 @@ def _load() -> C.CDLL:
         "tb_sm_count": (i32, [i32, P(i32)]),
         "tb_frontend_workspace_bytes": (sz, [i32, i32]),
         "tb_frontend": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, sz, vp]),
+        "tb_frontend_static": (i32, [P(Model), vp, vp, vp, i32, i32, vp, vp]),
         "tb_layernorm": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
         "tb_gemm": (i32, [i32, vp, ll, vp, i32, i32, i32, P(Epilogue), vp, vp]),
         "tb_relpos_attention": (i32, [i32, vp, vp, vp, vp, vp, vp, i32, P(Batch), vp, vp, vp]),
@@ -96,6 +99,7 @@ lib = _load()
 # Every symbol include/tbcuda.h declares, for the export check.
 EXPORTS = (
     "tb_version", "tb_tile_rows", "tb_launch_count", "tb_last_cuda_error", "tb_sm_count", "tb_frontend_workspace_bytes", "tb_frontend",
+    "tb_frontend_static",
     "tb_layernorm", "tb_gemm", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
 )

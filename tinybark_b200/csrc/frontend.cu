@@ -10,6 +10,8 @@
 // split into the 257 real-input bins. Twiddles come from sincospi in fp64 per block.
 // stats_kernel / finish_kernel / normalize_kernel: per-clip mean and std per mel bin,
 // accumulated in fp64 over frame ranges, then applied in place.
+#include <mutex>
+
 #include "common.cuh"
 #include "host.h"
 
@@ -182,4 +184,54 @@ int frontend(const tb_model& m, const float* samples, const long long* sample_of
   return check_launch();
 }
 
+// ---------------------------------------------------------------------------
+// The front-end's scratch (per-range partial sums, per-clip statistics) held by the
+// library itself, for callers that cannot allocate device memory. Sized for
+// TB_FRONTEND_STATIC_MAX_CLIPS clips; every GPU that loads the library keeps it until
+// the process exits. Every byte is written before it is read, so nothing is cleared
+// between calls.
+
+constexpr size_t FE_STATIC_PART = ((size_t)TB_FRONTEND_STATIC_MAX_CLIPS * FE_SPLIT * TB_MELS * 16 + 255) / 256 * 256;
+constexpr size_t FE_STATIC_BYTES = FE_STATIC_PART + ((size_t)TB_FRONTEND_STATIC_MAX_CLIPS * TB_MELS * 8 + 255) / 256 * 256;
+static __device__ __align__(256) unsigned char g_frontend_scratch[FE_STATIC_BYTES];
+
+// The device address of the scratch on the current device, looked up once per device.
+// In host code the array's name is only a stand-in; kernels must be given this address.
+static void* frontend_scratch(int* status) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = fail_cuda();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_frontend_scratch) != cudaSuccess || !p) {
+      *status = fail_cuda();
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *status = TB_OK;
+  return addr[dev];
+}
+
+int frontend_static(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off,
+                    int clips, int frames_total, float* feats, cudaStream_t stream) {
+  if (clips > TB_FRONTEND_STATIC_MAX_CLIPS) return TB_ERR_TOO_LARGE;
+  int status = TB_OK;
+  void* scratch = frontend_scratch(&status);
+  if (!scratch) return status;
+  return frontend(m, samples, sample_off, frame_off, clips, frames_total, feats, scratch, FE_STATIC_BYTES, stream);
+}
+
 }  // namespace tb
+
+extern "C" int tb_frontend_static(const tb_model* m, const float* samples, const long long* sample_off,
+                                  const int* frame_off, int clips, int frames_total, float* feats, void* stream) {
+  if (!m) return TB_ERR_ARG;
+  return tb::frontend_static(*m, samples, sample_off, frame_off, clips, frames_total, feats,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
