@@ -53,7 +53,9 @@ def args_parser():
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
+    p.add_argument("--lanes", default="64,512", help="--micro: decoder lanes")
     p.add_argument("--profile", action="store_true", help="one step of the pipeline, for a profiler")
+    p.add_argument("--decode-groups", type=int, default=0, help="concurrent decoder groups (0: by batch size)")
     return p
 
 
@@ -232,9 +234,12 @@ def run_ours(args):
 
     import tinybark_b200
     from tinybark_b200 import _lib as L
-    from tinybark_b200.engine import Engine
+    from tinybark_b200.engine import Engine, lane_order
 
     clips, durs = shard(rank, args.clips_per_rank)
+    # The decoder's lane order, as Bark.tokens_batch orders a batch.
+    order = lane_order(list(range(len(clips))), [len(c) // 160 for c in clips], args.decode_groups or None)
+    clips, durs = [clips[i] for i in order], durs[order]
     tensors, cfg = weights(args.layers)
     bark = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg))
     eng: Engine = bark.engine
@@ -246,7 +251,7 @@ def run_ours(args):
     def step():
         feats = eng.features(samples, sample_off, plan)
         enc = eng.encode(feats, plan)
-        return eng.decode(enc, plan)
+        return eng.decode(enc, plan, groups=args.decode_groups or None)
 
     def barrier():
         torch.cuda.synchronize()
@@ -279,7 +284,7 @@ def run_ours(args):
     eng.check()
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
     barrier()
-    stages = stage_split(eng, samples, sample_off, plan)
+    stages = stage_split(eng, samples, sample_off, plan, args.decode_groups or None)
     total_audio = audio_rank
     if world > 1:
         t = torch.tensor([audio_rank], device=dev, dtype=torch.float64)
@@ -464,6 +469,38 @@ def run_micro(args):
                      frac=nbytes / s2 / 1e9 / hbm, bound="hbm")
                 emit(kernel="conv_pw2_residual", dtype=dt_name, rows=bt, us=s3 * 1e6,
                      tflops=2 * bt * 1024 * 1024 / s3 / 1e12)
+            if want("decode") and code == L.BF16 and bt == max(map(int, args.rows.split(","))):
+                # The decoder's GEMMs at `--lanes` lanes, weights resident in L2 as in the
+                # greedy loop (back-to-back launches, no flush).
+                for lanes in map(int, args.lanes.split(",")):
+                    z, x0 = rnd(lanes, 640, dt=dt), rnd(lanes, 1280, dt=dt)
+                    wj, wl, wp = rnd(8448, 640, dt=dt) / 25, rnd(2560, 1280, dt=dt) / 36, rnd(640, 640, dt=dt) / 25
+                    bj, bl, bp = rnd(8448), rnd(2560), rnd(640)
+                    keys = torch.zeros(2, lanes, dtype=torch.int64, device=dev)
+                    c, h, mask = rnd(lanes, 640), rnd(lanes, 640), torch.ones(lanes, dtype=torch.int32, device=dev)
+                    dec, zz = torch.empty(lanes, 640, device=dev), torch.empty(lanes, 640, device=dev, dtype=dt)
+                    enc, erow = rnd(lanes, 640), torch.arange(lanes, dtype=torch.int32, device=dev)
+                    hout = torch.empty(lanes, 1280, device=dev, dtype=dt)
+                    cases = {
+                        "decode_joint_argmax": (z, wj, L.Epilogue(kind=L.EPI_ARGMAX, bias=bj.data_ptr(),
+                                                                   keys=keys[0].data_ptr(), keys2=keys[1].data_ptr(),
+                                                                   split=8256, split_end=8261)),
+                        "decode_lstm": (x0, wl, L.Epilogue(kind=L.EPI_LSTM, out_dtype=code, bias=bl.data_ptr(),
+                                                           c=c.data_ptr(), h=h.data_ptr(), mask=mask.data_ptr(),
+                                                           out=hout.data_ptr(), ldo=1280)),
+                        "decode_proj_joint_in": (h.to(dt), wp, L.Epilogue(kind=L.EPI_JOINT_IN, out_dtype=code,
+                                                                          bias=bp.data_ptr(), out=dec.data_ptr(),
+                                                                          ldo=640, out2=zz.data_ptr(), ldo2=640,
+                                                                          gather=enc.data_ptr(),
+                                                                          gather_row=erow.data_ptr())),
+                    }
+                    for name, (a, w, ep) in cases.items():
+                        for _ in range(3):
+                            K.gemm(a, w, ep)
+                        s = timed(lambda: K.gemm(a, w, ep), iters=50)
+                        fl = 2 * lanes * w.shape[0] * w.shape[1]
+                        emit(kernel=name, dtype=dt_name, lanes=lanes, us=s * 1e6, tflops=fl / s / 1e12,
+                             weight_gbs=w.numel() * 2 / s / 1e9)
             if want("mhsa"):
                 for t in map(int, filter(None, args.lengths.split(","))):
                     if t > bt and bt != min(map(int, args.rows.split(","))):
@@ -482,7 +519,7 @@ def run_micro(args):
     K.check(dev)
 
 
-def stage_split(eng, samples, sample_off, plan):
+def stage_split(eng, samples, sample_off, plan, groups=None):
     """Milliseconds of front-end, encoder and decode in one untimed extra step."""
     import torch
 
@@ -492,7 +529,7 @@ def stage_split(eng, samples, sample_off, plan):
     ev[1].record()
     enc = eng.encode(feats, plan)
     ev[2].record()
-    eng.decode(enc, plan)
+    eng.decode(enc, plan, groups=groups)
     ev[3].record()
     torch.cuda.synchronize()
     return {k: ev[i].elapsed_time(ev[i + 1]) for i, k in enumerate(("frontend", "encoder", "decode"))}
@@ -505,14 +542,19 @@ def run_profile(args):
     import tinybark_b200
 
     torch.cuda.set_device(0)
+    from tinybark_b200.engine import lane_order
+
+    groups = args.decode_groups or None
     clips, durs = shard(0, args.clips_per_rank)
+    order = lane_order(list(range(len(clips))), [len(c) // 160 for c in clips], groups)
+    clips, durs = [clips[i] for i in order], durs[order]
     tensors, cfg = weights(args.layers)
     bark = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg))
     eng = bark.engine
     plan = eng.plan([len(c) // 160 for c in clips])
     samples, sample_off = eng.upload(clips)
     for _ in range(args.steps):
-        split = stage_split(eng, samples, sample_off, plan)
+        split = stage_split(eng, samples, sample_off, plan, groups)
     eng.check()
     print(json.dumps({"profile_step_ms": split, "clips": len(clips), "audio_s": float(np.sum(durs))}), flush=True)
 

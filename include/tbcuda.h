@@ -67,9 +67,13 @@ enum tb_epilogue_kind {
   TB_EPI_QKV = 5,       /* N = 3072: out = q+bias_u, out2 = q+bias_v, out3 = k, out4 = v    */
   TB_EPI_ARGMAX = 6,    /* joint head: argmax of acc+bias over [0,split) into keys[m] and
                            over [split, split_end) into keys2[m]; first index wins ties   */
-  TB_EPI_LSTM = 7       /* W rows gate-interleaved (row 4u+g, gates i,f,g,o): LSTM cell for
+  TB_EPI_LSTM = 7,      /* W rows gate-interleaved (row 4u+g, gates i,f,g,o): LSTM cell for
                            rows with mask[m] != 0: c[m,u], h[m,u] updated, h also written
                            to out[m*ldo+u] and out2[m*ldo2+u] (out_dtype)                  */
+  TB_EPI_JOINT_IN = 8   /* the decoder projector: out[m,n] = acc + bias[n] (fp32), and for
+                           rows with gather_row[m] >= 0 the joint's next input
+                           out2[m*ldo2+n] = relu(gather[gather_row[m]*ldo + n] + out[m,n])
+                           (out_dtype)                                                    */
 };
 
 typedef struct tb_epilogue {
@@ -93,6 +97,8 @@ typedef struct tb_epilogue {
   float* h;
   const int* mask;
   const int* rows; /* if not NULL: only rows below *rows (device int, read at run time) are computed */
+  const float* gather;    /* TB_EPI_JOINT_IN: rows of N values (the encoder frames) */
+  const int* gather_row;  /* TB_EPI_JOINT_IN: row of `gather` for each output row, < 0 to skip */
 } tb_epilogue;
 
 /* One conformer layer, device pointers. Matrices are tb_model.dtype; vectors fp32. */
@@ -249,11 +255,18 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
  * tinybark/mojo/bark/model.mojo:294-318 (decode) ----
  * One lane per clip, all lanes stepped together. enc [t3_total, 640] fp32 packed by
  * clip (enc_off [lanes+1]); cap [lanes] = 10 * subsampled(frames + 1, 3) - 1.
- * tokens: [lanes, max_cap] int32; counts: [lanes]. host_flag: pinned host int used to
- * stop early once every lane is done (may be NULL: then max_cap iterations run). */
-size_t tb_decode_workspace_bytes(int dtype, int lanes);
+ * tokens: [lanes, max_cap] int32; counts: [lanes].
+ * The lanes are split into `groups` (1..8) contiguous groups decoded concurrently, group
+ * 0 on `stream` and the others on the library's own streams, joined back into `stream`
+ * before return: group g holds ceil((lanes - g) / groups) lanes, so dealing clips
+ * (longest first) round-robin into groups gives balanced groups. Within a group, lanes
+ * ordered longest first let its GEMMs shrink as clips finish.
+ * host_flag: pinned host memory, 2 ints per group, used to stop a group early once all
+ * its lanes are done (may be NULL: then every group runs its longest cap). */
+size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups);
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
-                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, void* stream);
+                  int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
+                  void* stream);
 
 #ifdef __cplusplus
 }

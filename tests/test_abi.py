@@ -37,7 +37,9 @@ def test_workspace_queries_need_no_gpu():
     lib = _lib.lib
     assert lib.tb_encoder_workspace_bytes(_lib.BF16, 250, 125) > 125 * 1024 * 2 * 10
     assert lib.tb_encoder_workspace_bytes(_lib.F32, 250, 125) > lib.tb_encoder_workspace_bytes(_lib.BF16, 250, 125)
-    assert lib.tb_decode_workspace_bytes(_lib.BF16, 64) > 64 * 640 * 4
+    one = lib.tb_decode_workspace_bytes(_lib.BF16, 64, 1)
+    assert one > 64 * 640 * 4
+    assert lib.tb_decode_workspace_bytes(_lib.BF16, 64, 4) >= one
     assert lib.tb_frontend_workspace_bytes(4, 1000) >= 4 * 128 * 16
     assert _lib.tile_rows(_lib.F32)[0] == 2
 

@@ -66,10 +66,10 @@ def test_encoder_24_layers_10s(dtype, tol):
     assert err < tol
 
 
-def run_decode(eng, frames_list, feature_frames):
+def run_decode(eng, frames_list, feature_frames, groups=None):
     plan = eng.plan(feature_frames)
     enc = torch.from_numpy(np.concatenate(frames_list)).cuda()
-    tokens, counts = eng.decode(enc, plan)
+    tokens, counts = eng.decode(enc, plan, groups=groups)
     eng.check()
     t, c = tokens.cpu().numpy(), counts.cpu().numpy()
     return [t[i, : c[i]].tolist() for i in range(len(frames_list))]
@@ -85,9 +85,11 @@ def test_decode_matches_reference_loop(case):
     assert tokens == g["tokens"]
 
 
-def test_decode_lanes_are_independent():
+@pytest.mark.parametrize("groups", [1, 2, 4])
+def test_decode_lanes_are_independent(groups):
     """The four golden cases' encoder frames as four lanes of one batch, under the
-    'mixed' weights, each equal to the oracle's single-clip loop."""
+    'mixed' weights, each equal to the oracle's single-clip loop, with the lanes
+    decoded as 1, 2 or 4 concurrent groups."""
     from golden.make_golden import DECODE_CASES, decode_frames, decode_weights
     from oracle import decoder
 
@@ -96,7 +98,7 @@ def test_decode_lanes_are_independent():
     cases = list(DECODE_CASES.values())
     frames = [decode_frames(c) for c in cases]
     ff = [c["feature_frames"] for c in cases]
-    got = run_decode(eng, frames, ff)
+    got = run_decode(eng, frames, ff, groups)
     dec = decoder.Decoder(sd)
     for fr, f, g in zip(frames, ff, got):
         assert g == dec.greedy(fr, f)

@@ -9,7 +9,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libtbcuda.so"
 
 F32, BF16 = 0, 1
-EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_BIAS_RELU, EPI_GLU, EPI_QKV, EPI_ARGMAX, EPI_LSTM = range(8)
+EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_BIAS_RELU, EPI_GLU, EPI_QKV, EPI_ARGMAX, EPI_LSTM, EPI_JOINT_IN = range(9)
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or dtype", 4: "workspace too small",
           5: "more clips than the library's own scratch holds"}
 FRONTEND_STATIC_MAX_CLIPS = 64
@@ -27,7 +27,7 @@ class Epilogue(C.Structure):
         ("kind", i32), ("out_dtype", i32), ("out", vp), ("ldo", ll), ("bias", vp), ("alpha", f32),
         ("out2", vp), ("ldo2", ll), ("out3", vp), ("out4", vp), ("bias_u", vp), ("bias_v", vp),
         ("keys", vp), ("keys2", vp), ("split", i32), ("split_end", i32), ("c", vp), ("h", vp), ("mask", vp),
-        ("rows", vp),
+        ("rows", vp), ("gather", vp), ("gather_row", vp),
     ]
 
 
@@ -85,8 +85,8 @@ def _load() -> C.CDLL:
         "tb_subsample": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),
         "tb_encoder_workspace_bytes": (sz, [i32, i32, i32]),
         "tb_encoder_forward": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),
-        "tb_decode_workspace_bytes": (sz, [i32, i32]),
-        "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
+        "tb_decode_workspace_bytes": (sz, [i32, i32, i32]),
+        "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

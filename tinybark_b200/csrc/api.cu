@@ -13,9 +13,10 @@ namespace tb {
 int frontend(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
              int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t frontend_ws(int clips);
-size_t decode_ws(int dtype, int lanes);
+size_t decode_ws_groups(int dtype, int lanes, int groups);
 int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
-               int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, cudaStream_t stream);
+               int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
+               cudaStream_t stream);
 
 static thread_local std::string g_last_error;
 
@@ -49,6 +50,13 @@ EncodeTiledFn tensor_map_encoder() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
+}
+
+static thread_local int g_sm_budget = 0;
+void set_sm_budget(int n) { g_sm_budget = n; }
+int sm_budget() {
+  const int s = sm_count();
+  return g_sm_budget > 0 && g_sm_budget < s ? g_sm_budget : s;
 }
 
 int sm_count() {
@@ -266,12 +274,17 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
   return encoder_forward(*m, *batch, feats, enc, ws, ws_bytes, err, as_stream(stream));
 }
 
-size_t tb_decode_workspace_bytes(int dtype, int lanes) { return decode_ws(dtype, lanes); }
+size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups) {
+  if (lanes <= 0) return 0;
+  groups = groups < 1 ? 1 : (groups > 8 ? 8 : groups);
+  return decode_ws_groups(dtype, lanes, groups < lanes ? groups : lanes);
+}
 
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
-                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, void* stream) {
+                  int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
+                  void* stream) {
   if (!m) return TB_ERR_ARG;
-  return tdt_decode(*m, enc, enc_off, cap, lanes, max_cap, tokens, counts, ws, ws_bytes, host_flag, err,
+  return tdt_decode(*m, enc, enc_off, cap, lanes, max_cap, groups, tokens, counts, ws, ws_bytes, host_flag, err,
                     as_stream(stream));
 }
 

@@ -204,6 +204,8 @@ __global__ void __launch_bounds__(192, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dep_wait();
+  grid_dep_launch();
   const int clip = tiles[2 * blockIdx.x], q0 = tiles[2 * blockIdx.x + 1], head = blockIdx.y;
   const int base = t3_off[clip], T_ = t3_off[clip + 1] - base;
   const int nk = (T_ + TK - 1) / TK;
@@ -449,9 +451,8 @@ static int launch_attn_tc(const void* qu, const void* k, const void* v, const vo
       !encode_tmap_2d(&mr, rel, 2LL * max_len - 1, TB_HIDDEN, TB_HIDDEN, 64, att::BAND))
     return TB_ERR_CUDA;
   dim3 grid(b.n_attn_tiles, TB_HEADS);
-  relpos_attention_tc<<<grid, 192, att::SMEM, stream>>>(mq, mk, mv, mr, rel_c, max_len, b.t3_off, b.attn_tiles,
-                                                        reinterpret_cast<__nv_bfloat16*>(out), err);
-  return check_launch();
+  return launch_pdl(relpos_attention_tc, grid, 192, att::SMEM, stream, mq, mk, mv, mr, rel_c, max_len, b.t3_off,
+                    b.attn_tiles, reinterpret_cast<__nv_bfloat16*>(out), err);
 }
 
 template <typename T>

@@ -69,6 +69,17 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int index) {
 __device__ __forceinline__ int argmax_index(unsigned long long key) { return (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)); }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch. Kernels launched with programmatic stream
+// serialization may start before their predecessor on the stream has finished: each
+// kernel here runs only its prologue (barrier init, tensor-memory allocation, descriptor
+// prefetch) before grid_dep_wait(), which returns once the predecessor has completed and
+// its writes are visible; grid_dep_launch() then lets the successor start its own
+// prologue. Without that launch attribute both are no-ops.
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // Timers, shared-memory addresses, mbarriers
 
 __device__ __forceinline__ uint64_t globaltimer() {

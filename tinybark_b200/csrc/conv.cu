@@ -16,6 +16,8 @@ __global__ void __launch_bounds__(256) depthwise_silu_kernel(const T* __restrict
                                                              const float* __restrict__ b,
                                                              const int* __restrict__ row_clip,
                                                              const int* __restrict__ off, int rows, T* __restrict__ y) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int c = blockIdx.y * 256 + threadIdx.x;
   const int r0 = blockIdx.x * DW_ROWS;
   float taps[TB_KERNEL];
@@ -51,15 +53,13 @@ int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, c
   if (!glu || !w || !b || !out || !bt.t3_clip || !bt.t3_off) return TB_ERR_ARG;
   dim3 grid((rows + DW_ROWS - 1) / DW_ROWS, TB_HIDDEN / 256);
   if (dtype == TB_BF16)
-    depthwise_silu_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(glu), w, b,
-                                                                   bt.t3_clip, bt.t3_off, rows,
-                                                                   reinterpret_cast<__nv_bfloat16*>(out));
-  else if (dtype == TB_F32)
-    depthwise_silu_kernel<float><<<grid, 256, 0, stream>>>(reinterpret_cast<const float*>(glu), w, b, bt.t3_clip,
-                                                           bt.t3_off, rows, reinterpret_cast<float*>(out));
-  else
-    return TB_ERR_ARG;
-  return check_launch();
+    return launch_pdl(depthwise_silu_kernel<__nv_bfloat16>, grid, 256, 0, stream,
+                      reinterpret_cast<const __nv_bfloat16*>(glu), w, b, bt.t3_clip, bt.t3_off, rows,
+                      reinterpret_cast<__nv_bfloat16*>(out));
+  if (dtype == TB_F32)
+    return launch_pdl(depthwise_silu_kernel<float>, grid, 256, 0, stream, reinterpret_cast<const float*>(glu), w, b,
+                      bt.t3_clip, bt.t3_off, rows, reinterpret_cast<float*>(out));
+  return TB_ERR_ARG;
 }
 
 }  // namespace tb

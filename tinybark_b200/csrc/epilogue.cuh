@@ -66,6 +66,18 @@ __device__ __forceinline__ void epi_group(const tb_epilogue& e, int m, int n, fl
       }
       break;
     }
+    case TB_EPI_JOINT_IN: {
+      float4 b = load4(e.bias + n);
+      v0 += b.x, v1 += b.y, v2 += b.z, v3 += b.w;
+      store4(reinterpret_cast<float*>(e.out) + (long long)m * e.ldo + n, v0, v1, v2, v3);
+      const int g = e.gather_row[m];
+      if (g >= 0) {
+        float4 x = load4(e.gather + (long long)g * e.ldo + n);
+        store4_dt(e.out2, (long long)m * e.ldo2 + n, e.out_dtype, fmaxf(x.x + v0, 0.f), fmaxf(x.y + v1, 0.f),
+                  fmaxf(x.z + v2, 0.f), fmaxf(x.w + v3, 0.f));
+      }
+      break;
+    }
     case TB_EPI_LSTM: {
       if (e.mask && e.mask[m] == 0) break;
       int u = n >> 2;  // state rows are TB_PRED units long

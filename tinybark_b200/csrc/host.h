@@ -16,6 +16,10 @@ EncodeTiledFn tensor_map_encoder();
 bool encode_tmap_2d(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
                     int box_cols, int box_rows);
 int sm_count();
+// SMs a GEMM launched from this thread may plan for (all by default): kernels that run
+// concurrently on several streams each take a share.
+int sm_budget();
+void set_sm_budget(int n);  // 0: all
 int fail_cuda();     // records cudaGetLastError() and returns TB_ERR_CUDA
 int check_launch();  // TB_OK, or fail_cuda() if the last launch failed; counts the launch
 void count_launches(long long n);  // adds kernels run by a graph replay (or removes captured ones)
@@ -33,6 +37,24 @@ int subsample(const tb_model& m, const tb_batch& batch, const float* feats, floa
               int* err, cudaStream_t stream);
 size_t subsample_ws(int dtype, int t2_total, int t3_total);
 int attention_tile_rows(int dtype);
+
+// Launches `kernel` with programmatic stream serialization (see grid_dep_wait in
+// common.cuh): its prologue may overlap the end of the previous kernel on the stream.
+template <typename... Params, typename... Args>
+int launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+  return check_launch();
+}
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 inline size_t dsize(int dtype) { return dtype == TB_BF16 ? 2 : 4; }

@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
                                                         const float* __restrict__ b, float* x_out,
                                                         const float* __restrict__ w2, const float* __restrict__ b2,
                                                         OutT* y, int rows) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -67,13 +69,12 @@ int layernorm(const float* x, const float* w, const float* b, float* x_out, cons
   if (!x || !w || !b || !y || (w2 && (!b2 || !x_out))) return TB_ERR_ARG;
   dim3 grid((rows + 7) / 8);
   if (y_dtype == TB_BF16)
-    layernorm_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(x, w, b, x_out, w2, b2,
-                                                              reinterpret_cast<__nv_bfloat16*>(y), rows);
-  else if (y_dtype == TB_F32)
-    layernorm_kernel<float><<<grid, 256, 0, stream>>>(x, w, b, x_out, w2, b2, reinterpret_cast<float*>(y), rows);
-  else
-    return TB_ERR_ARG;
-  return check_launch();
+    return launch_pdl(layernorm_kernel<__nv_bfloat16>, grid, 256, 0, stream, x, w, b, x_out, w2, b2,
+                      reinterpret_cast<__nv_bfloat16*>(y), rows);
+  if (y_dtype == TB_F32)
+    return launch_pdl(layernorm_kernel<float>, grid, 256, 0, stream, x, w, b, x_out, w2, b2,
+                      reinterpret_cast<float*>(y), rows);
+  return TB_ERR_ARG;
 }
 
 }  // namespace tb

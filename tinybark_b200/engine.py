@@ -20,6 +20,24 @@ from . import _lib as L
 from . import lengths, tables
 
 DTYPES = {"fp32": L.F32, "bf16": L.BF16}
+MAX_DECODE_GROUPS = 8
+
+
+def decode_groups(lanes: int) -> int:
+    """Concurrent decoder groups for `lanes` clips: one group per 128 clips, at most 4.
+    A decoder step's GEMMs are too small to fill the GPU at a few hundred rows, so
+    independent groups on separate streams run side by side instead of one after another."""
+    return max(1, min(4, lanes // 128))
+
+
+def lane_order(idx: list[int], frames: list[int], groups: int | None = None) -> list[int]:
+    """Orders clips `idx` (frame counts `frames[i]`) for the decoder: longest first, dealt
+    round-robin into `groups` groups (default decode_groups), the groups concatenated.
+    Each group then holds clips of every length, and within a group the lanes finish
+    from its end, so its GEMMs shrink to the lanes still running."""
+    order = sorted(idx, key=lambda i: -frames[i])
+    g = decode_groups(len(order)) if groups is None else groups
+    return [i for k in range(g) for i in order[k::g]]
 
 
 def _stream(device: torch.device) -> int:
@@ -95,7 +113,7 @@ class Engine:
         self._keep: list[torch.Tensor] = []
         with torch.cuda.device(self.device):
             self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
-            self.host_flag = torch.zeros(4, dtype=torch.int32).pin_memory()
+            self.host_flag = torch.zeros(2 * MAX_DECODE_GROUPS, dtype=torch.int32).pin_memory()
             self._pack(tensors)
             self.max_len = 0
             self.ensure_len(max_len)
@@ -272,17 +290,22 @@ class Engine:
                 "tb_encoder_forward")
         return enc
 
-    def decode(self, enc: torch.Tensor, plan: Plan, early_exit: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
-        """Greedy TDT decoding of every clip; returns device (tokens [clips, max_cap], counts [clips])."""
+    def decode(self, enc: torch.Tensor, plan: Plan, early_exit: bool = True,
+               groups: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Greedy TDT decoding of every clip; returns device (tokens [clips, max_cap], counts [clips]).
+        The clips are decoded as `groups` concurrent groups (default decode_groups(clips)),
+        group g holding clips g, g + groups, ... of the plan's order reshuffled by
+        lane_order; any order gives the same tokens."""
         b = plan.batch
+        g = decode_groups(b.clips) if groups is None else int(groups)
         tokens = torch.empty(b.clips, plan.max_cap, device=self.device, dtype=torch.int32)
         counts = torch.empty(b.clips, device=self.device, dtype=torch.int32)
-        nbytes = L.lib.tb_decode_workspace_bytes(self.dtype, b.clips)
+        nbytes = L.lib.tb_decode_workspace_bytes(self.dtype, b.clips, g)
         ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
         flag = self.host_flag.data_ptr() if early_exit else None
         L.check(L.lib.tb_tdt_decode(C.byref(self.model), enc.data_ptr(), plan.t3_off.data_ptr(), plan.caps.data_ptr(),
-                                    b.clips, plan.max_cap, tokens.data_ptr(), counts.data_ptr(), ws.data_ptr(), nbytes,
-                                    flag, self.err.data_ptr(), _stream(self.device)), "tb_tdt_decode")
+                                    b.clips, plan.max_cap, g, tokens.data_ptr(), counts.data_ptr(), ws.data_ptr(),
+                                    nbytes, flag, self.err.data_ptr(), _stream(self.device)), "tb_tdt_decode")
         return tokens, counts
 
     # ------------------------------------------------------------------ end to end
@@ -304,9 +327,7 @@ class Engine:
         Bark.tokens returns them one clip at a time (tinybark/tinygrad/model.py:196-234)."""
         clips = [np.asarray(c, np.float32).reshape(-1) for c in clips]
         frames = [lengths.frames(len(c)) for c in clips]
-        # Longest first: the decoder's lanes then finish from the end of the batch, and its
-        # GEMMs shrink to the lanes still running.
-        keep = sorted((i for i, f in enumerate(frames) if f >= 2), key=lambda i: -frames[i])
+        keep = lane_order([i for i, f in enumerate(frames) if f >= 2], frames)
         out: list[list[int]] = [[] for _ in clips]
         if not keep:
             return out
