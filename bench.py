@@ -76,6 +76,19 @@ def shard(rank: int, count: int):
     return [synthetic.to_float(pcm[i]) for i in order], durs[order]
 
 
+def reduce_over_ranks(x: float, op: str, device) -> float:
+    """x reduced ("max" or "sum") over the ranks of the default process group, as float64
+    on `device`; x itself without a group. Every rank must call it at the same point."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def weights(layers: int):
     from tinybark_b200 import synthetic
     from tinybark_b200 import weights as w
@@ -260,11 +273,7 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_over_ranks(x, "max", dev)
 
     for _ in range(args.warmup):
         step()
@@ -285,11 +294,7 @@ def run_ours(args):
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
     barrier()
     stages = stage_split(eng, samples, sample_off, plan, args.decode_groups or None)
-    total_audio = audio_rank
-    if world > 1:
-        t = torch.tensor([audio_rank], device=dev, dtype=torch.float64)
-        dist.all_reduce(t)
-        total_audio = float(t.item())
+    total_audio = reduce_over_ranks(audio_rank, "sum", dev)
     value = total_audio / (ms / 1000.0)
 
     # End to end through the public API: host float32 arrays in, token lists out.

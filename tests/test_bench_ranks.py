@@ -1,0 +1,80 @@
+"""The multi-rank host logic of bench.py on CPU: two gloo ranks, as torchrun launches the
+GPU ranks. Each rank's shard is its own seeded set of clips (no collective on the data
+path), the step time is the max over ranks and the audio total the sum."""
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank: int, world: int, port: int, out) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, str(ROOT))
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import bench
+
+    dist.init_process_group("gloo", timeout=timedelta(seconds=60))
+    try:
+        r, w, local = bench.rank_info()
+        clips, durs = bench.shard(r, 3)
+        step_ms = 100.0 + 10.0 * r  # rank 1 is the slower one
+        out.put({
+            "rank": r, "world": w, "local": local,
+            "durs": [float(d) for d in durs],
+            "lens": [len(c) for c in clips],
+            "max": bench.reduce_over_ranks(step_ms, "max", torch.device("cpu")),
+            "sum": bench.reduce_over_ranks(float(np.sum(durs)), "sum", torch.device("cpu")),
+        })
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_shard_and_reduce():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted((q.get(timeout=180) for _ in procs), key=lambda d: d["rank"])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [g["rank"] for g in got] == [0, 1] and all(g["world"] == 2 for g in got)
+    # Shards differ between ranks, are longest first and hold 2-30 s clips of 16 kHz audio.
+    assert got[0]["durs"] != got[1]["durs"]
+    for g in got:
+        assert g["durs"] == sorted(g["durs"], reverse=True)
+        assert all(2.0 <= d < 30.0 for d in g["durs"])
+        assert all(abs(n - 16000 * d) <= 1 for n, d in zip(g["lens"], g["durs"]))
+    # Max over ranks for the time, sum for the audio, the same on every rank.
+    assert all(g["max"] == 110.0 for g in got)
+    total = sum(sum(g["durs"]) for g in got)
+    assert all(abs(g["sum"] - total) < 1e-6 for g in got)
+
+
+def test_shard_is_deterministic():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    a, da = bench.shard(0, 2)
+    b, db = bench.shard(0, 2)
+    assert list(da) == list(db)
+    assert all(np.array_equal(x, y) for x, y in zip(a, b))

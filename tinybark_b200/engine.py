@@ -24,10 +24,11 @@ MAX_DECODE_GROUPS = 8
 
 
 def decode_groups(lanes: int) -> int:
-    """Concurrent decoder groups for `lanes` clips: one group per 128 clips, at most 4.
-    A decoder step's GEMMs are too small to fill the GPU at a few hundred rows, so
-    independent groups on separate streams run side by side instead of one after another."""
-    return max(1, min(4, lanes // 128))
+    """Concurrent decoder groups for `lanes` clips. One: on a B200 the greedy loop's time
+    is set by the latency of its chain of small GEMMs, which splitting the lanes into
+    groups on separate streams does not shorten (512 lanes: 182 ms as 1 group, the same
+    as 2 or 4 groups, 50 % more as 8)."""
+    return 1
 
 
 def lane_order(idx: list[int], frames: list[int], groups: int | None = None) -> list[int]:
