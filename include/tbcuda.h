@@ -256,13 +256,17 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
  * One lane per clip, all lanes stepped together. enc [t3_total, 640] fp32 packed by
  * clip (enc_off [lanes+1]); cap [lanes] = 10 * subsampled(frames + 1, 3) - 1.
  * tokens: [lanes, max_cap] int32; counts: [lanes].
- * The lanes are split into `groups` (1..8) contiguous groups decoded concurrently, group
- * 0 on `stream` and the others on the library's own streams, joined back into `stream`
- * before return: group g holds ceil((lanes - g) / groups) lanes, so dealing clips
- * (longest first) round-robin into groups gives balanced groups. Within a group, lanes
- * ordered longest first let its GEMMs shrink as clips finish.
- * host_flag: pinned host memory, 2 ints per group, used to stop a group early once all
- * its lanes are done (may be NULL: then every group runs its longest cap). */
+ * groups = 0 (bf16): one persistent kernel runs the whole loop over all lanes, its
+ * phases separated by a grid-wide barrier; it stops once no lane runs. fp32, or
+ * groups = 1..8: the loop is replayed as CUDA graphs of 32 iterations, one GEMM kernel
+ * per step, with the lanes split into `groups` contiguous groups decoded concurrently,
+ * group 0 on `stream` and the others on the library's own streams, joined back into
+ * `stream` before return: group g holds ceil((lanes - g) / groups) lanes, so dealing
+ * clips (longest first) round-robin into groups gives balanced groups. host_flag
+ * (graph decoder only): pinned host memory, 2 ints per group, used to stop a group early
+ * once all its lanes are done (may be NULL: then every group runs its longest cap).
+ * Lanes ordered longest first let the GEMMs shrink to the lanes still running. Both
+ * decoders give the same tokens. */
 size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups);
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                   int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,

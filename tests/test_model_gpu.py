@@ -104,6 +104,34 @@ def test_decode_lanes_are_independent(groups):
         assert g == dec.greedy(fr, f)
 
 
+def test_decode_bf16_persistent_matches_graph_decoder():
+    """bf16, 300 lanes of seeded encoder frames with lengths 1..60 (three 128-row tiles,
+    lanes finishing at different iterations): the persistent decoder (one kernel, grid
+    barriers) and the graph-replayed one (one kernel per GEMM) compute the same GEMMs
+    and epilogues in the same order, so every lane's tokens are identical."""
+    from golden.make_golden import DECODE_CASES, decode_weights
+
+    sd = decode_weights(DECODE_CASES["mixed"])
+    eng = make_engine(2, "bf16", sd)
+    rng = np.random.default_rng(7)
+    t3 = rng.integers(1, 61, 300)
+    t3[:5] = 60  # longest first, as the engine orders a batch
+    t3 = np.sort(t3)[::-1]
+    feature_frames = [int(8 * t - 4) for t in t3]  # 8x subsampling: feature frames giving t3 frames
+    frames = [rng.standard_normal((int(t), 640)).astype(np.float32) for t in t3]
+    plan = eng.plan(feature_frames)
+    assert list(plan.t3) == list(t3)
+    enc = torch.from_numpy(np.concatenate(frames)).cuda()
+    results = []
+    for groups in (0, 1):
+        tokens, counts = eng.decode(enc, plan, groups=groups)
+        eng.check()
+        t, c = tokens.cpu().numpy(), counts.cpu().numpy()
+        results.append([t[i, : c[i]].tolist() for i in range(len(frames))])
+    assert sum(len(r) for r in results[0]) > 0
+    assert results[0] == results[1]
+
+
 def test_end_to_end_fp32_tokens_match_oracle():
     import tinybark_b200
     from oracle import decoder

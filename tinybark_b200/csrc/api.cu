@@ -275,7 +275,7 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
 }
 
 size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups) {
-  if (lanes <= 0) return 0;
+  if (lanes <= 0) return 0;  // groups <= 0: the persistent decoder's workspace, that of one group
   groups = groups < 1 ? 1 : (groups > 8 ? 8 : groups);
   return decode_ws_groups(dtype, lanes, groups < lanes ? groups : lanes);
 }

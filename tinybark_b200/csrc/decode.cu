@@ -20,62 +20,11 @@
 #include <thread>
 #include <vector>
 
-#include "epilogue.cuh"
-#include "host.h"
+#include "decode.cuh"
 
 namespace tb {
 
-constexpr int DECODE_CHUNK = 32;       // iterations per captured graph
-constexpr int DECODE_MAX_CHUNKS = 8192;  // so max_cap <= 262144
-constexpr int DECODE_MAX_GROUPS = 8;     // lane groups decoded concurrently
-
-struct DecodeWs {
-  unsigned long long *keys, *keys2;
-  void *z, *x0, *x1, *hp;
-  float *h, *c, *dec;
-  int *frame, *it, *done, *mask, *count, *active;
-  int* erow;     // [lanes]: encoder row the joint reads next (enc_off + frame), -1 once done
-  int* m_chunk;  // [DECODE_MAX_CHUNKS]: only lanes below this index can run in chunk c
-  int* m_cur;    // [0]: the current chunk's bound, [1]: the current chunk
-};
-
-static DecodeWs carve(void* ws, int dtype, int lanes) {
-  const size_t e = dsize(dtype), L = lanes;
-  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
-  DecodeWs w;
-  auto take = [&](size_t bytes) {
-    void* q = p;
-    p += align256(bytes);
-    return q;
-  };
-  w.keys = (unsigned long long*)take(L * 8);
-  w.keys2 = (unsigned long long*)take(L * 8);
-  w.z = take(L * TB_PRED * e);
-  w.x0 = take(L * 2 * TB_PRED * e);
-  w.x1 = take(L * 2 * TB_PRED * e);
-  w.hp = take(L * TB_PRED * e);
-  w.h = (float*)take(2 * L * TB_PRED * 4);
-  w.c = (float*)take(2 * L * TB_PRED * 4);
-  w.dec = (float*)take(L * TB_PRED * 4);
-  w.frame = (int*)take(L * 4);
-  w.it = (int*)take(L * 4);
-  w.done = (int*)take(L * 4);
-  w.mask = (int*)take(L * 4);
-  w.count = (int*)take(L * 4);
-  w.active = (int*)take(256);
-  w.erow = (int*)take(L * 4);
-  w.m_chunk = (int*)take(DECODE_MAX_CHUNKS * 4);
-  w.m_cur = (int*)take(256);
-  return w;
-}
-
-size_t decode_ws(int dtype, int lanes) {
-  uint8_t* base = nullptr;
-  DecodeWs w = carve(base, dtype, lanes);
-  return (size_t)(reinterpret_cast<uint8_t*>(w.m_cur) - base) + 256;
-}
-
-// Lane state initialisation and the inputs of the first step (token = blank, zero state).
+// Lane state initialisation and the inputs of the first step (token blank, zero state).
 template <typename T>
 __global__ void decode_init_kernel(DecodeWs w, const T* __restrict__ emb, const int* __restrict__ enc_off,
                                    const int* __restrict__ cap, int lanes) {
@@ -83,32 +32,7 @@ __global__ void decode_init_kernel(DecodeWs w, const T* __restrict__ emb, const 
   grid_dep_launch();
   const int l = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (l >= lanes) return;
-  const long long L = lanes;
-  for (int j = lane; j < TB_PRED; j += 32) {
-    w.h[l * TB_PRED + j] = 0.f;
-    w.h[(L + l) * TB_PRED + j] = 0.f;
-    w.c[l * TB_PRED + j] = 0.f;
-    w.c[(L + l) * TB_PRED + j] = 0.f;
-  }
-  T* x0 = reinterpret_cast<T*>(w.x0) + (long long)l * 2 * TB_PRED;
-  T* x1 = reinterpret_cast<T*>(w.x1) + (long long)l * 2 * TB_PRED;
-  for (int j = lane; j < TB_PRED; j += 32) {
-    x0[j] = emb[(long long)TB_BLANK * TB_PRED + j];
-    x0[TB_PRED + j] = from_f<T>(0.f);
-    x1[TB_PRED + j] = from_f<T>(0.f);
-  }
-  if (lane == 0) {
-    const int valid = enc_off[l + 1] - enc_off[l];
-    const int done = (valid <= 0 || cap[l] <= 0) ? 1 : 0;
-    w.frame[l] = 0;
-    w.it[l] = 0;
-    w.count[l] = 0;
-    w.done[l] = done;
-    w.mask[l] = 1;
-    w.keys[l] = 0ull;
-    w.keys2[l] = 0ull;
-    w.erow[l] = done ? -1 : enc_off[l];
-  }
+  lane_init<T>(w, emb, enc_off, cap, l, lanes, lane);
 }
 
 // The loop body for each lane, then the LSTM inputs of lanes that step.
@@ -119,67 +43,7 @@ __global__ void decode_step_kernel(DecodeWs w, const T* __restrict__ emb, const 
   grid_dep_launch();
   const int l = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (l >= lanes || l >= w.m_cur[0]) return;  // lanes past the bound finished before this chunk
-  int step = 0, tok = 0;
-  if (lane == 0) {
-    if (!w.done[l]) {
-      tok = argmax_index(w.keys[l]);
-      int d = argmax_index(w.keys2[l]);  // durations are 0, 1, 2, 3, 4
-      w.keys[l] = 0ull;  // cleared for the next joint
-      w.keys2[l] = 0ull;
-      // The joint always sets both keys; an index out of range can only come from a
-      // key the joint never wrote, and is read as a blank of duration 1.
-      if (tok < 0 || tok >= TB_VOCAB) tok = TB_BLANK;
-      if (d < 0 || d >= TB_DURATIONS) d = 1;
-      const int valid = enc_off[l + 1] - enc_off[l];
-      int frame = w.frame[l], it = w.it[l] + 1, done = 0;
-      if (tok == TB_BLANK) {
-        frame += d > 1 ? d : 1;
-      } else {
-        const int n = w.count[l];
-        if (n < max_cap) tokens[(long long)l * max_cap + n] = tok;
-        w.count[l] = n + 1;
-        if (tok == TB_EOS) {
-          done = 1;
-        } else {
-          step = 1;
-          frame += d;
-        }
-      }
-      if (it >= cap[l] || frame >= valid) done = 1;
-      if (done) step = 0;
-      w.frame[l] = frame;
-      w.it[l] = it;
-      w.done[l] = done;
-      w.erow[l] = done ? -1 : enc_off[l] + frame;
-      if (!done) atomicAdd(w.active, 1);
-    }
-    w.mask[l] = step;
-  }
-  step = __shfl_sync(0xffffffffu, step, 0);
-  tok = __shfl_sync(0xffffffffu, tok, 0);
-  if (!step) return;
-  const long long L = lanes;
-  T* __restrict__ x0 = reinterpret_cast<T*>(w.x0) + (long long)l * 2 * TB_PRED;
-  T* __restrict__ x1 = reinterpret_cast<T*>(w.x1) + (long long)l * 2 * TB_PRED;
-  const T* __restrict__ er = emb + (long long)tok * TB_PRED;
-  const float* __restrict__ h0 = w.h + (long long)l * TB_PRED;
-  const float* __restrict__ h1 = w.h + (L + l) * TB_PRED;
-  // 640 = 5 x 32 lanes x 4 values; all loads first, then the stores.
-  float4 e4[5], a4[5], b4[5];
-#pragma unroll
-  for (int i = 0; i < 5; ++i) {
-    const int j = (i * 32 + lane) * 4;
-    e4[i] = load4(er + j);
-    a4[i] = load4(h0 + j);
-    b4[i] = load4(h1 + j);
-  }
-#pragma unroll
-  for (int i = 0; i < 5; ++i) {
-    const int j = (i * 32 + lane) * 4;
-    store4(x0 + j, e4[i].x, e4[i].y, e4[i].z, e4[i].w);
-    store4(x0 + TB_PRED + j, a4[i].x, a4[i].y, a4[i].z, a4[i].w);
-    store4(x1 + TB_PRED + j, b4[i].x, b4[i].y, b4[i].z, b4[i].w);
-  }
+  if (lane_step<T>(w, emb, enc_off, cap, l, lanes, max_cap, tokens, lane) && lane == 0) atomicAdd(w.active, 1);
 }
 
 // Ends a chunk of iterations: publishes (lanes still running, summed over the chunk's
@@ -326,7 +190,6 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
     l0.out_dtype = dt;
     l0.bias = m.lstm_b[0];
     l0.c = w.c;
-    l0.h = w.h;
     l0.mask = w.mask;
     l0.rows = w.m_cur;
     l0.out = w.x1;  // h0 -> first half of layer 1's input
@@ -334,7 +197,6 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
     tb_epilogue l1 = l0;
     l1.bias = m.lstm_b[1];
     l1.c = w.c + (long long)L * TB_PRED;
-    l1.h = w.h + (long long)L * TB_PRED;
     l1.out = w.hp;  // h1 -> the projector's input
     l1.ldo = TB_PRED;
     tb_epilogue pj = {};  // dec, and the next joint input z = relu(enc[frame] + dec)
@@ -451,11 +313,16 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
   return rc;
 }
 
+int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
+                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* err, cudaStream_t stream);
+
 int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
                cudaStream_t stream) {
   if (lanes <= 0) return TB_OK;
   if (!enc || !enc_off || !cap || !tokens || !counts || !ws || max_cap <= 0) return TB_ERR_ARG;
+  if (groups <= 0 && m.dtype == TB_BF16)
+    return tdt_decode_tc(m, enc, enc_off, cap, lanes, max_cap, tokens, counts, ws, ws_bytes, err, stream);
   groups = std::max(1, std::min(std::min(groups, DECODE_MAX_GROUPS), lanes));
   if (ws_bytes < decode_ws_groups(m.dtype, lanes, groups)) return TB_ERR_WORKSPACE;
   if (m.dtype == TB_BF16)

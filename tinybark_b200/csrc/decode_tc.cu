@@ -1,0 +1,453 @@
+// TDT greedy decoding in bf16 as ONE persistent kernel: every SM runs one CTA for the
+// whole loop, and the phases of an iteration are separated by a grid-wide barrier
+// instead of kernel launches. Replaces the prediction network, joint and greedy loop
+// of tinybark/tinygrad/model.py:162-233 (one clip and one host round trip per token in
+// the reference) for a batch of clips, one lane per clip, all lanes stepped together.
+//
+// Phases (q counts them from 0; every CTA takes part in every phase):
+//   q = 0             INIT   lane state, the first step's inputs (token blank)
+//   q = 1, 2, 3       LSTM0, LSTM1, PROJ of the first prediction step
+//   q = 4 + 5i + r    iteration i: r = 0 JOINT, 1 STEP, 2 LSTM0, 3 LSTM1, 4 PROJ
+// JOINT   z [lanes x 640] . joint_w^T [8448 x 640] -> per-lane argmax keys (BN = 256)
+// STEP    the loop body per lane (lane_step): token, duration, frame, stop; the LSTM
+//         inputs of lanes that emitted a token
+// LSTM0/1 [emb | h] . W^T [2560 x 1280] with the LSTM cell in the epilogue (BN = 128)
+// PROJ    h1 . dec_proj^T [640 x 640] -> dec, and z = relu(enc[frame] + dec) (BN = 64)
+// The GEMM phases use the tcgen05 pipeline of the GEMM kernel (gemm.cu): warp 0 loads
+// A and W tiles with TMA into a 4-stage ring, warp 1 issues the MMAs into one of two
+// tensor-memory accumulators, warps 2-5 run the epilogue (tcgemm.cuh) and the
+// INIT/STEP work. Tile t of a phase goes to CTA t mod gridDim.
+//
+// Each iteration only covers lanes below the row bound M_i = 1 + the last lane still
+// running after STEP i (lanes are ordered longest first, so M shrinks as clips end);
+// the loop ends when no lane runs. The barrier is a global arrival counter: after a
+// phase every CTA adds 1, and phase q starts once the counter reaches q * gridDim.
+// Every wait is bounded (TB_WAIT_NS): a CTA that gives up sets TB_DEV_DECODE_TIMEOUT in
+// the error word and a global abort flag, and every CTA then leaves the loop.
+#include <algorithm>
+
+#include "decode.cuh"
+#include "tcgemm.cuh"
+
+namespace tb {
+
+namespace {
+
+constexpr int DT_A_BYTES = 128 * 64 * 2;
+constexpr int DT_RING_BYTES = 4 * (DT_A_BYTES + 256 * 64 * 2);  // 4 stages of the widest (joint) tiles
+constexpr int DT_OUT_BYTES = 4 * 32 * TC_OUT_STRIDE * 4;
+constexpr int DT_SMEM = 1024 + DT_RING_BYTES + DT_OUT_BYTES + 256;
+constexpr int DT_ACC_COLS = 256;  // tensor-memory columns per accumulator
+
+enum { G_JOINT = 0, G_LSTM0 = 1, G_LSTM1 = 2, G_PROJ = 3 };
+enum { P_INIT = 0, P_STEP = 1, P_GEMM = 2 };
+
+struct DecodeTcArgs {
+  CUtensorMap a[4], w[4];  // A operand and weights of the joint, LSTM0, LSTM1 and projector
+  tb_epilogue e[4];
+  DecodeWs ws;
+  const __nv_bfloat16* emb;
+  const int* enc_off;
+  const int* cap;
+  int lanes, max_cap, max_iters;
+  int* tokens;
+  int* err;
+};
+
+__host__ __device__ constexpr int gemm_n(int g) { return g == G_JOINT ? TB_JOINT_ROWS : (g == G_PROJ ? TB_PRED : 4 * TB_PRED); }
+__host__ __device__ constexpr int gemm_k(int g) { return g == G_JOINT || g == G_PROJ ? TB_PRED : 2 * TB_PRED; }
+__host__ __device__ constexpr int gemm_bn(int g) { return g == G_JOINT ? 256 : (g == G_PROJ ? 64 : 128); }
+// The shared-memory ring is re-cut at every GEMM phase into as many stages of that
+// phase's tile size as fit (4 x 48 KB joint, 6 x 32 KB LSTM, 8 x 24 KB projector): the
+// narrower the tiles, the deeper the pipeline. A phase starts only when every copy and
+// MMA of the previous one has completed, so the re-cut never overlaps a stage in use.
+__host__ __device__ constexpr int stage_bytes(int g) { return DT_A_BYTES + gemm_bn(g) * 64 * 2; }
+__host__ __device__ constexpr int ring_slots(int g) {
+  return DT_RING_BYTES / stage_bytes(g) < 8 ? DT_RING_BYTES / stage_bytes(g) : 8;
+}
+
+struct Phase {
+  int kind;  // P_INIT, P_STEP or P_GEMM
+  int gemm;  // G_* for P_GEMM
+  int iter;  // greedy-loop iteration (-1 for the first prediction step)
+};
+
+__device__ __forceinline__ Phase phase_of(int q) {
+  if (q == 0) return {P_INIT, 0, -1};
+  if (q < 4) return {P_GEMM, q, -1};  // LSTM0, LSTM1, PROJ
+  const int i = (q - 4) / 5, r = (q - 4) % 5;
+  if (r == 0) return {P_GEMM, G_JOINT, i};
+  if (r == 1) return {P_STEP, 0, i};
+  return {P_GEMM, r - 1, i};
+}
+
+// Rows a phase covers: JOINT and STEP of iteration i read M_{i-1}, the rest M_i. Each
+// bound is written during one STEP phase and read only after its barrier, so every
+// role of every CTA reads the same value, however late it reads it.
+__device__ __forceinline__ int phase_rows(const Phase& p, const int* bounds) {
+  if (p.kind == P_INIT) return 0;
+  const int i = (p.kind == P_STEP || p.gemm == G_JOINT) ? p.iter - 1 : p.iter;
+  return bounds[i + 1];
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Waits until `count` phase arrivals are in (every CTA finished the phases before).
+// False if the decoder gave up: abort set by another CTA, or this wait timed out.
+__device__ bool grid_wait(unsigned* sync, unsigned count, int* err, volatile int* abort) {
+  const uint64_t start = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire(sync) >= count) {
+      fence_proxy_async_global();  // TMA reads issued after this see the phase's writes
+      return true;
+    }
+    if ((i & 15) == 15) {
+      if (*abort || reinterpret_cast<volatile unsigned*>(sync)[1]) {
+        *abort = 1;
+        return false;
+      }
+      if (globaltimer() - start > TB_WAIT_NS) {
+        atomicOr(err, TB_DEV_DECODE_TIMEOUT);
+        atomicExch(sync + 1, 1u);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// The CTA's view of the grid barrier: the producer thread is the only one that polls
+// global memory; it publishes each phase it has seen here, and the MMA thread and the
+// epilogue warps wait on that (release/acquire at CTA scope, after the producer's
+// acquire at GPU scope, so the phase's writes are visible to them too).
+__device__ __forceinline__ void post_phase(unsigned* slot, unsigned q) {
+  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(q) : "memory");
+}
+__device__ bool cta_phase_wait(unsigned* slot, unsigned q, int* err, volatile int* abort, unsigned* sync) {
+  const uint64_t start = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    unsigned v;
+    asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(slot)) : "memory");
+    if (v >= q) return true;
+    if ((i & 15) == 15) {
+      if (*abort) return false;
+      if (globaltimer() - start > TB_WAIT_NS) {
+        atomicOr(err, TB_DEV_DECODE_TIMEOUT);
+        atomicExch(sync + 1, 1u);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Named barrier of the four epilogue warps (128 threads) with an OR of `pred`.
+__device__ __forceinline__ bool epi_bar_or(bool pred) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n barrier.red.or.pred q, 1, 128, p;\n selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((int)pred)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ int tiles_of(int g, int rows) { return ((rows + 127) / 128) * (gemm_n(g) / gemm_bn(g)); }
+
+}  // namespace
+
+__global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant__ DecodeTcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* out_stage = reinterpret_cast<float*>(smem + DT_RING_BYTES);
+  TcBars* bars = reinterpret_cast<TcBars*>(smem + DT_RING_BYTES + DT_OUT_BYTES);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DecodeWs& w = args.ws;
+  int* bounds = w.bounds;
+  unsigned* sync = reinterpret_cast<unsigned*>(w.m_cur + 8);
+  const unsigned G = gridDim.x;
+  int* err = args.err;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 8; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->tfull[a], 1);
+      mbar_init(&bars->tempty[a], 4);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort = 0;
+    bars->phase = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem, 2 * DT_ACC_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+  // Phases run while q < q_end; the last iteration ends after its STEP.
+  const int q_end = 4 + 5 * args.max_iters;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int g = 0; g < 4; ++g) {
+        prefetch_tmap(&args.a[g]);
+        prefetch_tmap(&args.w[g]);
+      }
+      uint32_t use = 0, used = 0;  // per ring slot: parity of its next use; slots ever used
+      bool ok = true;
+      for (int q = 1; q < q_end && ok; ++q) {
+        const Phase p = phase_of(q);
+        if (!grid_wait(sync, (unsigned)q * G, err, abort)) break;
+        post_phase(&bars->phase, (unsigned)q);
+        const int rows = phase_rows(p, bounds);
+        if (rows <= 0) break;  // no lane runs: the loop is over
+        if (p.kind != P_GEMM) continue;
+        const int g = p.gemm, bn = gemm_bn(g), nt_count = gemm_n(g) / bn, kb_count = gemm_k(g) / 64;
+        const int sb = stage_bytes(g), slots = ring_slots(g), tiles = tiles_of(g, rows);
+        int s = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += G) {
+          const int mt = t / nt_count, nt = t % nt_count;
+          for (int kb = 0; kb < kb_count; ++kb) {
+            if (!mbar_wait(&bars->empty[s], ((use >> s) & 1) ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
+              ok = false;
+              break;
+            }
+            uint8_t* sa = smem + s * sb;
+            mbar_expect_tx(&bars->full[s], sb);
+            tma_load_2d(sa, &args.a[g], &bars->full[s], kb * 64, mt * 128);
+            tma_load_2d(sa + DT_A_BYTES, &args.w[g], &bars->full[s], kb * 64, nt * bn);
+            use ^= 1u << s;
+            used |= 1u << s;
+            if (++s == slots) s = 0;
+          }
+        }
+      }
+      // Let the copies in flight land before the CTA exits (all of them have landed
+      // unless the loop was abandoned).
+      for (int s = 0; s < 8; ++s)
+        if ((used >> s) & 1) drain_wait(&bars->full[s], ((use >> s) & 1) ^ 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int acc = 0;
+      uint32_t use = 0, acc_ph = 0;  // per ring slot: parity of its next use
+      bool ok = true;
+      for (int q = 1; q < q_end && ok; ++q) {
+        const Phase p = phase_of(q);
+        if (!cta_phase_wait(&bars->phase, (unsigned)q, err, abort, sync)) break;
+        const int rows = phase_rows(p, bounds);
+        if (rows <= 0) break;
+        if (p.kind != P_GEMM) continue;
+        const int g = p.gemm, kb_count = gemm_k(g) / 64, sb = stage_bytes(g), slots = ring_slots(g);
+        const uint32_t idesc = g == G_JOINT ? idesc_bf16(128, 256) : (g == G_PROJ ? idesc_bf16(128, 64) : idesc_bf16(128, 128));
+        const int tiles = tiles_of(g, rows);
+        int s = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += G) {
+          if (!mbar_wait(&bars->tempty[acc], acc_ph ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + acc * DT_ACC_COLS;
+          for (int kb = 0; kb < kb_count; ++kb) {
+            if (!mbar_wait(&bars->full[s], (use >> s) & 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * sb);
+            const uint64_t ad = sdesc_sw128(sa), bd = sdesc_sw128(sa + DT_A_BYTES);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            umma_commit(&bars->empty[s]);
+            use ^= 1u << s;
+            if (++s == slots) s = 0;
+          }
+          if (!ok) break;
+          umma_commit(&bars->tfull[acc]);
+          if (++acc == 2) acc = 0, acc_ph ^= 1;
+        }
+      }
+      if (!ok) *abort = 1;
+      // Every MMA issued has completed once this commit arrives.
+      umma_commit(&bars->done);
+      drain_wait(&bars->done, 0);
+    }
+  } else {
+    const int ew = warp - 2;   // epilogue warp 0..3
+    const int quarter = warp & 3;  // tensor-memory lane quarter this warp may access
+    float* stage = out_stage + quarter * 32 * TC_OUT_STRIDE;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int q = 0; q < q_end; ++q) {
+      const Phase p = phase_of(q);
+      bool ok = true;
+      int rows = args.lanes;
+      if (q > 0) {
+        if (ew == 0 && lane == 0) ok = cta_phase_wait(&bars->phase, (unsigned)q, err, abort, sync);
+        if (epi_bar_or(!ok || *abort)) break;
+        rows = phase_rows(p, bounds);
+        if (rows <= 0) break;
+      }
+      if (p.kind == P_INIT) {
+        for (int l = blockIdx.x * 4 + ew; l < args.lanes; l += G * 4)
+          lane_init<__nv_bfloat16>(w, args.emb, args.enc_off, args.cap, l, args.lanes, lane);
+      } else if (p.kind == P_STEP) {
+        for (int l = blockIdx.x * 4 + ew; l < rows; l += G * 4)
+          if (lane_step<__nv_bfloat16>(w, args.emb, args.enc_off, args.cap, l, args.lanes, args.max_cap,
+                                       args.tokens, lane) &&
+              lane == 0)
+            atomicMax(bounds + p.iter + 1, l + 1);
+      } else {
+        const int g = p.gemm, tiles = tiles_of(g, rows), nt_count = gemm_n(g) / gemm_bn(g);
+        for (int t = blockIdx.x; t < tiles; t += G) {
+          const int row0 = (t / nt_count) * 128 + quarter * 32, n0 = (t % nt_count) * gemm_bn(g);
+          const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + acc * DT_ACC_COLS;
+          if (ok) {
+            // Constant indices: the epilogue's operands are then read straight from the
+            // kernel parameters, never through a pointer that the stores might alias.
+            if (g == G_JOINT)
+              ok = epilogue_tile<256, TB_EPI_ARGMAX>(args.e[G_JOINT], stage, taddr, row0, n0, lane, rows,
+                                                     &bars->tfull[acc], acc_ph, err, abort);
+            else if (g == G_PROJ)
+              ok = epilogue_tile<64, TB_EPI_JOINT_IN>(args.e[G_PROJ], stage, taddr, row0, n0, lane, rows,
+                                                      &bars->tfull[acc], acc_ph, err, abort);
+            else if (g == G_LSTM0)
+              ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM0], stage, taddr, row0, n0, lane, rows,
+                                                   &bars->tfull[acc], acc_ph, err, abort);
+            else
+              ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM1], stage, taddr, row0, n0, lane, rows,
+                                                   &bars->tfull[acc], acc_ph, err, abort);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (ok && lane == 0) mbar_arrive(&bars->tempty[acc]);
+          if (++acc == 2) acc = 0, acc_ph ^= 1;
+        }
+      }
+      // The phase's writes, visible to the other CTAs' loads and TMA reads, then one
+      // arrival for this CTA.
+      fence_proxy_async_global();
+      __threadfence();
+      if (epi_bar_or(!ok)) {
+        *abort = 1;
+        break;
+      }
+      if (ew == 0 && lane == 0) {
+        __threadfence();
+        atomicAdd(sync, 1u);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * DT_ACC_COLS);
+  }
+}
+
+int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
+                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* err, cudaStream_t stream) {
+  if (lanes <= 0) return TB_OK;
+  if (m.dtype != TB_BF16) return TB_ERR_ARG;
+  if (!enc || !enc_off || !cap || !tokens || !counts || !ws || max_cap <= 0) return TB_ERR_ARG;
+  if (ws_bytes < decode_ws(TB_BF16, lanes)) return TB_ERR_WORKSPACE;
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail_cuda();
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DT_SMEM) != cudaSuccess)
+      return fail_cuda();
+    configured[dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_tc_kernel, 192, DT_SMEM) != cudaSuccess)
+    return fail_cuda();
+  if (per_sm < 1) return TB_ERR_UNSUPPORTED;
+  const int grid = sm_count();
+
+  DecodeTcArgs args = {};
+  DecodeWs& w = args.ws;
+  w = carve(ws, TB_BF16, lanes);
+  // A operands [lanes x K] and weights [N x K], 64-column boxes of 128 rows (A) or BN rows (W).
+  const void* a_ptr[4] = {w.z, w.x0, w.x1, w.hp};
+  const void* w_ptr[4] = {m.joint_w, m.lstm_w[0], m.lstm_w[1], m.dec_proj_w};
+  for (int g = 0; g < 4; ++g) {
+    if (!encode_tmap_2d(&args.a[g], a_ptr[g], lanes, gemm_k(g), gemm_k(g), 64, 128) ||
+        !encode_tmap_2d(&args.w[g], w_ptr[g], gemm_n(g), gemm_k(g), gemm_k(g), 64, gemm_bn(g)))
+      return TB_ERR_CUDA;
+  }
+  tb_epilogue& jt = args.e[G_JOINT];
+  jt.kind = TB_EPI_ARGMAX;
+  jt.bias = m.joint_b;
+  jt.keys = w.keys;
+  jt.keys2 = w.keys2;
+  jt.split = TB_TOKEN_ROWS;
+  jt.split_end = TB_TOKEN_ROWS + TB_DURATIONS;
+  for (int layer = 0; layer < 2; ++layer) {
+    tb_epilogue& e = args.e[G_LSTM0 + layer];
+    e.kind = TB_EPI_LSTM;
+    e.out_dtype = TB_BF16;
+    e.bias = m.lstm_b[layer];
+    e.c = w.c + (long long)layer * lanes * TB_PRED;
+    e.mask = w.mask;
+    e.out = layer == 0 ? w.x1 : w.hp;  // h0 -> first half of layer 1's input; h1 -> the projector's input
+    e.ldo = layer == 0 ? 2 * TB_PRED : TB_PRED;
+  }
+  tb_epilogue& pj = args.e[G_PROJ];
+  pj.kind = TB_EPI_JOINT_IN;
+  pj.out_dtype = TB_BF16;
+  pj.out = w.dec;
+  pj.ldo = TB_PRED;
+  pj.out2 = w.z;
+  pj.ldo2 = TB_PRED;
+  pj.bias = m.dec_proj_b;
+  pj.gather = enc;
+  pj.gather_row = w.erow;
+  args.emb = reinterpret_cast<const __nv_bfloat16*>(m.embedding);
+  args.enc_off = enc_off;
+  args.cap = cap;
+  args.lanes = lanes;
+  args.max_cap = max_cap;
+  args.max_iters = max_cap;  // every lane stops after at most cap <= max_cap iterations
+  if (max_cap > DECODE_MAX_ITERS) return TB_ERR_ARG;
+  args.tokens = tokens;
+  args.err = err;
+
+  // Row bounds: [0] = every lane, the rest zero until their iteration; barrier counter
+  // and abort flag zero.
+  if (cudaMemsetAsync(tokens, 0xff, (size_t)lanes * max_cap * sizeof(int), stream) != cudaSuccess ||
+      cudaMemsetAsync(w.bounds, 0, (size_t)(max_cap + 1) * sizeof(int), stream) != cudaSuccess ||
+      cudaMemsetAsync(w.m_cur, 0, 256, stream) != cudaSuccess ||
+      cudaMemcpyAsync(w.bounds, &lanes, sizeof(int), cudaMemcpyHostToDevice, stream) != cudaSuccess)
+    return fail_cuda();
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = DT_SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, decode_tc_kernel, args);
+  if (int rc = check_launch()) return rc;
+  if (cudaMemcpyAsync(counts, w.count, (size_t)lanes * sizeof(int), cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+    return fail_cuda();
+  return TB_OK;
+}
+
+}  // namespace tb

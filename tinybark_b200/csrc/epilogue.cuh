@@ -87,7 +87,7 @@ __device__ __forceinline__ void epi_group(const tb_epilogue& e, int m, int n, fl
       float c = fg * *cp + ig * gg;
       float h = og * tanhf(c);
       *cp = c;
-      e.h[(long long)m * TB_PRED + u] = h;
+      if (e.h) e.h[(long long)m * TB_PRED + u] = h;
       if (e.out) store1_dt(e.out, (long long)m * e.ldo + u, e.out_dtype, h);
       if (e.out2) store1_dt(e.out2, (long long)m * e.ldo2 + u, e.out_dtype, h);
       break;

@@ -13,8 +13,8 @@
 // over more SMs.
 // fp32: a CUDA-core kernel, 128 x 128 tiles, 8 x 8 outputs per thread, for the fp32
 // parity path.
-#include "epilogue.cuh"
 #include "host.h"
+#include "tcgemm.cuh"
 
 namespace tb {
 
@@ -29,258 +29,11 @@ struct TcCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int OUT_STRIDE = 36;  // floats per staged row: 16-byte aligned, conflict-free
+  static constexpr int OUT_STRIDE = TC_OUT_STRIDE;
   static constexpr int OUT_BYTES = 4 * 32 * OUT_STRIDE * 4;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES;
 };
-
-struct TcBars {
-  uint64_t full[8], empty[8], tfull[2], tempty[2], done;
-  uint32_t tmem;
-  int abort;
-};
-
-// Bounded wait used while winding down: ignores the abort flag.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-  uint64_t start = globaltimer();
-  while (!mbar_try_wait(bar, parity))
-    if (globaltimer() - start > TB_WAIT_NS) break;
-}
-
-// One lane waits, the warp follows.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, TB_DEV_GEMM_TIMEOUT, abort);
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
-__device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-// The PTX tanh.approx.f32 instruction (one MUFU operation, about 2^-11 relative error).
-// Used in the bf16 decoder's LSTM cell, whose inputs and outputs are bf16 (2^-8).
-__device__ __forceinline__ float tanh_mufu(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float sigmoid_mufu(float x) { return fmaf(0.5f, tanh_mufu(0.5f * x), 0.5f); }
-
-// Global values an epilogue reads, loaded by each epilogue warp for its 32 rows of a
-// tile before it waits for the tile's accumulator, so their latency hides behind the
-// main loop instead of adding to the epilogue. This matters for the decoder's GEMMs,
-// which run one tile per CTA: there nothing else overlaps the epilogue. Lane layout as
-// in epi_chunk: rows row0 + 4*it + lane/8, columns n0 + 32*ci + 4*(lane%8) .. +3.
-template <int EPI, int BN>
-struct EpiPre {
-  __device__ __forceinline__ void load(const tb_epilogue&, int, int, int, int) {}
-};
-
-template <int BN>
-struct EpiPre<TB_EPI_LSTM, BN> {
-  static constexpr int CH = BN / 32;
-  float cp[CH][8];  // previous cell state of unit n/4
-  float4 b[CH];
-  unsigned step;    // bit it: row 4*it + lane/8 is updated
-  __device__ __forceinline__ void load(const tb_epilogue& e, int row0, int n0, int lane, int M) {
-    const int sub = lane >> 3, col = (lane & 7) * 4;
-    step = 0;
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m < M && (!e.mask || e.mask[m] != 0)) step |= 1u << it;
-    }
-#pragma unroll
-    for (int ci = 0; ci < CH; ++ci) {
-      const int n = n0 + ci * 32 + col;
-      b[ci] = load4(e.bias + n);
-#pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int m = row0 + it * 4 + sub;
-        cp[ci][it] = m < M ? e.c[(long long)m * TB_PRED + (n >> 2)] : 0.f;
-      }
-    }
-  }
-};
-
-template <int BN>
-struct EpiPre<TB_EPI_JOINT_IN, BN> {
-  static constexpr int CH = BN / 32, PX = CH < 2 ? CH : 2;  // gathered values of the first PX chunks
-  int g[8];
-  float4 b[CH];
-  float4 x[PX][8];
-  __device__ __forceinline__ void load(const tb_epilogue& e, int row0, int n0, int lane, int M) {
-    const int sub = lane >> 3, col = (lane & 7) * 4;
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      g[it] = m < M ? e.gather_row[m] : -1;
-    }
-#pragma unroll
-    for (int ci = 0; ci < CH; ++ci) b[ci] = load4(e.bias + n0 + ci * 32 + col);
-#pragma unroll
-    for (int ci = 0; ci < PX; ++ci)
-#pragma unroll
-      for (int it = 0; it < 8; ++it)
-        x[ci][it] = g[it] >= 0 ? load4(e.gather + (long long)g[it] * e.ldo + n0 + ci * 32 + col)
-                               : make_float4(0, 0, 0, 0);
-  }
-};
-
-// The epilogue of one warp's 32 x 32 chunk ci of a tile, staged row-major (stride
-// OUT_STRIDE) in `stage`: lane reads rows 4*it + lane/8 (it = 0..7), columns
-// 4*(lane%8) .. +3. row0: global row of the chunk's first row; n0: global column of its
-// first column.
-template <int EPI, int BN>
-__device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* stage, int row0, int n0, int lane, int M,
-                                          const EpiPre<EPI, BN>& pre, int ci) {
-  constexpr int S = 36;
-  const int sub = lane >> 3, col = (lane & 7) * 4, n = n0 + col;
-  float4 v[8];
-#pragma unroll
-  for (int it = 0; it < 8; ++it) v[it] = *reinterpret_cast<const float4*>(stage + (it * 4 + sub) * S + col);
-  if constexpr (EPI == TB_EPI_RESIDUAL) {
-    float* out = reinterpret_cast<float*>(e.out);
-    float4 x[8];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      x[it] = m < M ? load4(out + (long long)m * e.ldo + n) : make_float4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m < M)
-        store4(out + (long long)m * e.ldo + n, x[it].x + e.alpha * v[it].x, x[it].y + e.alpha * v[it].y,
-               x[it].z + e.alpha * v[it].z, x[it].w + e.alpha * v[it].w);
-    }
-  } else if constexpr (EPI == TB_EPI_STORE || EPI == TB_EPI_BIAS_RELU) {
-    const float4 b = e.bias ? load4(e.bias + n) : make_float4(0, 0, 0, 0);
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m >= M) continue;
-      float a0 = v[it].x + b.x, a1 = v[it].y + b.y, a2 = v[it].z + b.z, a3 = v[it].w + b.w;
-      if constexpr (EPI == TB_EPI_BIAS_RELU) a0 = fmaxf(a0, 0.f), a1 = fmaxf(a1, 0.f), a2 = fmaxf(a2, 0.f), a3 = fmaxf(a3, 0.f);
-      store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, a0, a1, a2, a3);
-    }
-  } else if constexpr (EPI == TB_EPI_SILU) {
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m < M)
-        store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, fast_silu(v[it].x), fast_silu(v[it].y),
-                  fast_silu(v[it].z), fast_silu(v[it].w));
-    }
-  } else if constexpr (EPI == TB_EPI_GLU) {
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m < M)
-        store2_dt(e.out, (long long)m * e.ldo + (n >> 1), e.out_dtype, v[it].x * fast_sigmoid(v[it].y),
-                  v[it].z * fast_sigmoid(v[it].w));
-    }
-  } else if constexpr (EPI == TB_EPI_QKV) {
-    const int sec = n >> 10, c = n & 1023;
-    void* dst = sec == 0 ? e.out : (sec == 1 ? e.out3 : e.out4);
-    const float4 u = sec == 0 ? load4(e.bias_u + c) : make_float4(0, 0, 0, 0);
-    const float4 w = sec == 0 ? load4(e.bias_v + c) : make_float4(0, 0, 0, 0);
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m >= M) continue;
-      const long long off = (long long)m * e.ldo + c;
-      store4_dt(dst, off, e.out_dtype, v[it].x + u.x, v[it].y + u.y, v[it].z + u.z, v[it].w + u.w);
-      if (sec == 0 && e.out2)
-        store4_dt(e.out2, off, e.out_dtype, v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
-    }
-  } else if constexpr (EPI == TB_EPI_JOINT_IN) {
-    constexpr int PX = EpiPre<EPI, BN>::PX;
-    const float4 b = pre.b[ci];
-    float* out = reinterpret_cast<float*>(e.out);
-    float4 x[8];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      if (ci < PX)
-        x[it] = pre.x[ci < PX ? ci : 0][it];
-      else
-        x[it] = pre.g[it] >= 0 ? load4(e.gather + (long long)pre.g[it] * e.ldo + n) : make_float4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m >= M) continue;
-      const float d0 = v[it].x + b.x, d1 = v[it].y + b.y, d2 = v[it].z + b.z, d3 = v[it].w + b.w;
-      store4(out + (long long)m * e.ldo + n, d0, d1, d2, d3);
-      if (pre.g[it] >= 0)
-        store4_dt(e.out2, (long long)m * e.ldo2 + n, e.out_dtype, fmaxf(x[it].x + d0, 0.f), fmaxf(x[it].y + d1, 0.f),
-                  fmaxf(x[it].z + d2, 0.f), fmaxf(x[it].w + d3, 0.f));
-    }
-  } else if constexpr (EPI == TB_EPI_LSTM) {
-    // Columns n..n+3 are the gates i, f, g, o of unit n / 4.
-    const int u = n >> 2;
-    const float4 b = pre.b[ci];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      if (!((pre.step >> it) & 1u)) continue;
-      const int m = row0 + it * 4 + sub;
-      const float ig = sigmoid_mufu(v[it].x + b.x), fg = sigmoid_mufu(v[it].y + b.y);
-      const float gg = tanh_mufu(v[it].z + b.z), og = sigmoid_mufu(v[it].w + b.w);
-      const float c = fg * pre.cp[ci][it] + ig * gg;
-      const float h = og * tanh_mufu(c);
-      e.c[(long long)m * TB_PRED + u] = c;
-      e.h[(long long)m * TB_PRED + u] = h;
-      if (e.out) store1_dt(e.out, (long long)m * e.ldo + u, e.out_dtype, h);
-      if (e.out2) store1_dt(e.out2, (long long)m * e.ldo2 + u, e.out_dtype, h);
-    }
-  }
-}
-
-// The joint head's epilogue for one row (one lane) of a tile: the largest token logit
-// and the largest duration logit with their first column, merged into the row's keys.
-// `bias` holds the tile's BN bias values. Padding columns have bias -inf and never win.
-template <int BN>
-__device__ __forceinline__ void argmax_tile(const tb_epilogue& e, const float* bias, uint32_t taddr, int m, int n0,
-                                            int M) {
-  const float neg_inf = __int_as_float(0xff800000);
-  float best = neg_inf, dbest = neg_inf;
-  int bi = -1, di = -1;
-  const bool tokens_only = n0 + BN <= e.split;
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    tmem_ld32(taddr + c, r);
-    tmem_wait_ld();
-    if (tokens_only) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 b = *reinterpret_cast<const float4*>(bias + c + j);
-        const float x0 = __uint_as_float(r[j]) + b.x, x1 = __uint_as_float(r[j + 1]) + b.y;
-        const float x2 = __uint_as_float(r[j + 2]) + b.z, x3 = __uint_as_float(r[j + 3]) + b.w;
-        // Strictly greater, columns ascending: the first of equal values wins.
-        if (x0 > best) best = x0, bi = n0 + c + j;
-        if (x1 > best) best = x1, bi = n0 + c + j + 1;
-        if (x2 > best) best = x2, bi = n0 + c + j + 2;
-        if (x3 > best) best = x3, bi = n0 + c + j + 3;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = n0 + c + j;
-        const float x = __uint_as_float(r[j]) + bias[c + j];
-        if (n < e.split) {
-          if (x > best) best = x, bi = n;
-        } else if (n < e.split_end) {
-          if (x > dbest) dbest = x, di = n - e.split;
-        }
-      }
-    }
-  }
-  if (m < M) {
-    if (bi >= 0) atomicMax(e.keys + m, argmax_key(best, bi));
-    if (di >= 0) atomicMax(e.keys2 + m, argmax_key(dbest, di));
-  }
-}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
@@ -389,46 +142,9 @@ __global__ void __launch_bounds__(192, 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       const int mt = t / n_tiles, nt = t % n_tiles;
       const int row0 = mt * C::BM + q * 32, n0 = nt * BN;
-      if constexpr (EPI == TB_EPI_ARGMAX) {
-        // The tile's bias, loaded before the wait, then kept in the warp's staging rows.
-        float bias[BN / 32];
-#pragma unroll
-        for (int ci = 0; ci < BN / 32; ++ci) bias[ci] = e.bias[n0 + ci * 32 + lane];
-        if (!warp_wait(&bars->tfull[acc], acc_ph, err, abort)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int ci = 0; ci < BN / 32; ++ci) stage[ci * 32 + lane] = bias[ci];
-        __syncwarp();
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-        argmax_tile<BN>(e, stage, taddr, row0 + lane, n0, M);
-        __syncwarp();
-      } else {
-        EpiPre<EPI, BN> pre;
-        pre.load(e, row0, n0, lane, M);
-        if (!warp_wait(&bars->tfull[acc], acc_ph, err, abort)) break;
-        tc_fence_after();
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * BN;
-        auto chunk = [&](int ci) {
-          uint32_t r[32];
-          tmem_ld32(taddr + ci * 32, r);
-          tmem_wait_ld();
-          float4* srow = reinterpret_cast<float4*>(stage + lane * C::OUT_STRIDE);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            srow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          __syncwarp();
-          epi_chunk<EPI, BN>(e, stage, row0, n0 + ci * 32, lane, M, pre, ci);
-          __syncwarp();
-        };
-        if constexpr (EPI == TB_EPI_LSTM || EPI == TB_EPI_JOINT_IN) {
-#pragma unroll
-          for (int ci = 0; ci < BN / 32; ++ci) chunk(ci);  // prefetched values indexed by ci
-        } else {
-#pragma unroll 1
-          for (int ci = 0; ci < BN / 32; ++ci) chunk(ci);
-        }
-      }
+      if (!epilogue_tile<BN, EPI>(e, stage, tmem + ((uint32_t)(q * 32) << 16) + acc * BN, row0, n0, lane, M,
+                                  &bars->tfull[acc], acc_ph, err, abort))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[acc]);
@@ -595,7 +311,9 @@ static int launch_tc_kind(const void* a, long long lda, const void* w, int m, in
     case TB_EPI_GLU: return launch_tc<BN, TB_EPI_GLU>(a, lda, w, m, n, k, e, err, s);
     case TB_EPI_QKV: return launch_tc<BN, TB_EPI_QKV>(a, lda, w, m, n, k, e, err, s);
     case TB_EPI_ARGMAX: return launch_tc<BN, TB_EPI_ARGMAX>(a, lda, w, m, n, k, e, err, s);
-    case TB_EPI_LSTM: return launch_tc<BN, TB_EPI_LSTM>(a, lda, w, m, n, k, e, err, s);
+    case TB_EPI_LSTM:
+      if constexpr (BN <= 128) return launch_tc<BN, TB_EPI_LSTM>(a, lda, w, m, n, k, e, err, s);
+      return TB_ERR_UNSUPPORTED;
     case TB_EPI_JOINT_IN: return launch_tc<BN, TB_EPI_JOINT_IN>(a, lda, w, m, n, k, e, err, s);
     default: return TB_ERR_ARG;
   }
@@ -627,7 +345,9 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
   if (dtype == TB_BF16) {
     if (k % 64 || lda % 8 || (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
       return TB_ERR_UNSUPPORTED;
-    switch (pick_bn(m, n, k)) {
+    int bn = pick_bn(m, n, k);
+    if (e.kind == TB_EPI_LSTM && bn > 128) bn = n % 128 ? 64 : 128;  // the cell epilogue covers <= 32 units
+    switch (bn) {
       case 256: return launch_tc_kind<256>(a, lda, w, m, n, k, e, err, stream);
       case 128: return launch_tc_kind<128>(a, lda, w, m, n, k, e, err, stream);
       case 64: return launch_tc_kind<64>(a, lda, w, m, n, k, e, err, stream);

@@ -1,0 +1,403 @@
+// Device-side pieces of the tcgen05 GEMM shared by the GEMM kernel (gemm.cu) and the
+// persistent decoder (decode_tc.cu): shared-memory barriers, bounded waits and the
+// fused epilogues that drain one 128-row accumulator tile from tensor memory.
+#pragma once
+#include "epilogue.cuh"
+
+namespace tb {
+
+constexpr int TC_OUT_STRIDE = 36;  // floats per staged row: 16-byte aligned, conflict-free
+
+struct TcBars {
+  uint64_t full[8], empty[8], tfull[2], tempty[2], done;
+  uint32_t tmem;
+  int abort;
+  unsigned phase;  // persistent decoder: last phase whose grid barrier this CTA has seen
+};
+
+// Bounded wait used while winding down: ignores the abort flag.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - start > TB_WAIT_NS) break;
+}
+
+// One lane waits, the warp follows.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, TB_DEV_GEMM_TIMEOUT, abort);
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// The PTX tanh.approx.f32 instruction (one MUFU operation, about 2^-11 relative error).
+// Used in the bf16 decoder's LSTM cell, whose inputs and outputs are bf16 (2^-8).
+__device__ __forceinline__ float tanh_mufu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sigmoid_mufu(float x) { return fmaf(0.5f, tanh_mufu(0.5f * x), 0.5f); }
+
+// Global values an epilogue reads, loaded by each epilogue warp for its 32 rows of a
+// tile before it waits for the tile's accumulator, so their latency hides behind the
+// main loop instead of adding to the epilogue. This matters for the decoder's GEMMs,
+// which run one tile per CTA: there nothing else overlaps the epilogue. Lane layout as
+// in epi_chunk: rows row0 + 4*it + lane/8, columns n0 + 32*ci + 4*(lane%8) .. +3.
+template <int EPI, int BN>
+struct EpiPre {
+  __device__ __forceinline__ void load(const tb_epilogue&, int, int, int, int) {}
+};
+
+template <int BN>
+struct EpiPre<TB_EPI_JOINT_IN, BN> {
+  static constexpr int CH = BN / 32, PX = CH < 2 ? CH : 2;  // gathered values of the first PX chunks
+  int g[8];
+  float4 b[CH];
+  float4 x[PX][8];
+  __device__ __forceinline__ void load(const tb_epilogue& e, int row0, int n0, int lane, int M) {
+    const int sub = lane >> 3, col = (lane & 7) * 4;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      g[it] = m < M ? e.gather_row[m] : -1;
+    }
+#pragma unroll
+    for (int ci = 0; ci < CH; ++ci) b[ci] = load4(e.bias + n0 + ci * 32 + col);
+#pragma unroll
+    for (int ci = 0; ci < PX; ++ci)
+#pragma unroll
+      for (int it = 0; it < 8; ++it)
+        x[ci][it] = g[it] >= 0 ? load4(e.gather + (long long)g[it] * e.ldo + n0 + ci * 32 + col)
+                               : make_float4(0, 0, 0, 0);
+  }
+};
+
+// The epilogue of one warp's 32 x 32 chunk ci of a tile, staged row-major (stride
+// OUT_STRIDE) in `stage`: lane reads rows 4*it + lane/8 (it = 0..7), columns
+// 4*(lane%8) .. +3. row0: global row of the chunk's first row; n0: global column of its
+// first column.
+template <int EPI, int BN>
+__device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* stage, int row0, int n0, int lane, int M,
+                                          const EpiPre<EPI, BN>& pre, int ci) {
+  constexpr int S = TC_OUT_STRIDE;
+  const int sub = lane >> 3, col = (lane & 7) * 4, n = n0 + col;
+  float4 v[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) v[it] = *reinterpret_cast<const float4*>(stage + (it * 4 + sub) * S + col);
+  if constexpr (EPI == TB_EPI_RESIDUAL) {
+    float* out = reinterpret_cast<float*>(e.out);
+    float4 x[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      x[it] = m < M ? load4(out + (long long)m * e.ldo + n) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M)
+        store4(out + (long long)m * e.ldo + n, x[it].x + e.alpha * v[it].x, x[it].y + e.alpha * v[it].y,
+               x[it].z + e.alpha * v[it].z, x[it].w + e.alpha * v[it].w);
+    }
+  } else if constexpr (EPI == TB_EPI_STORE || EPI == TB_EPI_BIAS_RELU) {
+    const float4 b = e.bias ? load4(e.bias + n) : make_float4(0, 0, 0, 0);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m >= M) continue;
+      float a0 = v[it].x + b.x, a1 = v[it].y + b.y, a2 = v[it].z + b.z, a3 = v[it].w + b.w;
+      if constexpr (EPI == TB_EPI_BIAS_RELU) a0 = fmaxf(a0, 0.f), a1 = fmaxf(a1, 0.f), a2 = fmaxf(a2, 0.f), a3 = fmaxf(a3, 0.f);
+      store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, a0, a1, a2, a3);
+    }
+  } else if constexpr (EPI == TB_EPI_SILU) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M)
+        store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, fast_silu(v[it].x), fast_silu(v[it].y),
+                  fast_silu(v[it].z), fast_silu(v[it].w));
+    }
+  } else if constexpr (EPI == TB_EPI_GLU) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M)
+        store2_dt(e.out, (long long)m * e.ldo + (n >> 1), e.out_dtype, v[it].x * fast_sigmoid(v[it].y),
+                  v[it].z * fast_sigmoid(v[it].w));
+    }
+  } else if constexpr (EPI == TB_EPI_QKV) {
+    const int sec = n >> 10, c = n & 1023;
+    void* dst = sec == 0 ? e.out : (sec == 1 ? e.out3 : e.out4);
+    const float4 u = sec == 0 ? load4(e.bias_u + c) : make_float4(0, 0, 0, 0);
+    const float4 w = sec == 0 ? load4(e.bias_v + c) : make_float4(0, 0, 0, 0);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m >= M) continue;
+      const long long off = (long long)m * e.ldo + c;
+      store4_dt(dst, off, e.out_dtype, v[it].x + u.x, v[it].y + u.y, v[it].z + u.z, v[it].w + u.w);
+      if (sec == 0 && e.out2)
+        store4_dt(e.out2, off, e.out_dtype, v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
+    }
+  } else if constexpr (EPI == TB_EPI_JOINT_IN) {
+    constexpr int PX = EpiPre<EPI, BN>::PX;
+    const float4 b = pre.b[ci];
+    float* out = reinterpret_cast<float*>(e.out);
+    float4 x[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      if (ci < PX)
+        x[it] = pre.x[ci < PX ? ci : 0][it];
+      else
+        x[it] = pre.g[it] >= 0 ? load4(e.gather + (long long)pre.g[it] * e.ldo + n) : make_float4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m >= M) continue;
+      const float d0 = v[it].x + b.x, d1 = v[it].y + b.y, d2 = v[it].z + b.z, d3 = v[it].w + b.w;
+      store4(out + (long long)m * e.ldo + n, d0, d1, d2, d3);
+      if (pre.g[it] >= 0)
+        store4_dt(e.out2, (long long)m * e.ldo2 + n, e.out_dtype, fmaxf(x[it].x + d0, 0.f), fmaxf(x[it].y + d1, 0.f),
+                  fmaxf(x[it].z + d2, 0.f), fmaxf(x[it].w + d3, 0.f));
+    }
+  }
+}
+
+// The LSTM cell epilogue for one warp's 32 rows of a tile. W rows are gate-interleaved,
+// so columns n0 .. n0+BN-1 hold the gates (i, f, g, o) of units u0 = n0/4 .. u0+U-1,
+// U = BN/4. Each lane computes the cells of one row (tensor-memory lane = row) straight
+// from its 32-column chunks; the previous cell state comes in (cp.async, issued before
+// the accumulator wait) and the new c and h go out through `tile` (32 rows x 33 floats
+// of shared memory), so that global loads and stores are whole row segments (one
+// 128-byte line per row for U = 32) rather than a 32-byte piece per row and chunk.
+// Loops are kept rolled: in the persistent decoder every phase runs its epilogue once
+// per iteration, and compact code stays in the instruction cache between iterations.
+// Rows with mask[m] == 0 (and rows >= M) are left as they are.
+template <int BN>
+__device__ __forceinline__ bool lstm_tile(const tb_epilogue& e, float* tile, uint32_t taddr, int row0, int n0,
+                                          int lane, int M, uint64_t* tfull, uint32_t ph, int* err,
+                                          volatile int* abort) {
+  static_assert(BN == 64 || BN == 128, "LSTM tiles cover 16 or 32 units");
+  constexpr int U = BN / 4, RPI = 32 / U, TS = 33;  // units per row, rows per warp access, tile stride
+  const int u0 = n0 >> 2, j = lane % U, rsub = lane / U;
+  float* const cst = e.c;
+  float* const hst = e.h;
+  const float* const bias = e.bias;
+  void* const out = e.out;
+  void* const out2 = e.out2;
+  const int dt = e.out_dtype;
+  const long long ldo = e.ldo, ldo2 = e.ldo2;
+#pragma unroll 1
+  for (int it = 0; it < U; ++it) {
+    const int row = it * RPI + rsub, m = row0 + row;
+    if (m < M) cp_async4(tile + row * TS + j, cst + (long long)m * TB_PRED + u0 + j);
+  }
+  cp_async_commit();
+  // Lane l holds the four gate biases of unit u0 + l (l < U); the cells take them by shuffle.
+  const float4 bl = load4(bias + n0 + 4 * (lane % U));
+  const int my_m = row0 + lane;
+  const int step = my_m < M && (!e.mask || e.mask[my_m] != 0);
+  if (!warp_wait(tfull, ph, err, abort)) {
+    cp_async_wait_all();
+    return false;
+  }
+  tc_fence_after();
+  cp_async_wait_all();
+  const unsigned steps = __ballot_sync(0xffffffffu, step);  // bit r: row row0 + r is updated
+  __syncwarp();
+  // Pass 1: the new cell state, into the tile, then out to e.c.
+#pragma unroll 1
+  for (int ci = 0; ci < BN / 32; ++ci) {
+    uint32_t r[32];
+    tmem_ld32(taddr + ci * 32, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int uu = ci * 8 + k;
+      const float ig = sigmoid_mufu(__uint_as_float(r[4 * k]) + __shfl_sync(0xffffffffu, bl.x, uu));
+      const float fg = sigmoid_mufu(__uint_as_float(r[4 * k + 1]) + __shfl_sync(0xffffffffu, bl.y, uu));
+      const float gg = tanh_mufu(__uint_as_float(r[4 * k + 2]) + __shfl_sync(0xffffffffu, bl.z, uu));
+      float* t = tile + lane * TS + uu;
+      *t = fg * *t + ig * gg;
+    }
+  }
+  __syncwarp();
+  // Row segments out: every tile read first, then the stores (program order keeps the
+  // loads from waiting behind stores the compiler cannot prove disjoint).
+  float v[U];
+#pragma unroll
+  for (int it = 0; it < U; ++it) v[it] = tile[(it * RPI + rsub) * TS + j];
+#pragma unroll
+  for (int it = 0; it < U; ++it) {
+    const int row = it * RPI + rsub, m = row0 + row;
+    if (((steps >> row) & 1u) && m < M) cst[(long long)m * TB_PRED + u0 + j] = v[it];
+  }
+  __syncwarp();
+  // Pass 2: h = o * tanh(c), the output gate read again from tensor memory (the
+  // accumulator is not released until this epilogue returns), into the tile and out.
+#pragma unroll 1
+  for (int ci = 0; ci < BN / 32; ++ci) {
+    uint32_t r[32];
+    tmem_ld32(taddr + ci * 32, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int uu = ci * 8 + k;
+      const float og = sigmoid_mufu(__uint_as_float(r[4 * k + 3]) + __shfl_sync(0xffffffffu, bl.w, uu));
+      float* t = tile + lane * TS + uu;
+      *t = og * tanh_mufu(*t);
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < U; ++it) v[it] = tile[(it * RPI + rsub) * TS + j];
+  auto row_ok = [&](int it) {
+    const int row = it * RPI + rsub;
+    return ((steps >> row) & 1u) && row0 + row < M;
+  };
+  auto at = [&](int it, long long ld) { return (long long)(row0 + it * RPI + rsub) * ld + u0 + j; };
+  if (hst) {
+#pragma unroll
+    for (int it = 0; it < U; ++it)
+      if (row_ok(it)) hst[at(it, TB_PRED)] = v[it];
+  }
+  if (dt == TB_BF16) {
+    if (out) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<__nv_bfloat16*>(out)[at(it, ldo)] = __float2bfloat16_rn(v[it]);
+    }
+    if (out2) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<__nv_bfloat16*>(out2)[at(it, ldo2)] = __float2bfloat16_rn(v[it]);
+    }
+  } else {
+    if (out) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<float*>(out)[at(it, ldo)] = v[it];
+    }
+    if (out2) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<float*>(out2)[at(it, ldo2)] = v[it];
+    }
+  }
+  __syncwarp();
+  return true;
+}
+
+// The joint head's epilogue for one row (one lane) of a tile: the largest token logit
+// and the largest duration logit with their first column, merged into the row's keys.
+// `bias` holds the tile's BN bias values. Padding columns have bias -inf and never win.
+template <int BN>
+__device__ __forceinline__ void argmax_tile(const tb_epilogue& e, const float* bias, uint32_t taddr, int m, int n0,
+                                            int M) {
+  const float neg_inf = __int_as_float(0xff800000);
+  const int split = e.split, split_end = e.split_end;
+  // Four running maxima over the columns j = 0, 1, 2, 3 mod 4 (shorter dependent compare
+  // chains), merged at the end; each keeps the first of equal values (strictly greater,
+  // columns ascending).
+  float best[4] = {neg_inf, neg_inf, neg_inf, neg_inf};
+  int idx[4] = {-1, -1, -1, -1};
+  float dbest = neg_inf;
+  int di = -1;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    const int n = n0 + c;
+    if (n >= split_end) break;  // only padding columns (bias -inf) from here on
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+    if (n + 32 <= split) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(bias + c + j);
+        const float x0 = __uint_as_float(r[j]) + b.x, x1 = __uint_as_float(r[j + 1]) + b.y;
+        const float x2 = __uint_as_float(r[j + 2]) + b.z, x3 = __uint_as_float(r[j + 3]) + b.w;
+        if (x0 > best[0]) best[0] = x0, idx[0] = n + j;
+        if (x1 > best[1]) best[1] = x1, idx[1] = n + j + 1;
+        if (x2 > best[2]) best[2] = x2, idx[2] = n + j + 2;
+        if (x3 > best[3]) best[3] = x3, idx[3] = n + j + 3;
+      }
+    } else {  // the chunk holding the token/duration boundary
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = __uint_as_float(r[j]) + bias[c + j];
+        if (n + j < split) {
+          if (x > best[0]) best[0] = x, idx[0] = n + j;
+        } else if (n + j < split_end) {
+          if (x > dbest) dbest = x, di = n + j - split;
+        }
+      }
+    }
+  }
+  float tb = best[0];
+  int ti = idx[0];
+#pragma unroll
+  for (int k = 1; k < 4; ++k)
+    if (idx[k] >= 0 && (ti < 0 || best[k] > tb || (best[k] == tb && idx[k] < ti))) tb = best[k], ti = idx[k];
+  if (m < M) {
+    if (ti >= 0) atomicMax(e.keys + m, argmax_key(tb, ti));
+    if (di >= 0) atomicMax(e.keys2 + m, argmax_key(dbest, di));
+  }
+}
+
+// The epilogue of one accumulator tile for the calling epilogue warp: its 32 rows
+// row0 .. row0+31 (tensor-memory lanes of the warp's quarter, at `taddr`), columns
+// n0 .. n0+BN-1. Loads the epilogue's global operands, waits for the accumulator
+// (`tfull`, parity `ph`), then drains it in 32-column chunks through the warp's staging
+// rows `stage` (32 x TC_OUT_STRIDE floats). Rows >= M are not written. False if the
+// wait gave up (error recorded in `err`).
+template <int BN, int EPI>
+__device__ __forceinline__ bool epilogue_tile(const tb_epilogue& e, float* stage, uint32_t taddr, int row0, int n0,
+                                              int lane, int M, uint64_t* tfull, uint32_t ph, int* err,
+                                              volatile int* abort) {
+  if constexpr (EPI == TB_EPI_LSTM) {
+    return lstm_tile<BN>(e, stage, taddr, row0, n0, lane, M, tfull, ph, err, abort);
+  } else if constexpr (EPI == TB_EPI_ARGMAX) {
+    // The tile's bias, loaded before the wait, then kept in the warp's staging rows.
+    float bias[BN / 32];
+#pragma unroll
+    for (int ci = 0; ci < BN / 32; ++ci) bias[ci] = e.bias[n0 + ci * 32 + lane];
+    if (!warp_wait(tfull, ph, err, abort)) return false;
+    tc_fence_after();
+#pragma unroll
+    for (int ci = 0; ci < BN / 32; ++ci) stage[ci * 32 + lane] = bias[ci];
+    __syncwarp();
+    argmax_tile<BN>(e, stage, taddr, row0 + lane, n0, M);
+    __syncwarp();
+  } else {
+    EpiPre<EPI, BN> pre;
+    pre.load(e, row0, n0, lane, M);
+    if (!warp_wait(tfull, ph, err, abort)) return false;
+    tc_fence_after();
+    auto chunk = [&](int ci) {
+      uint32_t r[32];
+      tmem_ld32(taddr + ci * 32, r);
+      tmem_wait_ld();
+      float4* srow = reinterpret_cast<float4*>(stage + lane * TC_OUT_STRIDE);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        srow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                              __uint_as_float(r[4 * j + 3]));
+      __syncwarp();
+      epi_chunk<EPI, BN>(e, stage, row0, n0 + ci * 32, lane, M, pre, ci);
+      __syncwarp();
+    };
+    if constexpr (EPI == TB_EPI_JOINT_IN) {
+#pragma unroll
+      for (int ci = 0; ci < BN / 32; ++ci) chunk(ci);  // prefetched values indexed by ci
+    } else {
+#pragma unroll 1
+      for (int ci = 0; ci < BN / 32; ++ci) chunk(ci);
+    }
+  }
+  return true;
+}
+
+}  // namespace tb

@@ -23,21 +23,14 @@ DTYPES = {"fp32": L.F32, "bf16": L.BF16}
 MAX_DECODE_GROUPS = 8
 
 
-def decode_groups(lanes: int) -> int:
-    """Concurrent decoder groups for `lanes` clips. One: on a B200 the greedy loop's time
-    is set by the latency of its chain of small GEMMs, which splitting the lanes into
-    groups on separate streams does not shorten (512 lanes: 182 ms as 1 group, the same
-    as 2 or 4 groups, 50 % more as 8)."""
-    return 1
-
-
 def lane_order(idx: list[int], frames: list[int], groups: int | None = None) -> list[int]:
-    """Orders clips `idx` (frame counts `frames[i]`) for the decoder: longest first, dealt
-    round-robin into `groups` groups (default decode_groups), the groups concatenated.
-    Each group then holds clips of every length, and within a group the lanes finish
-    from its end, so its GEMMs shrink to the lanes still running."""
+    """Orders clips `idx` (frame counts `frames[i]`) for the decoder: longest first, and
+    for the graph decoder with `groups` > 1 concurrent groups, dealt round-robin into
+    the groups, the groups concatenated. Each group then holds clips of every length,
+    and within a group the lanes finish from its end, so its GEMMs shrink to the lanes
+    still running."""
     order = sorted(idx, key=lambda i: -frames[i])
-    g = decode_groups(len(order)) if groups is None else groups
+    g = max(1, groups or 1)
     return [i for k in range(g) for i in order[k::g]]
 
 
@@ -294,11 +287,12 @@ class Engine:
     def decode(self, enc: torch.Tensor, plan: Plan, early_exit: bool = True,
                groups: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """Greedy TDT decoding of every clip; returns device (tokens [clips, max_cap], counts [clips]).
-        The clips are decoded as `groups` concurrent groups (default decode_groups(clips)),
-        group g holding clips g, g + groups, ... of the plan's order reshuffled by
-        lane_order; any order gives the same tokens."""
+        `groups` None or 0: the library's default decoder (bf16: one persistent kernel for
+        the whole loop; fp32: graph-replayed GEMM kernels); 1..8: the graph decoder with
+        that many concurrent lane groups (clips in lane_order for balanced groups). Every
+        choice gives the same tokens."""
         b = plan.batch
-        g = decode_groups(b.clips) if groups is None else int(groups)
+        g = 0 if groups is None else int(groups)
         tokens = torch.empty(b.clips, plan.max_cap, device=self.device, dtype=torch.int32)
         counts = torch.empty(b.clips, device=self.device, dtype=torch.int32)
         nbytes = L.lib.tb_decode_workspace_bytes(self.dtype, b.clips, g)
