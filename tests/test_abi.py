@@ -41,7 +41,7 @@ def test_workspace_queries_need_no_gpu():
     assert one > 64 * 640 * 4
     assert lib.tb_decode_workspace_bytes(_lib.BF16, 64, 4) >= one
     assert lib.tb_frontend_workspace_bytes(4, 1000) >= 4 * 128 * 16
-    assert _lib.tile_rows(_lib.F32)[0] == 2
+    assert _lib.tile_rows(_lib.F32)[0] == 8
 
 
 def test_bad_arguments_are_rejected_without_touching_the_device():

@@ -204,7 +204,7 @@ long long tb_launch_count(void) { return g_launches.load(); }
 
 int tb_tile_rows(int dtype, int* sub_rows, int* attn_rows) {
   if (!sub_rows || !attn_rows || (dtype != TB_F32 && dtype != TB_BF16)) return TB_ERR_ARG;
-  *sub_rows = 2;
+  *sub_rows = subsample_tile_rows();
   *attn_rows = attention_tile_rows(dtype);
   return TB_OK;
 }

@@ -36,6 +36,7 @@ int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, c
 int subsample(const tb_model& m, const tb_batch& batch, const float* feats, float* x, void* ws, size_t ws_bytes,
               int* err, cudaStream_t stream);
 size_t subsample_ws(int dtype, int t2_total, int t3_total);
+int subsample_tile_rows();  // depthwise-1 rows per work item of the fused conv-0 kernel
 int attention_tile_rows(int dtype);
 
 // Launches `kernel` with programmatic stream serialization (see grid_dep_wait in

@@ -8,19 +8,28 @@
 // already the (time, 16 * 256) matrix of the linear, whose weight columns the loader
 // permutes from the reference's (channel, frequency) order to (frequency, channel).
 //
-// The first conv is recomputed inside the first depthwise conv's tile (its halo is one
-// row), so its 256-channel output never reaches HBM.
+// The first conv is computed inside the first depthwise conv's kernel, so its
+// 256-channel output never reaches HBM.
 #include "epilogue.cuh"
 #include "host.h"
 
 namespace tb {
 
-constexpr int S_T2 = 2;          // depthwise-1 output rows per block
-constexpr int S_C = 32;          // channels per block (one warp)
-constexpr int S_T1 = 2 * S_T2 + 1;  // conv-0 rows a block needs
+constexpr int S_T2 = 8;          // depthwise-1 output rows per block: one warp each
+constexpr int S_C = 64;          // channels per block: two per lane
 constexpr int S_F1 = 64, S_F2 = 32, S_F3 = 16;
-constexpr int S_FEAT_ROWS = 2 * S_T1 + 1;
+constexpr int S_FEAT_ROWS = 4 * S_T2 + 3;  // feature rows behind S_T2 depthwise-1 rows
+constexpr int S_FEAT_COLS = TB_MELS + 2;   // frequency padded by one each side
 
+// conv 0 (3x3/2, 1 -> 256, + ReLU) fused into depthwise 1 (3x3/2 + bias). Warp w of a
+// block makes depthwise-1 row t2 = t2a + w for channels c0 + lane and c0 + 32 + lane,
+// sweeping its 32 output frequencies f2 left to right. Output f2 needs conv-0 columns
+// f1 = 2 f2 - 1, 2 f2, 2 f2 + 1 of conv-0 rows t1 = 2 t2 - 1 + dt (dt = 0..2); the
+// first of those columns is the previous step's last, so each step computes 2 x 3
+// conv-0 values per channel from a 7 x 5 window of features (the window's first
+// column also carried over), all features read from shared memory (the same address
+// for every lane: one broadcast per read). Conv-0 values outside the clip's rows or
+// the frequency range are the zero padding of depthwise 1.
 template <typename T>
 __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict__ feats,
                                                         const int* __restrict__ frame_off,
@@ -28,61 +37,82 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
                                                         const int* __restrict__ tiles, const float* __restrict__ w0,
                                                         const float* __restrict__ b0, const float* __restrict__ w1,
                                                         const float* __restrict__ b1, T* __restrict__ d1) {
-  __shared__ float sf[S_FEAT_ROWS][TB_MELS + 2];    // features, frequency padded by one each side
-  __shared__ float s1[S_T1][S_F1 + 2][S_C];          // conv-0 output, frequency padded by one each side
+  __shared__ float sf[S_FEAT_ROWS][S_FEAT_COLS];
   const int clip = tiles[2 * blockIdx.x], t2a = tiles[2 * blockIdx.x + 1];
-  const int c0 = blockIdx.y * S_C;
   const int F = frame_off[clip + 1] - frame_off[clip], T1 = t1_off[clip + 1] - t1_off[clip],
             T2 = t2_off[clip + 1] - t2_off[clip];
   const float* fbase = feats + (long long)frame_off[clip] * TB_MELS;
-  const int t1a = 2 * t2a - 1;        // first conv-0 row
-  const int fa = 2 * t1a - 1;         // first feature row
+  const int fa = 4 * t2a - 3;  // feature row of the tile's first shared-memory row
 
-  for (int i = threadIdx.x; i < S_FEAT_ROWS * (TB_MELS + 2); i += 256) {
-    const int r = i / (TB_MELS + 2), f = i % (TB_MELS + 2) - 1;
+  for (int i = threadIdx.x; i < S_FEAT_ROWS * S_FEAT_COLS; i += 256) {
+    const int r = i / S_FEAT_COLS, f = i % S_FEAT_COLS - 1;
     const int t = fa + r;
     sf[r][f + 1] = (t >= 0 && t < F && f >= 0 && f < TB_MELS) ? fbase[(long long)t * TB_MELS + f] : 0.f;
   }
-  const int c = threadIdx.x & (S_C - 1);
-  const int lane_group = threadIdx.x >> 5;  // warp: 0..7
-  float k0[9];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ca = blockIdx.y * S_C + lane, cb = ca + 32;
+  float k0a[9], k0b[9], k1a[9], k1b[9];
 #pragma unroll
-  for (int i = 0; i < 9; ++i) k0[i] = w0[(c0 + c) * 9 + i];
-  const float bias0 = b0[c0 + c];
-  __syncthreads();
-
-  // conv 0 (+ ReLU), zero outside the clip's rows and the frequency range.
-  for (int i = lane_group; i < S_T1 * (S_F1 + 2); i += 8) {
-    const int r = i / (S_F1 + 2), f1 = i % (S_F1 + 2) - 1;
-    const int t1 = t1a + r;
-    float v = 0.f;
-    if (t1 >= 0 && t1 < T1 && f1 >= 0 && f1 < S_F1) {
-      float acc = bias0;
-#pragma unroll
-      for (int dt = 0; dt < 3; ++dt)
-#pragma unroll
-        for (int df = 0; df < 3; ++df) acc = fmaf(k0[dt * 3 + df], sf[2 * r + dt][2 * f1 + df], acc);
-      v = fmaxf(acc, 0.f);
-    }
-    s1[r][f1 + 1][c] = v;
+  for (int i = 0; i < 9; ++i) {
+    k0a[i] = w0[ca * 9 + i];
+    k0b[i] = w0[cb * 9 + i];
+    k1a[i] = w1[ca * 9 + i];
+    k1b[i] = w1[cb * 9 + i];
   }
-  float k1[9];
-#pragma unroll
-  for (int i = 0; i < 9; ++i) k1[i] = w1[(c0 + c) * 9 + i];
-  const float bias1 = b1[c0 + c];
+  const float b0a = b0[ca], b0b = b0[cb], b1a = b1[ca], b1b = b1[cb];
   __syncthreads();
-
-  // depthwise 1
-  for (int i = lane_group; i < S_T2 * S_F2; i += 8) {
-    const int r = i / S_F2, f2 = i % S_F2;
-    const int t2 = t2a + r;
-    if (t2 >= T2) continue;
-    float acc = bias1;
+  const int t2 = t2a + w;
+  if (t2 >= T2) return;
+  bool rowok[3];
 #pragma unroll
-    for (int dt = 0; dt < 3; ++dt)
+  for (int dt = 0; dt < 3; ++dt) {
+    const int t1 = 2 * t2 - 1 + dt;
+    rowok[dt] = t1 >= 0 && t1 < T1;
+  }
+  const float* srow = &sf[4 * w][0];  // conv-0 row dt reads feature rows 2 dt .. 2 dt + 2 of these 7
+  float xc[7];                        // feature column 4 f2 (padded), carried from the previous step
 #pragma unroll
-      for (int df = 0; df < 3; ++df) acc = fmaf(k1[dt * 3 + df], s1[2 * r + dt][2 * f2 + df][c], acc);
-    d1[((long long)(t2_off[clip] + t2) * S_F2 + f2) * TB_CHANNELS + c0 + c] = from_f<T>(acc);
+  for (int r = 0; r < 7; ++r) xc[r] = srow[r * S_FEAT_COLS];
+  float pa[3] = {0.f, 0.f, 0.f}, pb[3] = {0.f, 0.f, 0.f};  // conv-0 column 2 f2 - 1 (zero at f2 = 0)
+  T* out = d1 + (long long)(t2_off[clip] + t2) * S_F2 * TB_CHANNELS;
+#pragma unroll 1
+  for (int f2 = 0; f2 < S_F2; ++f2) {
+    float x1[7], x2[7], x3[7], x4[7];
+#pragma unroll
+    for (int r = 0; r < 7; ++r) {
+      const float* q = srow + r * S_FEAT_COLS + 4 * f2;
+      x1[r] = q[1];
+      x2[r] = q[2];
+      x3[r] = q[3];
+      x4[r] = q[4];
+    }
+    float acc_a = b1a, acc_b = b1b;
+#pragma unroll
+    for (int dt = 0; dt < 3; ++dt) {
+      // conv 0 at columns 2 f2 (features 4 f2 .. 4 f2 + 2) and 2 f2 + 1 (4 f2 + 2 .. 4 f2 + 4)
+      float va = b0a, vb = b0b, ua = b0a, ub = b0b;
+#pragma unroll
+      for (int dr = 0; dr < 3; ++dr) {
+        const int r = 2 * dt + dr;
+        va = fmaf(k0a[dr * 3], xc[r], fmaf(k0a[dr * 3 + 1], x1[r], fmaf(k0a[dr * 3 + 2], x2[r], va)));
+        vb = fmaf(k0b[dr * 3], xc[r], fmaf(k0b[dr * 3 + 1], x1[r], fmaf(k0b[dr * 3 + 2], x2[r], vb)));
+        ua = fmaf(k0a[dr * 3], x2[r], fmaf(k0a[dr * 3 + 1], x3[r], fmaf(k0a[dr * 3 + 2], x4[r], ua)));
+        ub = fmaf(k0b[dr * 3], x2[r], fmaf(k0b[dr * 3 + 1], x3[r], fmaf(k0b[dr * 3 + 2], x4[r], ub)));
+      }
+      va = rowok[dt] ? fmaxf(va, 0.f) : 0.f;
+      vb = rowok[dt] ? fmaxf(vb, 0.f) : 0.f;
+      ua = rowok[dt] ? fmaxf(ua, 0.f) : 0.f;
+      ub = rowok[dt] ? fmaxf(ub, 0.f) : 0.f;
+      // depthwise 1 over conv-0 columns 2 f2 - 1, 2 f2, 2 f2 + 1
+      acc_a = fmaf(k1a[dt * 3], pa[dt], fmaf(k1a[dt * 3 + 1], va, fmaf(k1a[dt * 3 + 2], ua, acc_a)));
+      acc_b = fmaf(k1b[dt * 3], pb[dt], fmaf(k1b[dt * 3 + 1], vb, fmaf(k1b[dt * 3 + 2], ub, acc_b)));
+      pa[dt] = ua;
+      pb[dt] = ub;
+    }
+#pragma unroll
+    for (int r = 0; r < 7; ++r) xc[r] = x4[r];
+    out[f2 * TB_CHANNELS + ca] = from_f<T>(acc_a);
+    out[f2 * TB_CHANNELS + cb] = from_f<T>(acc_b);
   }
 }
 
@@ -111,6 +141,8 @@ __global__ void __launch_bounds__(256) dw2_kernel(const T* __restrict__ s2, cons
   }
   d2[((long long)row * S_F3 + f3) * TB_CHANNELS + c] = from_f<T>(acc);
 }
+
+int subsample_tile_rows() { return S_T2; }
 
 size_t subsample_ws(int dtype, int t2_total, int t3_total) {
   const size_t e = dsize(dtype);

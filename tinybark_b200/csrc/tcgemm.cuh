@@ -29,8 +29,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
-__device__ __forceinline__ float fast_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 // The PTX tanh.approx.f32 instruction (one MUFU operation, about 2^-11 relative error).
 // Used in the bf16 decoder's LSTM cell, whose inputs and outputs are bf16 (2^-8).
 __device__ __forceinline__ float tanh_mufu(float x) {
@@ -74,13 +72,56 @@ struct EpiPre<TB_EPI_JOINT_IN, BN> {
   }
 };
 
+// Global operands of one 32-column chunk, loaded one chunk ahead (the first before the
+// accumulator wait) so their latency overlaps the previous chunk's work: the residual
+// rows (RESIDUAL), the bias (STORE, BIAS_RELU) or the two position biases (QKV). Lane
+// layout as in epi_chunk.
+template <int EPI>
+struct ChunkOps {
+  __device__ __forceinline__ void load(const tb_epilogue&, int, int, int, int) {}
+};
+template <>
+struct ChunkOps<TB_EPI_RESIDUAL> {
+  float4 x[8];
+  __device__ __forceinline__ void load(const tb_epilogue& e, int row0, int n0, int lane, int M) {
+    const int sub = lane >> 3, n = n0 + (lane & 7) * 4;
+    const float* out = reinterpret_cast<const float*>(e.out);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      x[it] = m < M ? load4(out + (long long)m * e.ldo + n) : make_float4(0, 0, 0, 0);
+    }
+  }
+};
+template <int EPI>
+struct BiasOps {
+  float4 b;
+  __device__ __forceinline__ void load(const tb_epilogue& e, int, int n0, int lane, int) {
+    b = e.bias ? load4(e.bias + n0 + (lane & 7) * 4) : make_float4(0, 0, 0, 0);
+  }
+};
+template <>
+struct ChunkOps<TB_EPI_STORE> : BiasOps<TB_EPI_STORE> {};
+template <>
+struct ChunkOps<TB_EPI_BIAS_RELU> : BiasOps<TB_EPI_BIAS_RELU> {};
+template <>
+struct ChunkOps<TB_EPI_QKV> {
+  float4 u, v;
+  __device__ __forceinline__ void load(const tb_epilogue& e, int, int n0, int lane, int) {
+    const int n = n0 + (lane & 7) * 4, c = n & 1023;
+    const bool q = (n >> 10) == 0;
+    u = q ? load4(e.bias_u + c) : make_float4(0, 0, 0, 0);
+    v = q && e.out2 ? load4(e.bias_v + c) : make_float4(0, 0, 0, 0);
+  }
+};
+
 // The epilogue of one warp's 32 x 32 chunk ci of a tile, staged row-major (stride
 // OUT_STRIDE) in `stage`: lane reads rows 4*it + lane/8 (it = 0..7), columns
 // 4*(lane%8) .. +3. row0: global row of the chunk's first row; n0: global column of its
 // first column.
 template <int EPI, int BN>
 __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* stage, int row0, int n0, int lane, int M,
-                                          const EpiPre<EPI, BN>& pre, int ci) {
+                                          const EpiPre<EPI, BN>& pre, int ci, const ChunkOps<EPI>& ops) {
   constexpr int S = TC_OUT_STRIDE;
   const int sub = lane >> 3, col = (lane & 7) * 4, n = n0 + col;
   float4 v[8];
@@ -88,12 +129,7 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
   for (int it = 0; it < 8; ++it) v[it] = *reinterpret_cast<const float4*>(stage + (it * 4 + sub) * S + col);
   if constexpr (EPI == TB_EPI_RESIDUAL) {
     float* out = reinterpret_cast<float*>(e.out);
-    float4 x[8];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      x[it] = m < M ? load4(out + (long long)m * e.ldo + n) : make_float4(0, 0, 0, 0);
-    }
+    const float4* x = ops.x;
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int m = row0 + it * 4 + sub;
@@ -102,7 +138,7 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
                x[it].z + e.alpha * v[it].z, x[it].w + e.alpha * v[it].w);
     }
   } else if constexpr (EPI == TB_EPI_STORE || EPI == TB_EPI_BIAS_RELU) {
-    const float4 b = e.bias ? load4(e.bias + n) : make_float4(0, 0, 0, 0);
+    const float4 b = ops.b;
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int m = row0 + it * 4 + sub;
@@ -130,8 +166,8 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
   } else if constexpr (EPI == TB_EPI_QKV) {
     const int sec = n >> 10, c = n & 1023;
     void* dst = sec == 0 ? e.out : (sec == 1 ? e.out3 : e.out4);
-    const float4 u = sec == 0 ? load4(e.bias_u + c) : make_float4(0, 0, 0, 0);
-    const float4 w = sec == 0 ? load4(e.bias_v + c) : make_float4(0, 0, 0, 0);
+    (void)c;
+    const float4 u = ops.u, w = ops.v;
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int m = row0 + it * 4 + sub;
@@ -374,9 +410,13 @@ __device__ __forceinline__ bool epilogue_tile(const tb_epilogue& e, float* stage
   } else {
     EpiPre<EPI, BN> pre;
     pre.load(e, row0, n0, lane, M);
+    ChunkOps<EPI> ops;
+    ops.load(e, row0, n0, lane, M);
     if (!warp_wait(tfull, ph, err, abort)) return false;
     tc_fence_after();
     auto chunk = [&](int ci) {
+      ChunkOps<EPI> next;  // the next chunk's operands, in flight during this one
+      if (ci + 1 < BN / 32) next.load(e, row0, n0 + (ci + 1) * 32, lane, M);
       uint32_t r[32];
       tmem_ld32(taddr + ci * 32, r);
       tmem_wait_ld();
@@ -386,8 +426,9 @@ __device__ __forceinline__ bool epilogue_tile(const tb_epilogue& e, float* stage
         srow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
                               __uint_as_float(r[4 * j + 3]));
       __syncwarp();
-      epi_chunk<EPI, BN>(e, stage, row0, n0 + ci * 32, lane, M, pre, ci);
+      epi_chunk<EPI, BN>(e, stage, row0, n0 + ci * 32, lane, M, pre, ci, ops);
       __syncwarp();
+      ops = next;
     };
     if constexpr (EPI == TB_EPI_JOINT_IN) {
 #pragma unroll
