@@ -49,7 +49,7 @@ def args_parser():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated kernels (layernorm,ffn,conv,mhsa)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -522,6 +522,36 @@ def run_micro(args):
                     emit(kernel="relpos_attention", dtype=dt_name, rows=rows, T=t, clips=clips, us=s * 1e6,
                          tflops=fl / s / 1e12, frac=fl / s / 1e12 / tflops)
     K.check(dev)
+    if want("longform"):
+        run_longform(args, dev, tflops)
+
+
+def run_longform(args, dev, tflops):
+    """The long-form workload: one 10-minute clip (f0 redrawn every 2 s, T = 7500 encoder
+    frames) through front-end, encoder with full-context attention, and decode, bf16."""
+    import torch
+
+    import tinybark_b200
+    from tinybark_b200 import synthetic
+
+    seconds = 600.0
+    clip = synthetic.to_float(synthetic.clip(seconds, 3, segment=2.0))
+    tensors, cfg = weights(args.layers)
+    bark = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg))
+    eng = bark.engine
+    plan = eng.plan([len(clip) // 160])
+    eng.ensure_len(int(plan.t3.max()))
+    samples, off = eng.upload([clip])
+    split = {}
+    for _ in range(3):
+        split = stage_split(eng, samples, off, plan)
+    eng.check()
+    T = int(plan.t3[0])
+    enc_flop = args.layers * (48.2e6 * T + 6.0 * T * T * 1024)
+    total = sum(split.values())
+    print(json.dumps({"kernel": "longform_10min", "dtype": "bf16", "audio_s": seconds, "T": T, "layers": args.layers,
+                      "stages_ms": split, "rtfx": seconds / (total / 1000), "encoder_tflops": enc_flop / split["encoder"] / 1e9,
+                      "encoder_frac": enc_flop / split["encoder"] / 1e9 / tflops}), flush=True)
 
 
 def stage_split(eng, samples, sample_off, plan, groups=None):

@@ -224,6 +224,42 @@ def test_relpos_attention(L, dtype, t3, max_len, err):
 
 
 @pytest.mark.parametrize("dtype", [0, 1])
+def test_relpos_attention_long_form(L, dtype, err):
+    """One 10-minute clip (T = 7500 encoder frames, the long-form workload) with
+    full-context attention; the reference works in 500-row blocks (fp32, rel-shift as a
+    gather of the banded scores) so that no T x T x 128 tensor is formed."""
+    from tinybark_b200 import kernels
+
+    T = 7500
+    _, attn_rows = L.tile_rows(dtype)
+    b, keep, off = batch_for(L, [T], attn_rows)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q, k, v = (torch.randn(T, 1024, device="cuda", generator=g) for _ in range(3))
+    bu, bv = torch.randn(1024, device="cuda", generator=g), torch.randn(1024, device="cuda", generator=g)
+    qu, qv, k, v = (x.to(tdt(dtype)) for x in (q + bu, q + bv, k, v))
+    rel = torch.randn(2 * T - 1, 1024, device="cuda", generator=g).to(tdt(dtype))
+    rel_c = kernels.rel_bias(rel, bu, bv) if dtype == 1 else None
+    out = torch.empty(T, 1024, device="cuda", dtype=tdt(dtype))
+    L.check(L.lib.tb_relpos_attention(dtype, qu.data_ptr(), qv.data_ptr(), k.data_ptr(), v.data_ptr(), rel.data_ptr(),
+                                      None if rel_c is None else rel_c.data_ptr(), T, ctypes.byref(b), out.data_ptr(),
+                                      err.data_ptr(), stream()), "tb_relpos_attention")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    qpos = qv.float() if dtype == 0 else qu.float() + (bv - bu).to(tdt(dtype)).float()
+    heads = lambda x: x.float().view(-1, 8, 128).transpose(0, 1)  # (H, rows, d)
+    K, V, Rh = heads(k), heads(v), heads(rel)
+    worst = 0.0
+    for i0 in range(0, T, 500):
+        i = torch.arange(i0, min(i0 + 500, T), device="cuda")
+        band = heads(qpos[i]) @ Rh.transpose(1, 2)  # (H, rows, 2T-1): position T-1-n of row n
+        idx = (T - 1 - i[:, None] + torch.arange(T, device="cuda")[None, :]).expand(8, -1, -1)
+        scores = heads(qu[i]) @ K.transpose(1, 2) + band.gather(2, idx)
+        ref = (torch.softmax(scores / 128**0.5, -1) @ V).transpose(0, 1).reshape(len(i), 1024)
+        worst = max(worst, max_rel(out[i].float().cpu(), ref.cpu()))
+    assert worst < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
 def test_depthwise_conv_silu(L, dtype):
     t3 = [1, 5, 9, 40, 3]
     b, keep, off = batch_for(L, t3, 32)
