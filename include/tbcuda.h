@@ -150,6 +150,10 @@ typedef struct tb_model {
   const float* mel_w;       /* packed non-zero filter weights */
   const int* mel_start;     /* [128] first FFT bin of each filter */
   const int* mel_off;       /* [129] offsets of each filter's weights in mel_w */
+  /* persistent decoder (bf16): layer 0's LSTM split in its two inputs */
+  const void* lstm0_hh;     /* [2560, 640]: the h columns of lstm_w[0] (its last 640), contiguous */
+  const float* lstm0_emb;   /* [8193, 2560] fp32: embedding . (the x columns of lstm_w[0])^T,
+                               the input term of layer 0's gates for every token */
 } tb_model;
 
 /* A batch of clips, packed end to end at every stage (no padding between clips).

@@ -48,6 +48,7 @@ class Model(C.Structure):
         ("embedding", vp), ("lstm_w", vp * 2), ("lstm_b", vp * 2), ("dec_proj_w", vp), ("dec_proj_b", vp),
         ("joint_w", vp), ("joint_b", vp),
         ("window", vp), ("mel_w", vp), ("mel_start", vp), ("mel_off", vp),
+        ("lstm0_hh", vp), ("lstm0_emb", vp),
     ]
 
 

@@ -17,6 +17,7 @@ struct DecodeWs {
   unsigned long long *keys, *keys2;
   void *z, *x0, *x1, *hp;
   float *c, *dec;  // LSTM cell state [2][lanes][640]; projector output
+  float* pre0;     // persistent decoder: [lanes][2560] W_hh0 . h0 + b0 for the next step
   int *frame, *it, *done, *mask, *count, *active;
   int* erow;     // [lanes]: encoder row the joint reads next (enc_off + frame), -1 once done
   int* m_chunk;  // [DECODE_MAX_CHUNKS]: only lanes below this index can run in chunk c
@@ -43,6 +44,7 @@ inline DecodeWs carve(void* ws, int dtype, int lanes) {
   w.hp = take(L * TB_PRED * e);
   w.c = (float*)take(2 * L * TB_PRED * 4);
   w.dec = (float*)take(L * TB_PRED * 4);
+  w.pre0 = (float*)take(L * 4 * TB_PRED * 4);
   w.frame = (int*)take(L * 4);
   w.it = (int*)take(L * 4);
   w.done = (int*)take(L * 4);
@@ -93,17 +95,15 @@ __device__ __forceinline__ void lane_init(const DecodeWs& w, const T* __restrict
   }
 }
 
-// One iteration of the greedy loop for lane l (one warp): reads the joint's argmax
-// keys (and clears them for the next joint), then blank -> frame += max(d, 1);
-// otherwise emit, stop on EOS, else frame += d and the LSTM steps on the token; the
-// lane stops when frame >= valid or after cap[l] iterations. A lane that steps gets its
-// LSTM inputs [embedding(token) | h0] and [. | h1] assembled from the hidden states the
-// LSTM epilogues last wrote for it: h0 in x1[:, :640], h1 in hp.
-// Returns (on every lane of the warp) whether lane l is still running.
-template <typename T>
-__device__ __forceinline__ bool lane_step(const DecodeWs& w, const T* __restrict__ emb,
-                                          const int* __restrict__ enc_off, const int* __restrict__ cap, int l,
-                                          int lanes, int max_cap, int* __restrict__ tokens, int lane) {
+// One iteration of the greedy loop for lane l (one warp, lane 0 does the work): reads
+// the joint's argmax keys (and clears them for the next joint), then blank ->
+// frame += max(d, 1); otherwise emit, stop on EOS, else frame += d and the LSTM steps on
+// the token; the lane stops when frame >= valid or after cap[l] iterations. On every
+// lane of the warp: returns whether lane l still runs, and sets `step` (the LSTM steps)
+// and `tok`.
+__device__ __forceinline__ bool lane_scalar_step(const DecodeWs& w, const int* __restrict__ enc_off,
+                                                 const int* __restrict__ cap, int l, int max_cap,
+                                                 int* __restrict__ tokens, int lane, int& step_out, int& tok_out) {
   int step = 0, tok = 0, running = 0;
   if (lane == 0) {
     // Every scalar the step needs, loaded at once (one memory round trip), then used.
@@ -144,10 +144,22 @@ __device__ __forceinline__ bool lane_step(const DecodeWs& w, const T* __restrict
     }
     w.mask[l] = step;
   }
-  step = __shfl_sync(0xffffffffu, step, 0);
-  tok = __shfl_sync(0xffffffffu, tok, 0);
-  running = __shfl_sync(0xffffffffu, running, 0);
-  if (!step) return running != 0;
+  step_out = __shfl_sync(0xffffffffu, step, 0);
+  tok_out = __shfl_sync(0xffffffffu, tok, 0);
+  return __shfl_sync(0xffffffffu, running, 0) != 0;
+}
+
+// The loop body (lane_scalar_step) and, for a lane that steps, its LSTM inputs
+// [embedding(token) | h0] and [. | h1] assembled from the hidden states the LSTM
+// epilogues last wrote for it: h0 in x1[:, :640], h1 in hp. Returns whether lane l
+// still runs.
+template <typename T>
+__device__ __forceinline__ bool lane_step(const DecodeWs& w, const T* __restrict__ emb,
+                                          const int* __restrict__ enc_off, const int* __restrict__ cap, int l,
+                                          int lanes, int max_cap, int* __restrict__ tokens, int lane) {
+  int step, tok;
+  const bool running = lane_scalar_step(w, enc_off, cap, l, max_cap, tokens, lane, step, tok);
+  if (!step) return running;
   T* __restrict__ x0 = reinterpret_cast<T*>(w.x0) + (long long)l * 2 * TB_PRED;
   T* __restrict__ x1 = reinterpret_cast<T*>(w.x1) + (long long)l * 2 * TB_PRED;
   const T* __restrict__ er = emb + (long long)tok * TB_PRED;
@@ -170,7 +182,7 @@ __device__ __forceinline__ bool lane_step(const DecodeWs& w, const T* __restrict
     store4(x0 + TB_PRED + j, a4[i].x, a4[i].y, a4[i].z, a4[i].w);
     store4(x1 + TB_PRED + j, b4[i].x, b4[i].y, b4[i].z, b4[i].w);
   }
-  return true;
+  return running;
 }
 
 }  // namespace tb

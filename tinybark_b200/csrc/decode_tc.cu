@@ -4,22 +4,29 @@
 // of tinybark/tinygrad/model.py:162-233 (one clip and one host round trip per token in
 // the reference) for a batch of clips, one lane per clip, all lanes stepped together.
 //
+// Layer 0 of the LSTM is split in its two inputs: its gates are E[token] + P0, with
+// E = embedding . W_ih0^T precomputed for every token (tb_model.lstm0_emb) and
+// P0 = W_hh0 . h0 + b0 computed one iteration ahead, from the h0 the cell just made.
+// That leaves no GEMM between the argmax and layer 1:
+//
 // Phases (q counts them from 0; every CTA takes part in every phase):
-//   q = 0             INIT   lane state, the first step's inputs (token blank)
-//   q = 1, 2, 3       LSTM0, LSTM1, PROJ of the first prediction step
-//   q = 4 + 5i + r    iteration i: r = 0 JOINT, 1 STEP, 2 LSTM0, 3 LSTM1, 4 PROJ
-// JOINT   z [lanes x 640] . joint_w^T [8448 x 640] -> per-lane argmax keys (BN = 256)
-// STEP    the loop body per lane (lane_step): token, duration, frame, stop; the LSTM
-//         inputs of lanes that emitted a token
-// LSTM0/1 [emb | h] . W^T [2560 x 1280] with the LSTM cell in the epilogue (BN = 128)
-// PROJ    h1 . dec_proj^T [640 x 640] -> dec, and z = relu(enc[frame] + dec) (BN = 64)
+//   q = 0             INIT   lane state, h = 0, P0 = b0
+//   q = 1, 2, 3       CELL, LSTM, PROJ of the first prediction step (token blank)
+//   q = 4 + 4i + r    iteration i: r = 0 JOINT, 1 CELL, 2 LSTM, 3 PROJ
+// JOINT  z [lanes x 640] . joint_w^T [8448 x 640] -> per-lane argmax keys (BN = 256)
+// CELL   per lane (one warp): the loop body (lane_scalar_step: token, duration, frame,
+//        stop) and, for a lane that emitted a token, the layer-0 cell from E[token] + P0:
+//        c0 and h0 (into x1[:, :640]), and h1 (hp) copied into x1[:, 640:]
+// LSTM   layer 1: x1 . W1^T [2560 x 1280] with the cell in the epilogue (BN = 128), and
+//        on the SMs it leaves idle, the next P0 = x1[:, :640] . W_hh0^T + b0
+// PROJ   hp . dec_proj^T [640 x 640] -> dec, and z = relu(enc[frame] + dec) (BN = 64)
 // The GEMM phases use the tcgen05 pipeline of the GEMM kernel (gemm.cu): warp 0 loads
-// A and W tiles with TMA into a 4-stage ring, warp 1 issues the MMAs into one of two
-// tensor-memory accumulators, warps 2-5 run the epilogue (tcgemm.cuh) and the
-// INIT/STEP work. Tile t of a phase goes to CTA t mod gridDim.
+// A and W tiles with TMA into a shared-memory ring, warp 1 issues the MMAs into one of
+// two tensor-memory accumulators, warps 2-5 run the epilogue (tcgemm.cuh) and the
+// INIT/CELL work.
 //
 // Each iteration only covers lanes below the row bound M_i = 1 + the last lane still
-// running after STEP i (lanes are ordered longest first, so M shrinks as clips end);
+// running after CELL i (lanes are ordered longest first, so M shrinks as clips end);
 // the loop ends when no lane runs. The barrier is a global arrival counter: after a
 // phase every CTA adds 1, and phase q starts once the counter reaches q * gridDim.
 // Every wait is bounded (TB_WAIT_NS): a CTA that gives up sets TB_DEV_DECODE_TIMEOUT in
@@ -39,14 +46,15 @@ constexpr int DT_OUT_BYTES = 4 * 32 * TC_OUT_STRIDE * 4;
 constexpr int DT_SMEM = 1024 + DT_RING_BYTES + DT_OUT_BYTES + 256;
 constexpr int DT_ACC_COLS = 256;  // tensor-memory columns per accumulator
 
-enum { G_JOINT = 0, G_LSTM0 = 1, G_LSTM1 = 2, G_PROJ = 3 };
-enum { P_INIT = 0, P_STEP = 1, P_GEMM = 2 };
+enum { G_JOINT = 0, G_LSTM1 = 1, G_PRE0 = 2, G_PROJ = 3 };
+enum { P_INIT = 0, P_CELL = 1, P_JOINT = 2, P_LSTM = 3, P_PROJ = 4 };
 
 struct DecodeTcArgs {
-  CUtensorMap a[4], w[4];  // A operand and weights of the joint, LSTM0, LSTM1 and projector
+  CUtensorMap a[4], w[4];  // A operand and weights of the joint, LSTM1, next-P0 and projector GEMMs
   tb_epilogue e[4];
   DecodeWs ws;
-  const __nv_bfloat16* emb;
+  const float* emb_gates;  // [8193, 2560] E = embedding . W_ih0^T
+  const float* b0;         // [2560] layer 0's bias
   const int* enc_off;
   const int* cap;
   int lanes, max_cap, max_iters;
@@ -55,7 +63,7 @@ struct DecodeTcArgs {
 };
 
 __host__ __device__ constexpr int gemm_n(int g) { return g == G_JOINT ? TB_JOINT_ROWS : (g == G_PROJ ? TB_PRED : 4 * TB_PRED); }
-__host__ __device__ constexpr int gemm_k(int g) { return g == G_JOINT || g == G_PROJ ? TB_PRED : 2 * TB_PRED; }
+__host__ __device__ constexpr int gemm_k(int g) { return g == G_LSTM1 ? 2 * TB_PRED : TB_PRED; }
 __host__ __device__ constexpr int gemm_bn(int g) { return g == G_JOINT ? 256 : (g == G_PROJ ? 64 : 128); }
 // The shared-memory ring is re-cut at every GEMM phase into as many stages of that
 // phase's tile size as fit (4 x 48 KB joint, 6 x 32 KB LSTM, 8 x 24 KB projector): the
@@ -67,27 +75,62 @@ __host__ __device__ constexpr int ring_slots(int g) {
 }
 
 struct Phase {
-  int kind;  // P_INIT, P_STEP or P_GEMM
-  int gemm;  // G_* for P_GEMM
+  int kind;  // P_*
   int iter;  // greedy-loop iteration (-1 for the first prediction step)
 };
 
 __device__ __forceinline__ Phase phase_of(int q) {
-  if (q == 0) return {P_INIT, 0, -1};
-  if (q < 4) return {P_GEMM, q, -1};  // LSTM0, LSTM1, PROJ
-  const int i = (q - 4) / 5, r = (q - 4) % 5;
-  if (r == 0) return {P_GEMM, G_JOINT, i};
-  if (r == 1) return {P_STEP, 0, i};
-  return {P_GEMM, r - 1, i};
+  if (q == 0) return {P_INIT, -1};
+  if (q < 4) return {q == 1 ? P_CELL : (q == 2 ? P_LSTM : P_PROJ), -1};
+  const int i = (q - 4) / 4, r = (q - 4) % 4;
+  return {r == 0 ? P_JOINT : (r == 1 ? P_CELL : (r == 2 ? P_LSTM : P_PROJ)), i};
 }
 
-// Rows a phase covers: JOINT and STEP of iteration i read M_{i-1}, the rest M_i. Each
-// bound is written during one STEP phase and read only after its barrier, so every
+// Rows a phase covers: JOINT and CELL of iteration i read M_{i-1}, the rest M_i. Each
+// bound is written during one CELL phase and read only after its barrier, so every
 // role of every CTA reads the same value, however late it reads it.
 __device__ __forceinline__ int phase_rows(const Phase& p, const int* bounds) {
   if (p.kind == P_INIT) return 0;
-  const int i = (p.kind == P_STEP || p.gemm == G_JOINT) ? p.iter - 1 : p.iter;
+  if (p.iter < 0) return bounds[0];
+  const int i = (p.kind == P_CELL || p.kind == P_JOINT) ? p.iter - 1 : p.iter;
   return bounds[i + 1];
+}
+
+// The k-th GEMM tile of this CTA in a phase, as (gemm, m tile, n tile); false if none.
+// JOINT and PROJ: tile t = cta + k * gridDim. LSTM: layer 1's tiles (the critical path)
+// go one per CTA, and the next-P0 tiles (half the work each) to the CTAs left over, at
+// most two per CTA; with too few CTAs left, both lists are dealt round-robin.
+__device__ __forceinline__ bool phase_tile(int kind, int rows, int cta, int G, int k, int& g, int& mt, int& nt) {
+  const int mtiles = (rows + 127) / 128;
+  if (kind == P_JOINT || kind == P_PROJ) {
+    g = kind == P_JOINT ? G_JOINT : G_PROJ;
+    const int ntc = gemm_n(g) / gemm_bn(g), t = cta + k * G;
+    if (t >= mtiles * ntc) return false;
+    mt = t / ntc;
+    nt = t % ntc;
+    return true;
+  }
+  const int ntc = gemm_n(G_LSTM1) / gemm_bn(G_LSTM1), t1 = mtiles * ntc, free = G - t1;
+  int t;
+  if (free > 0 && (t1 + free - 1) / free <= 2) {
+    if (cta < t1) {
+      if (k > 0) return false;
+      g = G_LSTM1;
+      t = cta;
+    } else {
+      t = (cta - t1) + k * free;
+      if (t >= t1) return false;
+      g = G_PRE0;
+    }
+  } else {
+    t = cta + k * G;
+    if (t >= 2 * t1) return false;
+    g = t < t1 ? G_LSTM1 : G_PRE0;
+    if (t >= t1) t -= t1;
+  }
+  mt = t / ntc;
+  nt = t % ntc;
+  return true;
 }
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -157,7 +200,91 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
   return r != 0;
 }
 
-__device__ __forceinline__ int tiles_of(int g, int rows) { return ((rows + 127) / 128) * (gemm_n(g) / gemm_bn(g)); }
+// The ring's stage size in a GEMM phase (both LSTM-phase GEMMs have BN = 128).
+__device__ __forceinline__ int phase_stage_gemm(int kind) {
+  return kind == P_JOINT ? G_JOINT : (kind == P_PROJ ? G_PROJ : G_LSTM1);
+}
+
+// Lane l's state before the first step: zero LSTM state (h0, h1 in x1, c), P0 = b0 (its
+// value at h0 = 0), counters. One warp per lane.
+__device__ __forceinline__ void lane_init_tc(const DecodeTcArgs& args, int l, int lane) {
+  const DecodeWs& w = args.ws;
+  const long long L = args.lanes;
+  __nv_bfloat16* x1 = reinterpret_cast<__nv_bfloat16*>(w.x1) + (long long)l * 2 * TB_PRED;
+  for (int j = lane; j < TB_PRED; j += 32) {
+    w.c[l * TB_PRED + j] = 0.f;
+    w.c[(L + l) * TB_PRED + j] = 0.f;
+  }
+  for (int j = lane; j < 2 * TB_PRED; j += 32) x1[j] = __float2bfloat16_rn(0.f);
+  float* p0 = w.pre0 + (long long)l * 4 * TB_PRED;
+  for (int j = lane; j < 4 * TB_PRED; j += 32) p0[j] = args.b0[j];
+  if (lane == 0) {
+    const int valid = args.enc_off[l + 1] - args.enc_off[l];
+    const int done = (valid <= 0 || args.cap[l] <= 0) ? 1 : 0;
+    w.frame[l] = 0;
+    w.it[l] = 0;
+    w.count[l] = 0;
+    w.done[l] = done;
+    w.mask[l] = 1;
+    w.keys[l] = 0ull;
+    w.keys2[l] = 0ull;
+    w.erow[l] = done ? -1 : args.enc_off[l];
+  }
+}
+
+// The loop body for lane l (one warp) and, for a lane that emitted a token, layer 0's
+// cell from E[token] + P0 (the first prediction step, iter < 0, feeds the blank token to
+// every lane still running). Returns whether the lane still runs.
+__device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int iter, int lane) {
+  const DecodeWs& w = args.ws;
+  int step, tok;
+  bool running;
+  if (iter < 0) {
+    running = !w.done[l];
+    step = running;
+    tok = TB_BLANK;
+  } else {
+    running = lane_scalar_step(w, args.enc_off, args.cap, l, args.max_cap, args.tokens, lane, step, tok);
+  }
+  if (!step) return running;
+  const long long L = args.lanes;
+  const float4* __restrict__ eg = reinterpret_cast<const float4*>(args.emb_gates + (long long)tok * 4 * TB_PRED);
+  const float4* __restrict__ p0 = reinterpret_cast<const float4*>(w.pre0 + (long long)l * 4 * TB_PRED);
+  float* __restrict__ c0 = w.c + (long long)l * TB_PRED;
+  __nv_bfloat16* __restrict__ x1 = reinterpret_cast<__nv_bfloat16*>(w.x1) + (long long)l * 2 * TB_PRED;
+  const __nv_bfloat16* __restrict__ hp = reinterpret_cast<const __nv_bfloat16*>(w.hp) + (long long)l * TB_PRED;
+  float4 ge[TB_PRED / 32], gp[TB_PRED / 32];
+  float cv[TB_PRED / 32];
+#pragma unroll
+  for (int k = 0; k < TB_PRED / 32; ++k) {
+    const int u = k * 32 + lane;
+    ge[k] = eg[u];
+    gp[k] = p0[u];
+    cv[k] = c0[u];
+  }
+  // h1 (from the last layer-1 cell) into layer 1's next input; at the first step it is
+  // the zero that INIT wrote there.
+  uint2 h1v[TB_PRED / 128];
+  if (iter >= 0) {
+#pragma unroll
+    for (int k = 0; k < TB_PRED / 128; ++k) h1v[k] = reinterpret_cast<const uint2*>(hp)[k * 32 + lane];
+  }
+#pragma unroll
+  for (int k = 0; k < TB_PRED / 32; ++k) {
+    const int u = k * 32 + lane;
+    const float ig = sigmoid_mufu(ge[k].x + gp[k].x), fg = sigmoid_mufu(ge[k].y + gp[k].y);
+    const float gg = tanh_mufu(ge[k].z + gp[k].z), og = sigmoid_mufu(ge[k].w + gp[k].w);
+    const float c = fg * cv[k] + ig * gg;
+    c0[u] = c;
+    x1[u] = __float2bfloat16_rn(og * tanh_mufu(c));
+  }
+  if (iter >= 0) {
+#pragma unroll
+    for (int k = 0; k < TB_PRED / 128; ++k) reinterpret_cast<uint2*>(x1 + TB_PRED)[k * 32 + lane] = h1v[k];
+  }
+  (void)L;
+  return running;
+}
 
 }  // namespace
 
@@ -194,7 +321,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
   // Phases run while q < q_end; the last iteration ends after its STEP.
-  const int q_end = 4 + 5 * args.max_iters;
+  const int q_end = 4 + 4 * args.max_iters;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -210,19 +337,18 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         post_phase(&bars->phase, (unsigned)q);
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;  // no lane runs: the loop is over
-        if (p.kind != P_GEMM) continue;
-        const int g = p.gemm, bn = gemm_bn(g), nt_count = gemm_n(g) / bn, kb_count = gemm_k(g) / 64;
-        const int sb = stage_bytes(g), slots = ring_slots(g), tiles = tiles_of(g, rows);
-        int s = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += G) {
-          const int mt = t / nt_count, nt = t % nt_count;
+        if (p.kind == P_CELL) continue;
+        const int sg = phase_stage_gemm(p.kind), sb = stage_bytes(sg), slots = ring_slots(sg);
+        int s = 0, g, mt, nt;
+        for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, g, mt, nt); ++k) {
+          const int bn = gemm_bn(g), kb_count = gemm_k(g) / 64;
           for (int kb = 0; kb < kb_count; ++kb) {
             if (!mbar_wait(&bars->empty[s], ((use >> s) & 1) ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
               ok = false;
               break;
             }
             uint8_t* sa = smem + s * sb;
-            mbar_expect_tx(&bars->full[s], sb);
+            mbar_expect_tx(&bars->full[s], DT_A_BYTES + bn * 64 * 2);
             tma_load_2d(sa, &args.a[g], &bars->full[s], kb * 64, mt * 128);
             tma_load_2d(sa + DT_A_BYTES, &args.w[g], &bars->full[s], kb * 64, nt * bn);
             use ^= 1u << s;
@@ -246,12 +372,12 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         if (!cta_phase_wait(&bars->phase, (unsigned)q, err, abort, sync)) break;
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;
-        if (p.kind != P_GEMM) continue;
-        const int g = p.gemm, kb_count = gemm_k(g) / 64, sb = stage_bytes(g), slots = ring_slots(g);
-        const uint32_t idesc = g == G_JOINT ? idesc_bf16(128, 256) : (g == G_PROJ ? idesc_bf16(128, 64) : idesc_bf16(128, 128));
-        const int tiles = tiles_of(g, rows);
-        int s = 0;
-        for (int t = blockIdx.x; t < tiles && ok; t += G) {
+        if (p.kind == P_CELL) continue;
+        const int sg = phase_stage_gemm(p.kind), sb = stage_bytes(sg), slots = ring_slots(sg);
+        int s = 0, g, mt, nt;
+        for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, g, mt, nt); ++k) {
+          const int kb_count = gemm_k(g) / 64;
+          const uint32_t idesc = g == G_JOINT ? idesc_bf16(128, 256) : (g == G_PROJ ? idesc_bf16(128, 64) : idesc_bf16(128, 128));
           if (!mbar_wait(&bars->tempty[acc], acc_ph ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
             ok = false;
             break;
@@ -267,7 +393,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
             const uint32_t sa = smem_u32(smem + s * sb);
             const uint64_t ad = sdesc_sw128(sa), bd = sdesc_sw128(sa + DT_A_BYTES);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            for (int k4 = 0; k4 < 4; ++k4) umma_f16(d, ad + 2 * k4, bd + 2 * k4, idesc, (kb | k4) != 0);
             umma_commit(&bars->empty[s]);
             use ^= 1u << s;
             if (++s == slots) s = 0;
@@ -283,7 +409,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
       drain_wait(&bars->done, 0);
     }
   } else {
-    const int ew = warp - 2;   // epilogue warp 0..3
+    const int ew = warp - 2;       // epilogue warp 0..3
     const int quarter = warp & 3;  // tensor-memory lane quarter this warp may access
     float* stage = out_stage + quarter * 32 * TC_OUT_STRIDE;
     int acc = 0;
@@ -299,18 +425,14 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         if (rows <= 0) break;
       }
       if (p.kind == P_INIT) {
-        for (int l = blockIdx.x * 4 + ew; l < args.lanes; l += G * 4)
-          lane_init<__nv_bfloat16>(w, args.emb, args.enc_off, args.cap, l, args.lanes, lane);
-      } else if (p.kind == P_STEP) {
+        for (int l = blockIdx.x * 4 + ew; l < args.lanes; l += G * 4) lane_init_tc(args, l, lane);
+      } else if (p.kind == P_CELL) {
         for (int l = blockIdx.x * 4 + ew; l < rows; l += G * 4)
-          if (lane_step<__nv_bfloat16>(w, args.emb, args.enc_off, args.cap, l, args.lanes, args.max_cap,
-                                       args.tokens, lane) &&
-              lane == 0)
-            atomicMax(bounds + p.iter + 1, l + 1);
+          if (lane_cell(args, l, p.iter, lane) && p.iter >= 0 && lane == 0) atomicMax(bounds + p.iter + 1, l + 1);
       } else {
-        const int g = p.gemm, tiles = tiles_of(g, rows), nt_count = gemm_n(g) / gemm_bn(g);
-        for (int t = blockIdx.x; t < tiles; t += G) {
-          const int row0 = (t / nt_count) * 128 + quarter * 32, n0 = (t % nt_count) * gemm_bn(g);
+        int g, mt, nt;
+        for (int k = 0; phase_tile(p.kind, rows, blockIdx.x, G, k, g, mt, nt); ++k) {
+          const int row0 = mt * 128 + quarter * 32, n0 = nt * gemm_bn(g);
           const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + acc * DT_ACC_COLS;
           if (ok) {
             // Constant indices: the epilogue's operands are then read straight from the
@@ -321,12 +443,12 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
             else if (g == G_PROJ)
               ok = epilogue_tile<64, TB_EPI_JOINT_IN>(args.e[G_PROJ], stage, taddr, row0, n0, lane, rows,
                                                       &bars->tfull[acc], acc_ph, err, abort);
-            else if (g == G_LSTM0)
-              ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM0], stage, taddr, row0, n0, lane, rows,
-                                                   &bars->tfull[acc], acc_ph, err, abort);
-            else
+            else if (g == G_LSTM1)
               ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM1], stage, taddr, row0, n0, lane, rows,
                                                    &bars->tfull[acc], acc_ph, err, abort);
+            else
+              ok = epilogue_tile<128, TB_EPI_STORE>(args.e[G_PRE0], stage, taddr, row0, n0, lane, rows,
+                                                    &bars->tfull[acc], acc_ph, err, abort);
           }
           tc_fence_before();
           __syncwarp();
@@ -360,7 +482,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
 int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                   int* tokens, int* counts, void* ws, size_t ws_bytes, int* err, cudaStream_t stream) {
   if (lanes <= 0) return TB_OK;
-  if (m.dtype != TB_BF16) return TB_ERR_ARG;
+  if (m.dtype != TB_BF16 || !m.lstm0_hh || !m.lstm0_emb) return TB_ERR_ARG;
   if (!enc || !enc_off || !cap || !tokens || !counts || !ws || max_cap <= 0) return TB_ERR_ARG;
   if (ws_bytes < decode_ws(TB_BF16, lanes)) return TB_ERR_WORKSPACE;
   static bool configured[64] = {};
@@ -380,11 +502,13 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   DecodeTcArgs args = {};
   DecodeWs& w = args.ws;
   w = carve(ws, TB_BF16, lanes);
-  // A operands [lanes x K] and weights [N x K], 64-column boxes of 128 rows (A) or BN rows (W).
-  const void* a_ptr[4] = {w.z, w.x0, w.x1, w.hp};
-  const void* w_ptr[4] = {m.joint_w, m.lstm_w[0], m.lstm_w[1], m.dec_proj_w};
+  // A operands [lanes x K] and weights [N x K], 64-column boxes of 128 rows (A) or BN rows
+  // (W). The next-P0 GEMM reads the h0 half of layer 1's input x1.
+  const void* a_ptr[4] = {w.z, w.x1, w.x1, w.hp};
+  const long long a_ld[4] = {TB_PRED, 2 * TB_PRED, 2 * TB_PRED, TB_PRED};
+  const void* w_ptr[4] = {m.joint_w, m.lstm_w[1], m.lstm0_hh, m.dec_proj_w};
   for (int g = 0; g < 4; ++g) {
-    if (!encode_tmap_2d(&args.a[g], a_ptr[g], lanes, gemm_k(g), gemm_k(g), 64, 128) ||
+    if (!encode_tmap_2d(&args.a[g], a_ptr[g], lanes, gemm_k(g), a_ld[g], 64, 128) ||
         !encode_tmap_2d(&args.w[g], w_ptr[g], gemm_n(g), gemm_k(g), gemm_k(g), 64, gemm_bn(g)))
       return TB_ERR_CUDA;
   }
@@ -395,16 +519,20 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   jt.keys2 = w.keys2;
   jt.split = TB_TOKEN_ROWS;
   jt.split_end = TB_TOKEN_ROWS + TB_DURATIONS;
-  for (int layer = 0; layer < 2; ++layer) {
-    tb_epilogue& e = args.e[G_LSTM0 + layer];
-    e.kind = TB_EPI_LSTM;
-    e.out_dtype = TB_BF16;
-    e.bias = m.lstm_b[layer];
-    e.c = w.c + (long long)layer * lanes * TB_PRED;
-    e.mask = w.mask;
-    e.out = layer == 0 ? w.x1 : w.hp;  // h0 -> first half of layer 1's input; h1 -> the projector's input
-    e.ldo = layer == 0 ? 2 * TB_PRED : TB_PRED;
-  }
+  tb_epilogue& l1 = args.e[G_LSTM1];
+  l1.kind = TB_EPI_LSTM;
+  l1.out_dtype = TB_BF16;
+  l1.bias = m.lstm_b[1];
+  l1.c = w.c + (long long)lanes * TB_PRED;
+  l1.mask = w.mask;
+  l1.out = w.hp;  // h1 -> the projector's input
+  l1.ldo = TB_PRED;
+  tb_epilogue& p0 = args.e[G_PRE0];
+  p0.kind = TB_EPI_STORE;
+  p0.out_dtype = TB_F32;
+  p0.out = w.pre0;
+  p0.ldo = 4 * TB_PRED;
+  p0.bias = m.lstm_b[0];
   tb_epilogue& pj = args.e[G_PROJ];
   pj.kind = TB_EPI_JOINT_IN;
   pj.out_dtype = TB_BF16;
@@ -415,7 +543,8 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   pj.bias = m.dec_proj_b;
   pj.gather = enc;
   pj.gather_row = w.erow;
-  args.emb = reinterpret_cast<const __nv_bfloat16*>(m.embedding);
+  args.emb_gates = m.lstm0_emb;
+  args.b0 = m.lstm_b[0];
   args.enc_off = enc_off;
   args.cap = cap;
   args.lanes = lanes;

@@ -79,7 +79,12 @@ def plan_arrays(frames, sub_rows: int, attn_rows: int) -> dict[str, np.ndarray]:
     off = lambda n: np.concatenate([[0], np.cumsum(n)]).astype(np.int32)
     ids = np.arange(len(f), dtype=np.int32)
     order = np.argsort(-t3, kind="stable")
-    tiles = lambda n, step: np.array([(c, r) for c in order for r in range(0, int(n[c]), step)], np.int32).reshape(-1)
+    def tiles(n, step):  # (clip, first row) of every `step`-row work item, clips in `order`
+        per = (n[order] + step - 1) // step
+        clip = np.repeat(order, per)
+        first = np.arange(int(per.sum())) - np.repeat(np.cumsum(per) - per, per)
+        return np.stack([clip, first * step], 1).astype(np.int32).reshape(-1)
+
     return {
         "frames": f, "t3": t3,
         "frame_off": off(f), "t1_off": off(t1), "t2_off": off(t2), "t3_off": off(t3),
@@ -105,6 +110,9 @@ class Engine:
         self.layers = config["encoder_config"]["num_hidden_layers"]
         self.sub_rows, self.attn_rows = L.tile_rows(self.dtype)
         self._keep: list[torch.Tensor] = []
+        self._pinned: torch.Tensor | None = None  # sample staging buffer of upload()
+        self._staged = None  # event after the last copy out of it
+        self._threads = None
         with torch.cuda.device(self.device):
             self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.host_flag = torch.zeros(2 * MAX_DECODE_GROUPS, dtype=torch.int32).pin_memory()
@@ -172,13 +180,26 @@ class Engine:
         m.enc_proj_w = _ptr(self._mat(w["encoder_projector.weight"]))
         m.enc_proj_b = _ptr(self._vec(w["encoder_projector.bias"]))
 
-        m.embedding = _ptr(self._mat(w["decoder.embedding.weight"]))
+        emb = self._mat(w["decoder.embedding.weight"])
+        m.embedding = _ptr(emb)
         for l in range(2):
             # Gates side by side per unit: row 4u+g is gate g (i, f, g, o) of unit u.
             wl = w[f"decoder.lstm.weight_l{l}"].reshape(4, L.PRED, 2 * L.PRED).transpose(1, 0, 2).reshape(4 * L.PRED, -1)
             bl = w[f"decoder.lstm.bias_l{l}"].reshape(4, L.PRED).T.reshape(-1)
             m.lstm_w[l] = _ptr(self._mat(wl))
             m.lstm_b[l] = _ptr(self._vec(bl))
+            if l == 0 and self.dtype == L.BF16:
+                # The persistent decoder takes layer 0's gates as E[token] + W_hh . h0: the
+                # input term of every token, E = embedding . W_ih^T, computed once here.
+                m.lstm0_hh = _ptr(self._mat(wl[:, L.PRED :]))
+                w_ih = torch.from_numpy(np.ascontiguousarray(wl[:, : L.PRED], np.float32)).to(self.device, self.tdtype)
+                table = torch.empty(L.VOCAB, 4 * L.PRED, device=self.device, dtype=torch.float32)
+                self._keep.append(table)
+                from . import kernels
+
+                kernels.gemm(emb, w_ih, L.Epilogue(kind=L.EPI_STORE, out_dtype=L.F32, out=table.data_ptr(),
+                                                   ldo=4 * L.PRED))
+                m.lstm0_emb = _ptr(table)
         m.dec_proj_w = _ptr(self._mat(w["decoder.decoder_projector.weight"]))
         m.dec_proj_b = _ptr(self._vec(w["decoder.decoder_projector.bias"]))
         joint = np.zeros((L.JOINT_ROWS, L.PRED), np.float32)
@@ -306,16 +327,39 @@ class Engine:
     # ------------------------------------------------------------------ end to end
 
     def upload(self, clips: list[np.ndarray]) -> tuple[torch.Tensor, torch.Tensor]:
-        """Packs float32 sample arrays into one pinned buffer and copies it to the device."""
+        """Packs float32 sample arrays into the engine's pinned staging buffer (kept and
+        grown across calls: pinning memory is slow) with a few host threads, and copies
+        it to the device in one transfer."""
         sizes = np.array([len(c) for c in clips], np.int64)
         off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
-        host = torch.empty(int(off[-1]), dtype=torch.float32).pin_memory()
-        hv = host.numpy()
-        for c, s in zip(clips, off[:-1]):
-            hv[s : s + len(c)] = c
-        samples = host.to(self.device, non_blocking=True)
+        total = int(off[-1])
+        if self._staged is not None:
+            self._staged.synchronize()  # the previous transfer out of the buffer is done
+        if self._pinned is None or self._pinned.numel() < total + 1:
+            self._pinned = torch.empty(max(total + 1, int(total * 1.25)), dtype=torch.float32).pin_memory()
+        hv = self._pinned.numpy()
+        hv[total] = 0.0
+
+        def pack(i: int) -> None:
+            hv[off[i] : off[i + 1]] = clips[i]
+
+        if total >= 1 << 22:
+            list(self._pool().map(pack, range(len(clips))))
+        else:
+            for i in range(len(clips)):
+                pack(i)
+        samples = self._pinned[:total].to(self.device, non_blocking=True)
+        self._staged = torch.cuda.Event()
+        self._staged.record()
         sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
         return samples, sample_off
+
+    def _pool(self):
+        if self._threads is None:
+            from concurrent.futures import ThreadPoolExecutor
+
+            self._threads = ThreadPoolExecutor(max_workers=8)
+        return self._threads
 
     def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
         """Token ids of every clip (16 kHz mono float32 samples), as the reference's
