@@ -11,6 +11,13 @@ namespace tb {
 constexpr int DW_ROWS = 32;  // output frames per block
 constexpr int DW_HALO = TB_KERNEL / 2;
 
+// SiLU: exact for the fp32 parity path, one MUFU operation for bf16.
+template <typename T>
+__device__ __forceinline__ float act(float x) {
+  if constexpr (sizeof(T) == 4) return siluf_(x);
+  return fast_silu(x);
+}
+
 template <typename T> struct Pair;
 template <> struct Pair<float> {
   static __device__ __forceinline__ float2 load(const float* p) { return *reinterpret_cast<const float2*>(p); }
@@ -55,7 +62,7 @@ __global__ void __launch_bounds__(256) depthwise_silu_kernel(const T* __restrict
       float acc_a = ba, acc_b = bb;
 #pragma unroll
       for (int k = 0; k < TB_KERNEL; ++k) acc_a = fmaf(ta[k], ia[i + k], acc_a), acc_b = fmaf(tb[k], ib[i + k], acc_b);
-      Pair<T>::store(y + (long long)(r0 + i) * TB_HIDDEN + c, fast_silu(acc_a), fast_silu(acc_b));
+      Pair<T>::store(y + (long long)(r0 + i) * TB_HIDDEN + c, act<T>(acc_a), act<T>(acc_b));
     }
   } else {
 #pragma unroll
@@ -70,7 +77,7 @@ __global__ void __launch_bounds__(256) depthwise_silu_kernel(const T* __restrict
         const int d = k - DW_HALO;
         if (d >= lo && d < hi) acc_a = fmaf(ta[k], ia[i + k], acc_a), acc_b = fmaf(tb[k], ib[i + k], acc_b);
       }
-      Pair<T>::store(y + (long long)r * TB_HIDDEN + c, fast_silu(acc_a), fast_silu(acc_b));
+      Pair<T>::store(y + (long long)r * TB_HIDDEN + c, act<T>(acc_a), act<T>(acc_b));
     }
   }
 }

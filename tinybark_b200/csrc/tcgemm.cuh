@@ -115,6 +115,27 @@ struct ChunkOps<TB_EPI_QKV> {
   }
 };
 
+// Stores the 8 row segments of a chunk (rows row0 + 4 it + sub, columns n .. n + 3) to
+// e.out in e.out_dtype, skipping rows >= M; the dtype test is made once, not per row.
+__device__ __forceinline__ void store_rows4(const tb_epilogue& e, const float4 (&v)[8], int row0, int sub, int n,
+                                            int M) {
+  if (e.out_dtype == TB_BF16) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M) store4(out + (long long)m * e.ldo + n, v[it].x, v[it].y, v[it].z, v[it].w);
+    }
+  } else {
+    float* out = reinterpret_cast<float*>(e.out);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m < M) store4(out + (long long)m * e.ldo + n, v[it].x, v[it].y, v[it].z, v[it].w);
+    }
+  }
+}
+
 // The epilogue of one warp's 32 x 32 chunk ci of a tile, staged row-major (stride
 // OUT_STRIDE) in `stage`: lane reads rows 4*it + lane/8 (it = 0..7), columns
 // 4*(lane%8) .. +3. row0: global row of the chunk's first row; n0: global column of its
@@ -130,53 +151,69 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
   if constexpr (EPI == TB_EPI_RESIDUAL) {
     float* out = reinterpret_cast<float*>(e.out);
     const float4* x = ops.x;
+    const float alpha = e.alpha;
+#pragma unroll
+    for (int it = 0; it < 8; ++it)
+      v[it] = make_float4(fmaf(alpha, v[it].x, x[it].x), fmaf(alpha, v[it].y, x[it].y), fmaf(alpha, v[it].z, x[it].z),
+                          fmaf(alpha, v[it].w, x[it].w));
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int m = row0 + it * 4 + sub;
-      if (m < M)
-        store4(out + (long long)m * e.ldo + n, x[it].x + e.alpha * v[it].x, x[it].y + e.alpha * v[it].y,
-               x[it].z + e.alpha * v[it].z, x[it].w + e.alpha * v[it].w);
+      if (m < M) store4(out + (long long)m * e.ldo + n, v[it].x, v[it].y, v[it].z, v[it].w);
     }
   } else if constexpr (EPI == TB_EPI_STORE || EPI == TB_EPI_BIAS_RELU) {
     const float4 b = ops.b;
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m >= M) continue;
-      float a0 = v[it].x + b.x, a1 = v[it].y + b.y, a2 = v[it].z + b.z, a3 = v[it].w + b.w;
-      if constexpr (EPI == TB_EPI_BIAS_RELU) a0 = fmaxf(a0, 0.f), a1 = fmaxf(a1, 0.f), a2 = fmaxf(a2, 0.f), a3 = fmaxf(a3, 0.f);
-      store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, a0, a1, a2, a3);
+      float4& a = v[it];
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+      if constexpr (EPI == TB_EPI_BIAS_RELU) a.x = fmaxf(a.x, 0.f), a.y = fmaxf(a.y, 0.f), a.z = fmaxf(a.z, 0.f), a.w = fmaxf(a.w, 0.f);
     }
+    store_rows4(e, v, row0, sub, n, M);
   } else if constexpr (EPI == TB_EPI_SILU) {
+    // All 32 activations first (independent chains the scheduler can interleave), then
+    // the stores.
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m < M)
-        store4_dt(e.out, (long long)m * e.ldo + n, e.out_dtype, fast_silu(v[it].x), fast_silu(v[it].y),
-                  fast_silu(v[it].z), fast_silu(v[it].w));
-    }
+    for (int it = 0; it < 8; ++it)
+      v[it] = make_float4(fast_silu(v[it].x), fast_silu(v[it].y), fast_silu(v[it].z), fast_silu(v[it].w));
+    store_rows4(e, v, row0, sub, n, M);
   } else if constexpr (EPI == TB_EPI_GLU) {
+    float2 g[8];
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m < M)
-        store2_dt(e.out, (long long)m * e.ldo + (n >> 1), e.out_dtype, v[it].x * fast_sigmoid(v[it].y),
-                  v[it].z * fast_sigmoid(v[it].w));
+    for (int it = 0; it < 8; ++it) g[it] = make_float2(v[it].x * fast_sigmoid(v[it].y), v[it].z * fast_sigmoid(v[it].w));
+    if (e.out_dtype == TB_BF16) {
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out);
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int m = row0 + it * 4 + sub;
+        if (m < M) store2(out + (long long)m * e.ldo + (n >> 1), g[it].x, g[it].y);
+      }
+    } else {
+      float* out = reinterpret_cast<float*>(e.out);
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int m = row0 + it * 4 + sub;
+        if (m < M) store2(out + (long long)m * e.ldo + (n >> 1), g[it].x, g[it].y);
+      }
     }
   } else if constexpr (EPI == TB_EPI_QKV) {
     const int sec = n >> 10, c = n & 1023;
     void* dst = sec == 0 ? e.out : (sec == 1 ? e.out3 : e.out4);
     (void)c;
     const float4 u = ops.u, w = ops.v;
+    if (sec == 0 && e.out2) {  // fp32 path: q + bias_v as well
+      float4 qv[8];
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int m = row0 + it * 4 + sub;
-      if (m >= M) continue;
-      const long long off = (long long)m * e.ldo + c;
-      store4_dt(dst, off, e.out_dtype, v[it].x + u.x, v[it].y + u.y, v[it].z + u.z, v[it].w + u.w);
-      if (sec == 0 && e.out2)
-        store4_dt(e.out2, off, e.out_dtype, v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
+      for (int it = 0; it < 8; ++it) qv[it] = make_float4(v[it].x + w.x, v[it].y + w.y, v[it].z + w.z, v[it].w + w.w);
+      tb_epilogue e2 = e;
+      e2.out = e.out2;
+      store_rows4(e2, qv, row0, sub, c, M);
     }
+#pragma unroll
+    for (int it = 0; it < 8; ++it) v[it] = make_float4(v[it].x + u.x, v[it].y + u.y, v[it].z + u.z, v[it].w + u.w);
+    tb_epilogue e1 = e;
+    e1.out = dst;
+    store_rows4(e1, v, row0, sub, c, M);
   } else if constexpr (EPI == TB_EPI_JOINT_IN) {
     constexpr int PX = EpiPre<EPI, BN>::PX;
     const float4 b = pre.b[ci];
