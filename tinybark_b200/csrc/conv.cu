@@ -8,7 +8,7 @@
 
 namespace tb {
 
-constexpr int DW_ROWS = 32;  // output frames per block
+constexpr int DW_ROWS = 16;  // output frames per block (registers allow two blocks per SM)
 constexpr int DW_HALO = TB_KERNEL / 2;
 
 // SiLU: exact for the fp32 parity path, one MUFU operation for bf16.
@@ -34,7 +34,7 @@ template <> struct Pair<__nv_bfloat16> {
 // block, DW_ROWS + 8 frames). Blocks whose frames and halo all lie in one clip (almost
 // all of them) skip the per-tap clip-boundary tests.
 template <typename T>
-__global__ void __launch_bounds__(256) depthwise_silu_kernel(const T* __restrict__ x, const float* __restrict__ w,
+__global__ void __launch_bounds__(256, 2) depthwise_silu_kernel(const T* __restrict__ x, const float* __restrict__ w,
                                                              const float* __restrict__ b,
                                                              const int* __restrict__ row_clip,
                                                              const int* __restrict__ off, int rows, T* __restrict__ y) {
