@@ -323,15 +323,25 @@ __global__ void __launch_bounds__(192, 1)
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     uint32_t r[32];
+    // This warp's window of the (bias_v - bias_u) . r term for key tile j, loaded one
+    // tile ahead so its latency hides behind the previous tile.
+    float cnext[WIN / 32];
+    auto load_cband = [&](int j) {
+      const int band0 = max_len - TQ - q0 + j * TK;
+#pragma unroll
+      for (int t = 0; t < WIN / 32; ++t) {
+        const int n = band0 + wcol + t * 32 + lane;
+        cnext[t] = (n >= 0 && n < rel_rows) ? rel_c[(long long)n * 128 + head] : 0.f;
+      }
+    };
+    load_cband(0);
     for (int j = 0; j < nk; ++j) {
       const int k0 = j * TK;
-      const int band0 = max_len - TQ - q0 + k0;
       __syncwarp();  // every lane is done with the previous tile's cband
-      for (int t = lane; t < WIN; t += 32) {
-        const int n = band0 + wcol + t;
-        cband[t] = (n >= 0 && n < rel_rows) ? rel_c[(long long)n * 128 + head] : 0.f;
-      }
+#pragma unroll
+      for (int t = 0; t < WIN / 32; ++t) cband[t * 32 + lane] = cnext[t];
       __syncwarp();
+      if (j + 1 < nk) load_cband(j + 1);
       if (!att_warp_wait(&bars->sbd_full, j & 1, err, abort)) {
         ok = false;
         break;
@@ -369,8 +379,15 @@ __global__ void __launch_bounds__(192, 1)
         sc[jj] = k0 + jj < T_ ? v : -INFINITY;
         mx = fmaxf(mx, sc[jj]);
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float corr = exp2f(m_run - m_new);
+      // The running max moves only when the row max grows by more than 8 (a factor 256 in
+      // the exponentials, which bf16 P and the fp32 sums hold exactly): O is rescaled far
+      // less often, and the final O / l is the same for any reference max.
+      float corr = 1.0f;
+      if (mx > m_run + 8.0f) {
+        corr = exp2f(m_run - mx);
+        m_run = mx;
+      }
+      const float m_new = m_run;
       float sum = 0.f;
 #pragma unroll
       for (int jj = 0; jj < TK; jj += 2) {
@@ -380,7 +397,6 @@ __global__ void __launch_bounds__(192, 1)
         r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
       }
       l_run = l_run * corr + sum;
-      m_run = m_new;
       if (j > 0) {
         if (!att_warp_wait(&bars->o_done, (j - 1) & 1, err, abort)) {
           ok = false;
