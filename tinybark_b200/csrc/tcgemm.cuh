@@ -447,13 +447,16 @@ __device__ __forceinline__ bool epilogue_tile(const tb_epilogue& e, float* stage
   } else {
     EpiPre<EPI, BN> pre;
     pre.load(e, row0, n0, lane, M);
-    ChunkOps<EPI> ops;
+    // Operands two chunks ahead: the residual rows come from HBM, whose latency is
+    // longer than one chunk's work.
+    ChunkOps<EPI> ops, ops1;
     ops.load(e, row0, n0, lane, M);
+    if (BN / 32 > 1) ops1.load(e, row0, n0 + 32, lane, M);
     if (!warp_wait(tfull, ph, err, abort)) return false;
     tc_fence_after();
     auto chunk = [&](int ci) {
-      ChunkOps<EPI> next;  // the next chunk's operands, in flight during this one
-      if (ci + 1 < BN / 32) next.load(e, row0, n0 + (ci + 1) * 32, lane, M);
+      ChunkOps<EPI> next;  // chunk ci + 2's operands, in flight during this one
+      if (ci + 2 < BN / 32) next.load(e, row0, n0 + (ci + 2) * 32, lane, M);
       uint32_t r[32];
       tmem_ld32(taddr + ci * 32, r);
       tmem_wait_ld();
@@ -465,7 +468,8 @@ __device__ __forceinline__ bool epilogue_tile(const tb_epilogue& e, float* stage
       __syncwarp();
       epi_chunk<EPI, BN>(e, stage, row0, n0 + ci * 32, lane, M, pre, ci, ops);
       __syncwarp();
-      ops = next;
+      ops = ops1;
+      ops1 = next;
     };
     if constexpr (EPI == TB_EPI_JOINT_IN) {
 #pragma unroll

@@ -328,8 +328,9 @@ class Engine:
 
     def upload(self, clips: list[np.ndarray]) -> tuple[torch.Tensor, torch.Tensor]:
         """Packs float32 sample arrays into the engine's pinned staging buffer (kept and
-        grown across calls: pinning memory is slow) with a few host threads, and copies
-        it to the device in one transfer."""
+        grown across calls: pinning memory is slow) with a few host threads, in slices
+        whose copy to the device starts as soon as each is packed, so packing and the
+        transfer overlap."""
         sizes = np.array([len(c) for c in clips], np.int64)
         off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
         total = int(off[-1])
@@ -343,12 +344,18 @@ class Engine:
         def pack(i: int) -> None:
             hv[off[i] : off[i + 1]] = clips[i]
 
+        samples = torch.empty(total, device=self.device, dtype=torch.float32)
         if total >= 1 << 22:
-            list(self._pool().map(pack, range(len(clips))))
+            # About eight slices of whole clips; each copied once packed.
+            bounds = np.searchsorted(off, np.linspace(0, total, 9)[1:-1]).tolist()
+            edges = [0, *sorted(set(b for b in bounds if 0 < b < len(clips))), len(clips)]
+            for a, b in zip(edges[:-1], edges[1:]):
+                list(self._pool().map(pack, range(a, b)))
+                samples[off[a] : off[b]].copy_(self._pinned[off[a] : off[b]], non_blocking=True)
         else:
             for i in range(len(clips)):
                 pack(i)
-        samples = self._pinned[:total].to(self.device, non_blocking=True)
+            samples.copy_(self._pinned[:total], non_blocking=True)
         self._staged = torch.cuda.Event()
         self._staged.record()
         sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
