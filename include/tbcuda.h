@@ -271,6 +271,15 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
  * once all its lanes are done (may be NULL: then every group runs its longest cap).
  * Lanes ordered longest first let the GEMMs shrink to the lanes still running. Both
  * decoders give the same tokens. */
+/* Self-test of the failure handling; no reference counterpart. Launches one CTA that
+ * waits on something nothing will complete: kind 0 an mbarrier (the wait between the
+ * warps of every tcgen05 kernel here), kind 1 the persistent decoder's grid barrier
+ * (counter and abort flag in `scratch`, 256 device bytes this call zeroes). The wait
+ * gives up after the library's limit (2 s), or-s TB_DEV_GEMM_TIMEOUT (kind 0) or
+ * TB_DEV_DECODE_TIMEOUT (kind 1) into *err and the kernel returns: no hang, no fault, and
+ * the context stays usable. */
+int tb_selftest_wait(int kind, void* scratch, int* err, void* stream);
+
 size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups);
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                   int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,

@@ -326,3 +326,26 @@ def test_subsample_matches_oracle(engine2):
     for i, f in enumerate(feats):
         ref = oenc.subsample(state_dict(2), torch.from_numpy(f)).numpy()
         assert max_rel(x[off[i] : off[i + 1]].cpu().numpy(), ref) < 1e-5
+
+
+@pytest.mark.parametrize("kind,bit", [(0, 1), (1, 4)])
+def test_bounded_wait_gives_up_and_reports(L, kind, bit, err):
+    """A wait that nothing completes (an mbarrier, or the decoder's grid barrier) gives
+    up after the library's limit, sets its TB_DEV_* bit and returns; the context then
+    still runs kernels correctly."""
+    import time
+
+    scratch = torch.empty(256, dtype=torch.uint8, device="cuda")
+    err.zero_()
+    t0 = time.time()
+    L.check(L.lib.tb_selftest_wait(kind, scratch.data_ptr(), err.data_ptr(), stream()), "tb_selftest_wait")
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert int(err.item()) == bit
+    assert 1.0 < waited < 30.0
+    err.zero_()
+    a, w, ref = operands(1, 64, 256, 64, seed=9)
+    out = torch.empty(64, 256, device="cuda", dtype=torch.float32)
+    gemm(L, 1, a, w, L.Epilogue(kind=L.EPI_STORE, out_dtype=L.F32, out=out.data_ptr(), ldo=256), err)
+    assert int(err.item()) == 0
+    assert max_rel(out.cpu(), ref.cpu()) < TOL[1]

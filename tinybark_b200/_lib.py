@@ -87,6 +87,7 @@ def _load() -> C.CDLL:
         "tb_encoder_workspace_bytes": (sz, [i32, i32, i32]),
         "tb_encoder_forward": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),
         "tb_decode_workspace_bytes": (sz, [i32, i32, i32]),
+        "tb_selftest_wait": (i32, [i32, vp, vp, vp]),
         "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
@@ -103,6 +104,7 @@ EXPORTS = (
     "tb_frontend_static",
     "tb_layernorm", "tb_gemm", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
+    "tb_selftest_wait",
 )
 
 

@@ -14,6 +14,7 @@ int frontend(const tb_model& m, const float* samples, const long long* sample_of
              int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t frontend_ws(int clips);
 size_t decode_ws_groups(int dtype, int lanes, int groups);
+int selftest_wait(int kind, unsigned* scratch, int* err, cudaStream_t stream);
 int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
                cudaStream_t stream);
@@ -278,6 +279,10 @@ size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups) {
   if (lanes <= 0) return 0;  // groups <= 0: the persistent decoder's workspace, that of one group
   groups = groups < 1 ? 1 : (groups > 8 ? 8 : groups);
   return decode_ws_groups(dtype, lanes, groups < lanes ? groups : lanes);
+}
+
+int tb_selftest_wait(int kind, void* scratch, int* err, void* stream) {
+  return selftest_wait(kind, reinterpret_cast<unsigned*>(scratch), err, as_stream(stream));
 }
 
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,

@@ -479,6 +479,33 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
   }
 }
 
+// Self-test of the bounded waits (no reference counterpart): one CTA waits on a
+// shared-memory barrier that nothing completes (kind 0: the wait every tcgen05 kernel
+// here uses between its warps) or on the decoder's grid barrier with a counter nothing
+// increments (kind 1). Each gives up after TB_WAIT_NS, or-s its TB_DEV_* bit into *err
+// and returns; nothing hangs and nothing faults.
+__global__ void selftest_wait_kernel(int kind, unsigned* counter, int* err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x != 0) return;
+  abort = 0;
+  if (kind == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0, err, TB_DEV_GEMM_TIMEOUT, &abort);  // phase 0 never completes
+  } else {
+    grid_wait(counter, 1u, err, &abort);  // the counter stays 0
+  }
+}
+
+int selftest_wait(int kind, unsigned* scratch, int* err, cudaStream_t stream) {
+  if ((kind != 0 && kind != 1) || !err || !scratch) return TB_ERR_ARG;
+  // scratch: 256 zeroed bytes for the counter and the abort flag of kind 1.
+  if (cudaMemsetAsync(scratch, 0, 256, stream) != cudaSuccess) return fail_cuda();
+  selftest_wait_kernel<<<1, 32, 0, stream>>>(kind, scratch, err);
+  return check_launch();
+}
+
 int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                   int* tokens, int* counts, void* ws, size_t ws_bytes, int* err, cudaStream_t stream) {
   if (lanes <= 0) return TB_OK;
