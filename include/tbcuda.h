@@ -195,6 +195,12 @@ int tb_sm_count(int device, int* out);
 size_t tb_frontend_workspace_bytes(int clips, int frames_total);
 int tb_frontend(const tb_model* m, const float* samples, const long long* sample_off, const int* frame_off,
                 int clips, int frames_total, int max_frames, float* feats, void* ws, size_t ws_bytes, void* stream);
+/* The same from 16-bit PCM (s16le as transcribe_pcm takes it, tinybark/tinygrad/__init__.py:33-35),
+ * converted on the device as pcm / 32768 (tinybark/pytorch/__init__.py:50): half the bytes
+ * to move, the same features. */
+int tb_frontend_pcm16(const tb_model* m, const int16_t* pcm, const long long* sample_off, const int* frame_off,
+                      int clips, int frames_total, int max_frames, float* feats, void* ws, size_t ws_bytes,
+                      void* stream);
 
 /* ---- front-end without a caller-supplied workspace (no counterpart in the reference) ----
  * The same features as tb_frontend, for callers that cannot allocate device memory:

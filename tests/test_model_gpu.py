@@ -160,3 +160,24 @@ def test_end_to_end_bf16_batch_consistent():
     for c, b in zip(clips, batch):
         assert bark.tokens(c) == b
         assert len(b) > 0
+
+
+def test_pcm16_ingest_matches_float_path():
+    """int16 PCM goes to the GPU as 16-bit and is converted there (pcm / 32768): the same
+    features, bit for bit, and the same tokens as the float32 path of the same audio."""
+    import tinybark_b200
+    from tinybark_b200 import lengths, synthetic, weights
+
+    sd = state_dict(2)
+    bark = tinybark_b200.load("gpu", weights=(weights.convert(sd, synthetic.config(2)), synthetic.config(2)))
+    eng = bark.engine
+    pcm = [synthetic.clip(s, 70 + i) for i, s in enumerate((3.0, 7.5, 1.2))]
+    flt = [synthetic.to_float(p) for p in pcm]
+    plan = eng.plan([lengths.frames(len(p)) for p in pcm])
+    feats = []
+    for clips in (pcm, flt):
+        s, o = eng.upload(clips)
+        assert s.dtype == (torch.int16 if clips is pcm else torch.float32)
+        feats.append(eng.features(s, o, plan).cpu())
+    assert torch.equal(feats[0], feats[1])
+    assert bark.tokens_batch(pcm) == bark.tokens_batch(flt)

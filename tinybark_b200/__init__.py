@@ -61,7 +61,8 @@ class Bark:
         return self.engine.tokens_batch([samples])[0]
 
     def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
-        """Token ids of many clips, packed into one GPU pass."""
+        """Token ids of many clips, packed into one GPU pass: float32 samples, or int16 PCM
+        (then moved to the GPU as 16-bit and converted there, as pcm / 32768)."""
         return self.engine.tokens_batch(clips)
 
     @property
@@ -81,8 +82,9 @@ class Bark:
         return self.tokenizer.decode(self.tokens(samples))
 
     def transcribe_pcm(self, pcm: bytes) -> str:
-        """16 kHz s16le mono PCM (tinybark/tinygrad/__init__.py:33-35)."""
-        return self.transcribe(np.frombuffer(pcm, dtype="<i2").astype(np.float32) / 32768)
+        """16 kHz s16le mono PCM (tinybark/tinygrad/__init__.py:33-35), converted to float on
+        the GPU."""
+        return self.tokenizer.decode(self.tokens(np.frombuffer(pcm, dtype="<i2").astype(np.int16)))
 
     def close(self) -> None:
         self.engine = None

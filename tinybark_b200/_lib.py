@@ -77,6 +77,7 @@ def _load() -> C.CDLL:
         "tb_sm_count": (i32, [i32, P(i32)]),
         "tb_frontend_workspace_bytes": (sz, [i32, i32]),
         "tb_frontend": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, sz, vp]),
+        "tb_frontend_pcm16": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, sz, vp]),
         "tb_frontend_static": (i32, [P(Model), vp, vp, vp, i32, i32, vp, vp]),
         "tb_layernorm": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
         "tb_gemm": (i32, [i32, vp, ll, vp, i32, i32, i32, P(Epilogue), vp, vp]),
@@ -101,7 +102,7 @@ lib = _load()
 # Every symbol include/tbcuda.h declares, for the export check.
 EXPORTS = (
     "tb_version", "tb_tile_rows", "tb_launch_count", "tb_last_cuda_error", "tb_sm_count", "tb_frontend_workspace_bytes", "tb_frontend",
-    "tb_frontend_static",
+    "tb_frontend_static", "tb_frontend_pcm16",
     "tb_layernorm", "tb_gemm", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
     "tb_selftest_wait",

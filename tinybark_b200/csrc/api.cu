@@ -13,6 +13,8 @@ namespace tb {
 int frontend(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
              int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t frontend_ws(int clips);
+int frontend_pcm16(const tb_model& m, const int16_t* pcm, const long long* sample_off, const int* frame_off,
+                   int clips, int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t decode_ws_groups(int dtype, int lanes, int groups);
 int selftest_wait(int kind, unsigned* scratch, int* err, cudaStream_t stream);
 int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
@@ -230,6 +232,14 @@ int tb_frontend(const tb_model* m, const float* samples, const long long* sample
   (void)max_frames;
   if (!m) return TB_ERR_ARG;
   return frontend(*m, samples, sample_off, frame_off, clips, frames_total, feats, ws, ws_bytes, as_stream(stream));
+}
+
+int tb_frontend_pcm16(const tb_model* m, const int16_t* pcm, const long long* sample_off, const int* frame_off,
+                      int clips, int frames_total, int max_frames, float* feats, void* ws, size_t ws_bytes,
+                      void* stream) {
+  (void)max_frames;
+  if (!m) return TB_ERR_ARG;
+  return frontend_pcm16(*m, pcm, sample_off, frame_off, clips, frames_total, feats, ws, ws_bytes, as_stream(stream));
 }
 
 int tb_layernorm(const float* x, const float* w, const float* b, float* x_out, const float* w2, const float* b2,

@@ -30,13 +30,20 @@ __device__ __forceinline__ int find_clip(const int* off, int clips, int row) {
   return lo;
 }
 
-__device__ __forceinline__ float preemph_sample(const float* x, long long n, long long len) {
+// A sample as float32: float input as is, 16-bit PCM as pcm / 32768 (exact: a power of
+// two), as tinybark/pytorch/__init__.py:50 converts it.
+__device__ __forceinline__ float sample_f(const float* x, long long n) { return x[n]; }
+__device__ __forceinline__ float sample_f(const int16_t* x, long long n) { return (float)x[n] * (1.0f / 32768.0f); }
+
+template <typename S>
+__device__ __forceinline__ float preemph_sample(const S* x, long long n, long long len) {
   if (n < 0 || n >= len) return 0.f;
   // Rounded as numpy rounds it: the product, then the difference.
-  return n == 0 ? x[0] : __fsub_rn(x[n], __fmul_rn(PREEMPH, x[n - 1]));
+  return n == 0 ? sample_f(x, 0) : __fsub_rn(sample_f(x, n), __fmul_rn(PREEMPH, sample_f(x, n - 1)));
 }
 
-__global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ samples,
+template <typename S>
+__global__ void __launch_bounds__(256) logmel_kernel(const S* __restrict__ samples,
                                                      const long long* __restrict__ sample_off,
                                                      const int* __restrict__ frame_off, int clips, int frames_total,
                                                      const float* __restrict__ window, const float* __restrict__ mel_w,
@@ -65,7 +72,7 @@ __global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ s
   if (row >= frames_total) return;
   const int clip = find_clip(frame_off, clips, row);
   const int f = row - frame_off[clip];
-  const float* x = samples + sample_off[clip];
+  const S* x = samples + sample_off[clip];
   const long long len = sample_off[clip + 1] - sample_off[clip];
   float2* zw = z[warp];
 
@@ -164,8 +171,9 @@ size_t frontend_ws(int clips) {
   return align256((size_t)clips * FE_SPLIT * TB_MELS * sizeof(double2)) + align256((size_t)clips * TB_MELS * sizeof(float2));
 }
 
-int frontend(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
-             int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream) {
+template <typename S>
+static int frontend_t(const tb_model& m, const S* samples, const long long* sample_off, const int* frame_off,
+                      int clips, int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream) {
   if (clips <= 0 || frames_total <= 0) return TB_OK;
   if (!samples || !sample_off || !frame_off || !feats || !m.window || !m.mel_w || !m.mel_start || !m.mel_off)
     return TB_ERR_ARG;
@@ -182,6 +190,16 @@ int frontend(const tb_model& m, const float* samples, const long long* sample_of
   if (int rc = check_launch()) return rc;
   normalize_kernel<<<(frames_total + 7) / 8, 256, 0, stream>>>(feats, frame_off, clips, frames_total, stats);
   return check_launch();
+}
+
+int frontend(const tb_model& m, const float* samples, const long long* sample_off, const int* frame_off, int clips,
+             int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  return frontend_t(m, samples, sample_off, frame_off, clips, frames_total, feats, ws, ws_bytes, stream);
+}
+
+int frontend_pcm16(const tb_model& m, const int16_t* pcm, const long long* sample_off, const int* frame_off,
+                   int clips, int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  return frontend_t(m, pcm, sample_off, frame_off, clips, frames_total, feats, ws, ws_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

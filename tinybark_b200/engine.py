@@ -284,14 +284,16 @@ class Engine:
     # ------------------------------------------------------------------ stages
 
     def features(self, samples: torch.Tensor, sample_off: torch.Tensor, plan: Plan) -> torch.Tensor:
-        """Packed float32 samples (device) to packed normalised log-mel features [frames, 128]."""
+        """Packed samples (device; float32, or int16 PCM converted on the device) to packed
+        normalised log-mel features [frames, 128]."""
         b = plan.batch
         feats = torch.empty(b.frames_total, L.MELS, device=self.device, dtype=torch.float32)
         nbytes = L.lib.tb_frontend_workspace_bytes(b.clips, b.frames_total)
         ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
-        L.check(L.lib.tb_frontend(C.byref(self.model), samples.data_ptr(), sample_off.data_ptr(),
-                                  plan.frame_off.data_ptr(), b.clips, b.frames_total, int(plan.frames.max()),
-                                  feats.data_ptr(), ws.data_ptr(), nbytes, _stream(self.device)), "tb_frontend")
+        fn = L.lib.tb_frontend_pcm16 if samples.dtype == torch.int16 else L.lib.tb_frontend
+        L.check(fn(C.byref(self.model), samples.data_ptr(), sample_off.data_ptr(), plan.frame_off.data_ptr(), b.clips,
+                   b.frames_total, int(plan.frames.max()), feats.data_ptr(), ws.data_ptr(), nbytes,
+                   _stream(self.device)), "tb_frontend")
         return feats
 
     def encode(self, feats: torch.Tensor, plan: Plan) -> torch.Tensor:
@@ -327,35 +329,39 @@ class Engine:
     # ------------------------------------------------------------------ end to end
 
     def upload(self, clips: list[np.ndarray]) -> tuple[torch.Tensor, torch.Tensor]:
-        """Packs float32 sample arrays into the engine's pinned staging buffer (kept and
-        grown across calls: pinning memory is slow) with a few host threads, in slices
-        whose copy to the device starts as soon as each is packed, so packing and the
-        transfer overlap."""
+        """Packs sample arrays (all float32, or all int16 PCM) into the engine's pinned
+        staging buffer (kept and grown across calls: pinning memory is slow) with a few
+        host threads, in slices whose copy to the device starts as soon as each is packed,
+        so packing and the transfer overlap."""
+        pcm = len(clips) > 0 and all(c.dtype == np.int16 for c in clips)
+        tdt = torch.int16 if pcm else torch.float32
         sizes = np.array([len(c) for c in clips], np.int64)
         off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
         total = int(off[-1])
         if self._staged is not None:
             self._staged.synchronize()  # the previous transfer out of the buffer is done
-        if self._pinned is None or self._pinned.numel() < total + 1:
-            self._pinned = torch.empty(max(total + 1, int(total * 1.25)), dtype=torch.float32).pin_memory()
-        hv = self._pinned.numpy()
-        hv[total] = 0.0
+        nbytes = (total + 1) * (2 if pcm else 4)
+        if self._pinned is None or self._pinned.numel() < nbytes:
+            self._pinned = torch.empty(max(nbytes, int(nbytes * 1.25)), dtype=torch.uint8).pin_memory()
+        staged = self._pinned[: (total + 1) * (2 if pcm else 4)].view(tdt)
+        hv = staged.numpy()
+        hv[total] = 0
 
         def pack(i: int) -> None:
             hv[off[i] : off[i + 1]] = clips[i]
 
-        samples = torch.empty(total, device=self.device, dtype=torch.float32)
+        samples = torch.empty(total, device=self.device, dtype=tdt)
         if total >= 1 << 22:
             # About eight slices of whole clips; each copied once packed.
             bounds = np.searchsorted(off, np.linspace(0, total, 9)[1:-1]).tolist()
             edges = [0, *sorted(set(b for b in bounds if 0 < b < len(clips))), len(clips)]
             for a, b in zip(edges[:-1], edges[1:]):
                 list(self._pool().map(pack, range(a, b)))
-                samples[off[a] : off[b]].copy_(self._pinned[off[a] : off[b]], non_blocking=True)
+                samples[off[a] : off[b]].copy_(staged[off[a] : off[b]], non_blocking=True)
         else:
             for i in range(len(clips)):
                 pack(i)
-            samples.copy_(self._pinned[:total], non_blocking=True)
+            samples.copy_(staged[:total], non_blocking=True)
         self._staged = torch.cuda.Event()
         self._staged.record()
         sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
@@ -371,7 +377,9 @@ class Engine:
     def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
         """Token ids of every clip (16 kHz mono float32 samples), as the reference's
         Bark.tokens returns them one clip at a time (tinybark/tinygrad/model.py:196-234)."""
-        clips = [np.asarray(c, np.float32).reshape(-1) for c in clips]
+        clips = [np.asarray(c).reshape(-1) for c in clips]
+        if not all(c.dtype == np.int16 for c in clips):  # 16-bit PCM stays 16-bit up to the GPU
+            clips = [np.asarray(c, np.float32) for c in clips]
         frames = [lengths.frames(len(c)) for c in clips]
         keep = lane_order([i for i, f in enumerate(frames) if f >= 2], frames)
         out: list[list[int]] = [[] for _ in clips]
