@@ -170,7 +170,7 @@ constexpr int ST_BYTES = 4 * 32 * ST_STRIDE * 4, C_BYTES = 4 * WIN * 4;
 constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_R = OFF_K + K_BYTES, OFF_V = OFF_R + R_BYTES,
               OFF_ST = OFF_V + V_BYTES, OFF_C = OFF_ST + ST_BYTES, OFF_BAR = OFF_C + C_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, TMEM_COLS = 512;
+constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, COL_P = 384, TMEM_COLS = 512;
 // log2(e) / sqrt(128): scores are kept in the base-2 exponent domain.
 constexpr float SCALE_LOG2 = 0.12751743074f;
 
@@ -276,14 +276,9 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t id_s = idesc_bf16(TQ, TK), id_bd = idesc_bf16(TQ, BAND), id_pv = idesc_bf16_bmn(TQ, D);
       const uint32_t qa = smem_u32(smem + OFF_Q), ka = smem_u32(smem + OFF_K), ra = smem_u32(smem + OFF_R),
                      va = smem_u32(smem + OFF_V);
-      bool ok = mbar_wait(&bars->q_full, 0, err, TB_DEV_ATTN_TIMEOUT, abort);
-      for (int j = 0; j < nk && ok; ++j) {
-        if (!mbar_wait(&bars->kr_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
-        if (j > 0) {
-          // S and BD of the previous tile read, and P (in S's columns) consumed.
-          if (!mbar_wait(&bars->sbd_empty, (j - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
-          if (!mbar_wait(&bars->o_done, (j - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
-        }
+      // S and BD of tile j + 1 are issued as soon as the softmax has read tile j's (before
+      // tile j's PV), so they overlap the softmax of tile j; P has its own columns.
+      auto sbd = [&]() {
         tc_fence_after();
 #pragma unroll
         for (int s = 0; s < 2; ++s)
@@ -299,12 +294,24 @@ __global__ void __launch_bounds__(192, 1)
                      (s | k) != 0);
         umma_commit(&bars->sbd_full);
         umma_commit(&bars->kr_empty);
+      };
+      bool ok = mbar_wait(&bars->q_full, 0, err, TB_DEV_ATTN_TIMEOUT, abort);
+      if (ok && nk > 0) {
+        ok = mbar_wait(&bars->kr_full, 0, err, TB_DEV_ATTN_TIMEOUT, abort);
+        if (ok) sbd();
+      }
+      for (int j = 0; j < nk && ok; ++j) {
+        if (j + 1 < nk) {
+          if (!mbar_wait(&bars->kr_full, (j + 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+          if (!mbar_wait(&bars->sbd_empty, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;  // tile j read
+          sbd();
+        }
         if (!mbar_wait(&bars->p_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
         if (!mbar_wait(&bars->v_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk)
-          umma_f16_ts(tmem + COL_O, tmem + COL_S + 8 * kk, sdesc_sw128_mn(va + 2048 * kk, V_SUB), id_pv,
+          umma_f16_ts(tmem + COL_O, tmem + COL_P + 8 * kk, sdesc_sw128_mn(va + 2048 * kk, V_SUB), id_pv,
                       (j | kk) != 0);
         umma_commit(&bars->o_done);
         umma_commit(&bars->v_empty);
@@ -415,7 +422,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      tmem_st32(tl + COL_S, r);
+      tmem_st32(tl + COL_P, r);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
