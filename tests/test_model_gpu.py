@@ -104,17 +104,21 @@ def test_decode_lanes_are_independent(groups):
         assert g == dec.greedy(fr, f)
 
 
-def test_decode_bf16_persistent_matches_graph_decoder():
-    """bf16, 300 lanes of seeded encoder frames with lengths 1..60 (three 128-row tiles,
-    lanes finishing at different iterations): the persistent decoder (one kernel, grid
-    barriers) and the graph-replayed one (one kernel per GEMM) compute the same GEMMs
-    and epilogues in the same order, so every lane's tokens are identical."""
+@pytest.mark.parametrize("lanes", [300, 1000])
+def test_decode_bf16_persistent_matches_graph_decoder(lanes):
+    """bf16, lanes of seeded encoder frames with lengths 1..60 (lanes finishing at
+    different iterations): the persistent decoder (one kernel, grid barriers) and the
+    graph-replayed one (one kernel per GEMM) compute the same products and epilogues;
+    only fp32 summation orders differ (the persistent kernel takes layer 0 as
+    E[token] + W_hh0.h0, and at 300 lanes layer 1's h1 half one phase ahead of its h0
+    half; at 1000 lanes layer 1's tiles outnumber the SMs and it runs unsplit), and
+    every lane's tokens come out identical."""
     from golden.make_golden import DECODE_CASES, decode_weights
 
     sd = decode_weights(DECODE_CASES["mixed"])
     eng = make_engine(2, "bf16", sd)
     rng = np.random.default_rng(7)
-    t3 = rng.integers(1, 61, 300)
+    t3 = rng.integers(1, 61, lanes)
     t3[:5] = 60  # longest first, as the engine orders a batch
     t3 = np.sort(t3)[::-1]
     feature_frames = [int(8 * t - 4) for t in t3]  # 8x subsampling: feature frames giving t3 frames

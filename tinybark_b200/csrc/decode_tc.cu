@@ -20,6 +20,11 @@
 // LSTM   layer 1: x1 . W1^T [2560 x 1280] with the cell in the epilogue (BN = 128), and
 //        on the SMs it leaves idle, the next P0 = x1[:, :640] . W_hh0^T + b0
 // PROJ   hp . dec_proj^T [640 x 640] -> dec, and z = relu(enc[frame] + dec) (BN = 64)
+// Split layer 1 (when its tiles fit one per SM, up to 896 lanes): the h1 half of layer
+// 1's product, hp . W_hh1^T, does not wait for the token. PROJ computes it on the SMs
+// the projector leaves idle, into a tensor-memory accumulator that the SM keeps through
+// JOINT and CELL; LSTM then adds h0 . W_ih1^T (K = 640 instead of 1280) into the same
+// accumulator, so layer 1 reads half the bytes on the critical path.
 // The GEMM phases use the tcgen05 pipeline of the GEMM kernel (gemm.cu): warp 0 loads
 // A and W tiles with TMA into a shared-memory ring, warp 1 issues the MMAs into one of
 // two tensor-memory accumulators, warps 2-5 run the epilogue (tcgemm.cuh) and the
@@ -45,13 +50,15 @@ constexpr int DT_RING_BYTES = 4 * (DT_A_BYTES + 256 * 64 * 2);  // 4 stages of t
 constexpr int DT_OUT_BYTES = 4 * 32 * TC_OUT_STRIDE * 4;
 constexpr int DT_SMEM = 1024 + DT_RING_BYTES + DT_OUT_BYTES + 256;
 constexpr int DT_ACC_COLS = 256;  // tensor-memory columns per accumulator
+constexpr int DT_CARRY_COL = 384;  // split layer 1: the accumulator kept from PROJ to LSTM
 
-enum { G_JOINT = 0, G_LSTM1 = 1, G_PRE0 = 2, G_PROJ = 3 };
+enum { G_JOINT = 0, G_LSTM1 = 1, G_PRE0 = 2, G_PROJ = 3, G_HH1 = 4 };
 enum { P_INIT = 0, P_CELL = 1, P_JOINT = 2, P_LSTM = 3, P_PROJ = 4 };
 
 struct DecodeTcArgs {
-  CUtensorMap a[4], w[4];  // A operand and weights of the joint, LSTM1, next-P0 and projector GEMMs
-  tb_epilogue e[4];
+  CUtensorMap a[5], w[5];  // A operand and weights of the joint, LSTM1, next-P0, projector, W_hh1 GEMMs
+  tb_epilogue e[4];        // epilogues of the first four (the W_hh1 product has none)
+  int split;               // 1: layer 1 split in its h0 and h1 halves (see above)
   DecodeWs ws;
   const float* emb_gates;  // [8193, 2560] E = embedding . W_ih0^T
   const float* b0;         // [2560] layer 0's bias
@@ -63,12 +70,15 @@ struct DecodeTcArgs {
 };
 
 __host__ __device__ constexpr int gemm_n(int g) { return g == G_JOINT ? TB_JOINT_ROWS : (g == G_PROJ ? TB_PRED : 4 * TB_PRED); }
-__host__ __device__ constexpr int gemm_k(int g) { return g == G_LSTM1 ? 2 * TB_PRED : TB_PRED; }
+__host__ __device__ constexpr int gemm_k(int g, int split) { return g == G_LSTM1 && !split ? 2 * TB_PRED : TB_PRED; }
 __host__ __device__ constexpr int gemm_bn(int g) { return g == G_JOINT ? 256 : (g == G_PROJ ? 64 : 128); }
+// Layer 1's tiles for `rows` lanes (mtiles x 20); the split needs them one per SM.
+__host__ __device__ constexpr int lstm1_tiles(int rows) { return (rows + 127) / 128 * (4 * TB_PRED / 128); }
 // The shared-memory ring is re-cut at every GEMM phase into as many stages of that
-// phase's tile size as fit (4 x 48 KB joint, 6 x 32 KB LSTM, 8 x 24 KB projector): the
-// narrower the tiles, the deeper the pipeline. A phase starts only when every copy and
-// MMA of the previous one has completed, so the re-cut never overlaps a stage in use.
+// phase's tile size as fit (4 x 48 KB joint, 6 x 32 KB LSTM and split PROJ, 8 x 24 KB
+// projector): the narrower the tiles, the deeper the pipeline. Before a re-cut the
+// producer waits until the MMAs have released every stage of the previous cut (only the
+// W_hh1 product, which has no epilogue, can still be running then).
 __host__ __device__ constexpr int stage_bytes(int g) { return DT_A_BYTES + gemm_bn(g) * 64 * 2; }
 __host__ __device__ constexpr int ring_slots(int g) {
   return DT_RING_BYTES / stage_bytes(g) < 8 ? DT_RING_BYTES / stage_bytes(g) : 8;
@@ -100,19 +110,48 @@ __device__ __forceinline__ int phase_rows(const Phase& p, const int* bounds) {
 // JOINT and PROJ: tile t = cta + k * gridDim. LSTM: layer 1's tiles (the critical path)
 // go one per CTA, and the next-P0 tiles (half the work each) to the CTAs left over, at
 // most two per CTA; with too few CTAs left, both lists are dealt round-robin.
-__device__ __forceinline__ bool phase_tile(int kind, int rows, int cta, int G, int k, int& g, int& mt, int& nt) {
+// Split layer 1: layer 1's tile t always runs on CTA t, in LSTM and, for its h1 half,
+// in the PROJ before it (so the accumulator stays on that SM); the projector's tiles
+// then start at CTA t1 and the next-P0 tiles are dealt to CTAs t1 and up.
+__device__ __forceinline__ bool phase_tile(int kind, int rows, int cta, int G, int k, int split, int& g, int& mt,
+                                           int& nt) {
   const int mtiles = (rows + 127) / 128;
-  if (kind == P_JOINT || kind == P_PROJ) {
-    g = kind == P_JOINT ? G_JOINT : G_PROJ;
-    const int ntc = gemm_n(g) / gemm_bn(g), t = cta + k * G;
-    if (t >= mtiles * ntc) return false;
-    mt = t / ntc;
-    nt = t % ntc;
-    return true;
-  }
   const int ntc = gemm_n(G_LSTM1) / gemm_bn(G_LSTM1), t1 = mtiles * ntc, free = G - t1;
   int t;
-  if (free > 0 && (t1 + free - 1) / free <= 2) {
+  if (kind == P_JOINT || (kind == P_PROJ && !split)) {
+    g = kind == P_JOINT ? G_JOINT : G_PROJ;
+    const int nc = gemm_n(g) / gemm_bn(g);
+    t = cta + k * G;
+    if (t >= mtiles * nc) return false;
+    mt = t / nc;
+    nt = t % nc;
+    return true;
+  }
+  if (kind == P_PROJ) {
+    const int nc = gemm_n(G_PROJ) / gemm_bn(G_PROJ), pt = mtiles * nc;
+    const int base = (cta - t1 % G + G) % G;  // this CTA's first projector tile
+    const int np = base < pt ? (pt - 1 - base) / G + 1 : 0;
+    if (k < np) {
+      g = G_PROJ;
+      t = base + k * G;
+      mt = t / nc;
+      nt = t % nc;
+      return true;
+    }
+    if (k > np || cta >= t1) return false;
+    g = G_HH1;
+    t = cta;
+  } else if (split) {
+    if (cta < t1) {
+      if (k > 0) return false;
+      g = G_LSTM1;
+      t = cta;
+    } else {
+      t = (cta - t1) + k * free;
+      if (t >= t1) return false;
+      g = G_PRE0;
+    }
+  } else if (free > 0 && (t1 + free - 1) / free <= 2) {
     if (cta < t1) {
       if (k > 0) return false;
       g = G_LSTM1;
@@ -200,10 +239,61 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
   return r != 0;
 }
 
-// The ring's stage size in a GEMM phase (both LSTM-phase GEMMs have BN = 128).
-__device__ __forceinline__ int phase_stage_gemm(int kind) {
-  return kind == P_JOINT ? G_JOINT : (kind == P_PROJ ? G_PROJ : G_LSTM1);
+// The ring's stage size in a GEMM phase (both LSTM-phase GEMMs have BN = 128, and so
+// has the W_hh1 product that joins the projector's phase when layer 1 is split).
+__device__ __forceinline__ int phase_stage_gemm(int kind, int split) {
+  return kind == P_JOINT ? G_JOINT : (kind == P_PROJ ? (split ? G_HH1 : G_PROJ) : G_LSTM1);
 }
+
+// The A-operand descriptor of GEMM g. With layer 1 split, layer 1 and the next-P0 GEMM
+// read the same x1 columns, and the W_hh1 product and the projector the same hp: they
+// share one descriptor, so fewer descriptors compete for the TMA unit's cache.
+__device__ __forceinline__ int a_map(int g, int split) {
+  if (!split) return g;
+  return g == G_LSTM1 ? G_PRE0 : (g == G_HH1 ? G_PROJ : g);
+}
+
+// Brings the descriptors a GEMM phase uses into the TMA unit's cache (issued while the
+// producer waits for the phase's barrier).
+__device__ __forceinline__ void prefetch_phase_maps(const DecodeTcArgs& args, int kind) {
+  if (kind == P_JOINT) {
+    prefetch_tmap(&args.a[G_JOINT]);
+    prefetch_tmap(&args.w[G_JOINT]);
+  } else if (kind == P_LSTM) {
+    prefetch_tmap(&args.a[a_map(G_LSTM1, args.split)]);
+    prefetch_tmap(&args.w[G_LSTM1]);
+    prefetch_tmap(&args.a[G_PRE0]);
+    prefetch_tmap(&args.w[G_PRE0]);
+  } else if (kind == P_PROJ) {
+    prefetch_tmap(&args.a[G_PROJ]);
+    prefetch_tmap(&args.w[G_PROJ]);
+    if (args.split) prefetch_tmap(&args.w[G_HH1]);
+  }
+}
+
+// The two tensor-memory accumulators the GEMM tiles alternate between, with one phase bit
+// each. With layer 1 split, the joint's 256-column tiles always take buffer 0 (buffer 1
+// then has 128 columns; the carried accumulator holds the other 128). The MMA thread and
+// the epilogue warps walk the same tiles in the same order, so they pick alike.
+struct AccPick {
+  int next = 0;
+  uint32_t ph = 0;  // bit b: parity of buffer b's next use
+  __device__ __forceinline__ int pick(bool first_only) {
+    const int b = first_only ? 0 : next;
+    if (!first_only) next ^= 1;
+    return b;
+  }
+  __device__ __forceinline__ uint32_t parity(int b) const { return (ph >> b) & 1u; }
+  __device__ __forceinline__ void used(int b) { ph ^= 1u << b; }
+};
+
+// Barriers beyond the GEMM kernel's: the carried accumulator of split layer 1 is full
+// (layer 1's MMAs done) and empty (its epilogue has read it).
+struct DtBars {
+  TcBars tc;
+  uint64_t cfull, cempty;
+};
+static_assert(sizeof(DtBars) <= 256, "decoder barriers");
 
 // Lane l's state before the first step: zero LSTM state (h0, h1 in x1, c), P0 = b0 (its
 // value at h0 = 0), counters. One warp per lane.
@@ -265,7 +355,8 @@ __device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int i
   // h1 (from the last layer-1 cell) into layer 1's next input; at the first step it is
   // the zero that INIT wrote there.
   uint2 h1v[TB_PRED / 128];
-  if (iter >= 0) {
+  const bool copy_h1 = iter >= 0 && !args.split;  // split layer 1 reads h1 from hp itself
+  if (copy_h1) {
 #pragma unroll
     for (int k = 0; k < TB_PRED / 128; ++k) h1v[k] = reinterpret_cast<const uint2*>(hp)[k * 32 + lane];
   }
@@ -278,7 +369,7 @@ __device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int i
     c0[u] = c;
     x1[u] = __float2bfloat16_rn(og * tanh_mufu(c));
   }
-  if (iter >= 0) {
+  if (copy_h1) {
 #pragma unroll
     for (int k = 0; k < TB_PRED / 128; ++k) reinterpret_cast<uint2*>(x1 + TB_PRED)[k * 32 + lane] = h1v[k];
   }
@@ -292,7 +383,8 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* out_stage = reinterpret_cast<float*>(smem + DT_RING_BYTES);
-  TcBars* bars = reinterpret_cast<TcBars*>(smem + DT_RING_BYTES + DT_OUT_BYTES);
+  DtBars* dbars = reinterpret_cast<DtBars*>(smem + DT_RING_BYTES + DT_OUT_BYTES);
+  TcBars* bars = &dbars->tc;
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const DecodeWs& w = args.ws;
@@ -311,6 +403,8 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
       mbar_init(&bars->tempty[a], 4);
     }
     mbar_init(&bars->done, 1);
+    mbar_init(&dbars->cfull, 1);
+    mbar_init(&dbars->cempty, 4);
     bars->abort = 0;
     bars->phase = 0;
     fence_mbar_init();
@@ -325,23 +419,29 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int g = 0; g < 4; ++g) {
+      for (int g = 0; g < 5; ++g) {
         prefetch_tmap(&args.a[g]);
         prefetch_tmap(&args.w[g]);
       }
       uint32_t use = 0, used = 0;  // per ring slot: parity of its next use; slots ever used
+      int last = -1;               // the slot filled last
       bool ok = true;
       for (int q = 1; q < q_end && ok; ++q) {
         const Phase p = phase_of(q);
+        prefetch_phase_maps(args, p.kind);
         if (!grid_wait(sync, (unsigned)q * G, err, abort)) break;
         post_phase(&bars->phase, (unsigned)q);
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;  // no lane runs: the loop is over
         if (p.kind == P_CELL) continue;
-        const int sg = phase_stage_gemm(p.kind), sb = stage_bytes(sg), slots = ring_slots(sg);
+        const int sg = phase_stage_gemm(p.kind, args.split), sb = stage_bytes(sg), slots = ring_slots(sg);
+        // The new cut may overlap stages of the old one: wait until the MMAs have
+        // released every stage in use. They complete in issue order, so the release of
+        // the stage filled last implies all the others.
+        if (last >= 0) ok = mbar_wait(&bars->empty[last], ((use >> last) & 1) ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort);
         int s = 0, g, mt, nt;
-        for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, g, mt, nt); ++k) {
-          const int bn = gemm_bn(g), kb_count = gemm_k(g) / 64;
+        for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, args.split, g, mt, nt); ++k) {
+          const int bn = gemm_bn(g), kb_count = gemm_k(g, args.split) / 64;
           for (int kb = 0; kb < kb_count; ++kb) {
             if (!mbar_wait(&bars->empty[s], ((use >> s) & 1) ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
               ok = false;
@@ -349,10 +449,11 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
             }
             uint8_t* sa = smem + s * sb;
             mbar_expect_tx(&bars->full[s], DT_A_BYTES + bn * 64 * 2);
-            tma_load_2d(sa, &args.a[g], &bars->full[s], kb * 64, mt * 128);
+            tma_load_2d(sa, &args.a[a_map(g, args.split)], &bars->full[s], kb * 64, mt * 128);
             tma_load_2d(sa + DT_A_BYTES, &args.w[g], &bars->full[s], kb * 64, nt * bn);
             use ^= 1u << s;
             used |= 1u << s;
+            last = s;
             if (++s == slots) s = 0;
           }
         }
@@ -364,8 +465,8 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int acc = 0;
-      uint32_t use = 0, acc_ph = 0;  // per ring slot: parity of its next use
+      AccPick ap;
+      uint32_t use = 0, cph = 0;  // per ring slot: parity of its next use; carried accumulator's parity
       bool ok = true;
       for (int q = 1; q < q_end && ok; ++q) {
         const Phase p = phase_of(q);
@@ -373,17 +474,32 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;
         if (p.kind == P_CELL) continue;
-        const int sg = phase_stage_gemm(p.kind), sb = stage_bytes(sg), slots = ring_slots(sg);
+        const int sg = phase_stage_gemm(p.kind, args.split), sb = stage_bytes(sg), slots = ring_slots(sg);
         int s = 0, g, mt, nt;
-        for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, g, mt, nt); ++k) {
-          const int kb_count = gemm_k(g) / 64;
+        for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, args.split, g, mt, nt); ++k) {
+          const int kb_count = gemm_k(g, args.split) / 64;
           const uint32_t idesc = g == G_JOINT ? idesc_bf16(128, 256) : (g == G_PROJ ? idesc_bf16(128, 64) : idesc_bf16(128, 128));
-          if (!mbar_wait(&bars->tempty[acc], acc_ph ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
+          // Split layer 1: the W_hh1 product starts the carried accumulator once the last
+          // layer-1 epilogue has read it; layer 1's MMAs then add to it (except at the
+          // first step, where h1 = 0 and nothing was carried).
+          const bool carried = g == G_HH1 || (g == G_LSTM1 && args.split);
+          const bool add = g == G_LSTM1 && args.split && p.iter >= 0;
+          int b = 0;
+          bool waited;
+          if (g == G_HH1) {
+            waited = mbar_wait(&dbars->cempty, cph ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort);
+          } else if (carried) {
+            waited = true;
+          } else {
+            b = ap.pick(args.split && g == G_JOINT);
+            waited = mbar_wait(&bars->tempty[b], ap.parity(b) ^ 1, err, TB_DEV_DECODE_TIMEOUT, abort);
+          }
+          if (!waited) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + acc * DT_ACC_COLS;
+          const uint32_t d = tmem + (carried ? DT_CARRY_COL : b * DT_ACC_COLS);
           for (int kb = 0; kb < kb_count; ++kb) {
             if (!mbar_wait(&bars->full[s], (use >> s) & 1, err, TB_DEV_DECODE_TIMEOUT, abort)) {
               ok = false;
@@ -393,14 +509,20 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
             const uint32_t sa = smem_u32(smem + s * sb);
             const uint64_t ad = sdesc_sw128(sa), bd = sdesc_sw128(sa + DT_A_BYTES);
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) umma_f16(d, ad + 2 * k4, bd + 2 * k4, idesc, (kb | k4) != 0);
+            for (int k4 = 0; k4 < 4; ++k4) umma_f16(d, ad + 2 * k4, bd + 2 * k4, idesc, add || (kb | k4) != 0);
             umma_commit(&bars->empty[s]);
             use ^= 1u << s;
             if (++s == slots) s = 0;
           }
           if (!ok) break;
-          umma_commit(&bars->tfull[acc]);
-          if (++acc == 2) acc = 0, acc_ph ^= 1;
+          if (g == G_HH1) continue;  // read by layer 1's MMAs, issued after these
+          if (carried) {
+            umma_commit(&dbars->cfull);
+            cph ^= 1;
+          } else {
+            umma_commit(&bars->tfull[b]);
+            ap.used(b);
+          }
         }
       }
       if (!ok) *abort = 1;
@@ -412,8 +534,8 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
     const int ew = warp - 2;       // epilogue warp 0..3
     const int quarter = warp & 3;  // tensor-memory lane quarter this warp may access
     float* stage = out_stage + quarter * 32 * TC_OUT_STRIDE;
-    int acc = 0;
-    uint32_t acc_ph = 0;
+    AccPick ap;
+    uint32_t cph = 0;  // carried accumulator's parity
     for (int q = 0; q < q_end; ++q) {
       const Phase p = phase_of(q);
       bool ok = true;
@@ -431,29 +553,38 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
           if (lane_cell(args, l, p.iter, lane) && p.iter >= 0 && lane == 0) atomicMax(bounds + p.iter + 1, l + 1);
       } else {
         int g, mt, nt;
-        for (int k = 0; phase_tile(p.kind, rows, blockIdx.x, G, k, g, mt, nt); ++k) {
+        for (int k = 0; phase_tile(p.kind, rows, blockIdx.x, G, k, args.split, g, mt, nt); ++k) {
+          if (g == G_HH1) continue;  // no epilogue: layer 1 reads it from tensor memory
+          const bool carried = g == G_LSTM1 && args.split;
+          const int b = carried ? 0 : ap.pick(args.split && g == G_JOINT);
+          uint64_t* full = carried ? &dbars->cfull : &bars->tfull[b];
+          const uint32_t ph = carried ? cph : ap.parity(b);
           const int row0 = mt * 128 + quarter * 32, n0 = nt * gemm_bn(g);
-          const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + acc * DT_ACC_COLS;
+          const uint32_t taddr =
+              tmem + ((uint32_t)(quarter * 32) << 16) + (carried ? DT_CARRY_COL : b * DT_ACC_COLS);
           if (ok) {
             // Constant indices: the epilogue's operands are then read straight from the
             // kernel parameters, never through a pointer that the stores might alias.
             if (g == G_JOINT)
-              ok = epilogue_tile<256, TB_EPI_ARGMAX>(args.e[G_JOINT], stage, taddr, row0, n0, lane, rows,
-                                                     &bars->tfull[acc], acc_ph, err, abort);
+              ok = epilogue_tile<256, TB_EPI_ARGMAX>(args.e[G_JOINT], stage, taddr, row0, n0, lane, rows, full, ph,
+                                                     err, abort);
             else if (g == G_PROJ)
-              ok = epilogue_tile<64, TB_EPI_JOINT_IN>(args.e[G_PROJ], stage, taddr, row0, n0, lane, rows,
-                                                      &bars->tfull[acc], acc_ph, err, abort);
+              ok = epilogue_tile<64, TB_EPI_JOINT_IN>(args.e[G_PROJ], stage, taddr, row0, n0, lane, rows, full, ph,
+                                                      err, abort);
             else if (g == G_LSTM1)
-              ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM1], stage, taddr, row0, n0, lane, rows,
-                                                   &bars->tfull[acc], acc_ph, err, abort);
+              ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM1], stage, taddr, row0, n0, lane, rows, full, ph,
+                                                   err, abort);
             else
-              ok = epilogue_tile<128, TB_EPI_STORE>(args.e[G_PRE0], stage, taddr, row0, n0, lane, rows,
-                                                    &bars->tfull[acc], acc_ph, err, abort);
+              ok = epilogue_tile<128, TB_EPI_STORE>(args.e[G_PRE0], stage, taddr, row0, n0, lane, rows, full, ph,
+                                                    err, abort);
           }
           tc_fence_before();
           __syncwarp();
-          if (ok && lane == 0) mbar_arrive(&bars->tempty[acc]);
-          if (++acc == 2) acc = 0, acc_ph ^= 1;
+          if (ok && lane == 0) mbar_arrive(carried ? &dbars->cempty : &bars->tempty[b]);
+          if (carried)
+            cph ^= 1;
+          else
+            ap.used(b);
         }
       }
       // The phase's writes, visible to the other CTAs' loads and TMA reads, then one
@@ -529,14 +660,20 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   DecodeTcArgs args = {};
   DecodeWs& w = args.ws;
   w = carve(ws, TB_BF16, lanes);
+  // Layer 1 splits when its tiles fit one per SM with SMs left for the next P0.
+  args.split = lstm1_tiles(lanes) < grid ? 1 : 0;
   // A operands [lanes x K] and weights [N x K], 64-column boxes of 128 rows (A) or BN rows
-  // (W). The next-P0 GEMM reads the h0 half of layer 1's input x1.
-  const void* a_ptr[4] = {w.z, w.x1, w.x1, w.hp};
-  const long long a_ld[4] = {TB_PRED, 2 * TB_PRED, 2 * TB_PRED, TB_PRED};
-  const void* w_ptr[4] = {m.joint_w, m.lstm_w[1], m.lstm0_hh, m.dec_proj_w};
-  for (int g = 0; g < 4; ++g) {
-    if (!encode_tmap_2d(&args.a[g], a_ptr[g], lanes, gemm_k(g), a_ld[g], 64, 128) ||
-        !encode_tmap_2d(&args.w[g], w_ptr[g], gemm_n(g), gemm_k(g), gemm_k(g), 64, gemm_bn(g)))
+  // (W). The next-P0 GEMM and split layer 1 read the h0 half of layer 1's input x1; the
+  // W_hh1 product reads h1 (hp) and the right half of layer 1's weights.
+  const void* a_ptr[5] = {w.z, w.x1, w.x1, w.hp, w.hp};
+  const long long a_ld[5] = {TB_PRED, 2 * TB_PRED, 2 * TB_PRED, TB_PRED, TB_PRED};
+  const void* w_ptr[5] = {m.joint_w, m.lstm_w[1], m.lstm0_hh, m.dec_proj_w,
+                          static_cast<const __nv_bfloat16*>(m.lstm_w[1]) + TB_PRED};
+  const long long w_ld[5] = {TB_PRED, 2 * TB_PRED, TB_PRED, TB_PRED, 2 * TB_PRED};
+  for (int g = 0; g < 5; ++g) {
+    const int k = gemm_k(g, args.split);
+    if (!encode_tmap_2d(&args.a[g], a_ptr[g], lanes, k, a_ld[g], 64, 128) ||
+        !encode_tmap_2d(&args.w[g], w_ptr[g], gemm_n(g), k, w_ld[g], 64, gemm_bn(g)))
       return TB_ERR_CUDA;
   }
   tb_epilogue& jt = args.e[G_JOINT];
