@@ -70,7 +70,7 @@ enum tb_epilogue_kind {
   TB_EPI_LSTM = 7,      /* W rows gate-interleaved (row 4u+g, gates i,f,g,o): LSTM cell for
                            rows with mask[m] != 0: c[m,u], h[m,u] updated, h also written
                            to out[m*ldo+u] and out2[m*ldo2+u] (out_dtype)                  */
-  TB_EPI_JOINT_IN = 8   /* the decoder projector: out[m,n] = acc + bias[n] (fp32), and for
+  TB_EPI_JOINT_IN = 8   /* the decoder projector: out[m,n] = acc + bias[n] (fp32; out may be NULL), and for
                            rows with gather_row[m] >= 0 the joint's next input
                            out2[m*ldo2+n] = relu(gather[gather_row[m]*ldo + n] + out[m,n])
                            (out_dtype)                                                    */

@@ -153,6 +153,33 @@ def test_gemm_argmax(L, dtype, err):
         assert (tok == lt.argmax(1)).all() and (dur == ld.argmax(1)).all()
 
 
+@pytest.mark.parametrize("lanes", [90, 300])
+def test_gemm_argmax_first_index_exact(L, err, lanes):
+    """bf16 with small-integer operands and biases: every accumulator and logit is an
+    exact integer whatever the summation order, ties are common, and the epilogue must
+    return the first column of the maximum, as the reference's argmax does
+    (tinybark/tinygrad/model.py:43-53). 90 lanes run 64-column tiles, 300 lanes
+    256-column tiles (four chunks per row, each row with its own winning chunk)."""
+    split, n, k = 8193, 8448, 640
+    g = torch.Generator(device="cuda").manual_seed(lanes)
+    a = torch.randint(-1, 2, (lanes, k), device="cuda", generator=g).to(torch.bfloat16)
+    w = torch.randint(-1, 2, (n, k), device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randint(-2, 3, (n,), device="cuda", generator=g).float()
+    bias[split + 5 :] = float("-inf")
+    keys = torch.zeros(lanes, dtype=torch.int64, device="cuda")
+    keys2 = torch.zeros(lanes, dtype=torch.int64, device="cuda")
+    ep = L.Epilogue(kind=L.EPI_ARGMAX, bias=bias.data_ptr(), keys=keys.data_ptr(), keys2=keys2.data_ptr(),
+                    split=split, split_end=split + 5)
+    gemm(L, 1, a, w, ep, err)
+    logits = (a.double() @ w.double().T + bias.double()).cpu().numpy()
+    tok = (0xFFFFFFFF - (keys & 0xFFFFFFFF)).cpu().numpy()
+    dur = (0xFFFFFFFF - (keys2 & 0xFFFFFFFF)).cpu().numpy()
+    ties = sum(int((row == row.max()).sum() > 1) for row in logits[:, :split])
+    assert ties > 0  # the case exercises first-index ties
+    assert (tok == logits[:, :split].argmax(1)).all()
+    assert (dur == logits[:, split : split + 5].argmax(1)).all()
+
+
 @pytest.mark.parametrize("dtype", [0, 1])
 @pytest.mark.parametrize("fused", [False, True])
 def test_layernorm(L, dtype, fused):

@@ -536,6 +536,11 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
     float* stage = out_stage + quarter * 32 * TC_OUT_STRIDE;
     AccPick ap;
     uint32_t cph = 0;  // carried accumulator's parity
+    // Split layer 1: the cell state of this warp's 32 rows of the CTA's layer-1 tile (the
+    // tile never moves to another SM), one row per lane.
+    float c1[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) c1[u] = 0.f;
     for (int q = 0; q < q_end; ++q) {
       const Phase p = phase_of(q);
       bool ok = true;
@@ -571,6 +576,9 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
             else if (g == G_PROJ)
               ok = epilogue_tile<64, TB_EPI_JOINT_IN>(args.e[G_PROJ], stage, taddr, row0, n0, lane, rows, full, ph,
                                                       err, abort);
+            else if (carried)
+              ok = lstm_tile<128, true>(args.e[G_LSTM1], stage, taddr, row0, n0, lane, rows, full, ph, err, abort,
+                                        &c1);
             else if (g == G_LSTM1)
               ok = epilogue_tile<128, TB_EPI_LSTM>(args.e[G_LSTM1], stage, taddr, row0, n0, lane, rows, full, ph,
                                                    err, abort);
@@ -700,8 +708,8 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   tb_epilogue& pj = args.e[G_PROJ];
   pj.kind = TB_EPI_JOINT_IN;
   pj.out_dtype = TB_BF16;
-  pj.out = w.dec;
-  pj.ldo = TB_PRED;
+  pj.out = nullptr;  // dec itself is not needed again: PROJ recomputes it every iteration
+  pj.ldo = TB_PRED;  // the gather's row stride
   pj.out2 = w.z;
   pj.ldo2 = TB_PRED;
   pj.bias = m.dec_proj_b;

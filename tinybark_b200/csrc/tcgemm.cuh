@@ -231,10 +231,61 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
       const int m = row0 + it * 4 + sub;
       if (m >= M) continue;
       const float d0 = v[it].x + b.x, d1 = v[it].y + b.y, d2 = v[it].z + b.z, d3 = v[it].w + b.w;
-      store4(out + (long long)m * e.ldo + n, d0, d1, d2, d3);
+      if (out) store4(out + (long long)m * e.ldo + n, d0, d1, d2, d3);
       if (pre.g[it] >= 0)
         store4_dt(e.out2, (long long)m * e.ldo2 + n, e.out_dtype, fmaxf(x[it].x + d0, 0.f), fmaxf(x[it].y + d1, 0.f),
                   fmaxf(x[it].z + d2, 0.f), fmaxf(x[it].w + d3, 0.f));
+    }
+  }
+}
+
+// The new h of one warp's 32 rows (lane = row, in `tile`, 32 rows x 33 floats) out to
+// e.h (fp32), e.out and e.out2 (out_dtype) as row segments: U units of a row per warp
+// store. Only rows whose bit is set in `steps` (and below M) are written.
+template <int BN>
+__device__ __forceinline__ void lstm_store_h(const tb_epilogue& e, const float* tile, int row0, int n0, int lane,
+                                             int M, unsigned steps) {
+  constexpr int U = BN / 4, RPI = 32 / U, TS = 33;
+  const int u0 = n0 >> 2, j = lane % U, rsub = lane / U;
+  float* const hst = e.h;
+  void* const out = e.out;
+  void* const out2 = e.out2;
+  const int dt = e.out_dtype;
+  const long long ldo = e.ldo, ldo2 = e.ldo2;
+  float v[U];
+#pragma unroll
+  for (int it = 0; it < U; ++it) v[it] = tile[(it * RPI + rsub) * TS + j];
+  auto row_ok = [&](int it) {
+    const int row = it * RPI + rsub;
+    return ((steps >> row) & 1u) && row0 + row < M;
+  };
+  auto at = [&](int it, long long ld) { return (long long)(row0 + it * RPI + rsub) * ld + u0 + j; };
+  if (hst) {
+#pragma unroll
+    for (int it = 0; it < U; ++it)
+      if (row_ok(it)) hst[at(it, TB_PRED)] = v[it];
+  }
+  if (dt == TB_BF16) {
+    if (out) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<__nv_bfloat16*>(out)[at(it, ldo)] = __float2bfloat16_rn(v[it]);
+    }
+    if (out2) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<__nv_bfloat16*>(out2)[at(it, ldo2)] = __float2bfloat16_rn(v[it]);
+    }
+  } else {
+    if (out) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<float*>(out)[at(it, ldo)] = v[it];
+    }
+    if (out2) {
+#pragma unroll
+      for (int it = 0; it < U; ++it)
+        if (row_ok(it)) reinterpret_cast<float*>(out2)[at(it, ldo2)] = v[it];
     }
   }
 }
@@ -249,20 +300,49 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
 // Loops are kept rolled: in the persistent decoder every phase runs its epilogue once
 // per iteration, and compact code stays in the instruction cache between iterations.
 // Rows with mask[m] == 0 (and rows >= M) are left as they are.
-template <int BN>
+//
+// CREG: the cell state of the lane's row lives in the caller's registers `creg` instead
+// of e.c (the persistent decoder runs a tile's rows on the same warp every step): no
+// loads or stores of c, and one pass over the accumulator.
+template <int BN, bool CREG = false>
 __device__ __forceinline__ bool lstm_tile(const tb_epilogue& e, float* tile, uint32_t taddr, int row0, int n0,
                                           int lane, int M, uint64_t* tfull, uint32_t ph, int* err,
-                                          volatile int* abort) {
+                                          volatile int* abort, float (*creg)[BN / 4] = nullptr) {
   static_assert(BN == 64 || BN == 128, "LSTM tiles cover 16 or 32 units");
   constexpr int U = BN / 4, RPI = 32 / U, TS = 33;  // units per row, rows per warp access, tile stride
   const int u0 = n0 >> 2, j = lane % U, rsub = lane / U;
+  if constexpr (CREG) {
+    const float4 bl = load4(e.bias + n0 + 4 * (lane % U));
+    const int my_m = row0 + lane;
+    const int step = my_m < M && (!e.mask || e.mask[my_m] != 0);
+    if (!warp_wait(tfull, ph, err, abort)) return false;
+    tc_fence_after();
+    const unsigned steps = __ballot_sync(0xffffffffu, step);
+    float* c = *creg;
+#pragma unroll
+    for (int ci = 0; ci < BN / 32; ++ci) {
+      uint32_t r[32];
+      tmem_ld32(taddr + ci * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int uu = ci * 8 + k;
+        const float ig = sigmoid_mufu(__uint_as_float(r[4 * k]) + __shfl_sync(0xffffffffu, bl.x, uu));
+        const float fg = sigmoid_mufu(__uint_as_float(r[4 * k + 1]) + __shfl_sync(0xffffffffu, bl.y, uu));
+        const float gg = tanh_mufu(__uint_as_float(r[4 * k + 2]) + __shfl_sync(0xffffffffu, bl.z, uu));
+        const float og = sigmoid_mufu(__uint_as_float(r[4 * k + 3]) + __shfl_sync(0xffffffffu, bl.w, uu));
+        const float cn = fg * c[uu] + ig * gg;
+        if (step) c[uu] = cn;
+        tile[lane * TS + uu] = og * tanh_mufu(cn);
+      }
+    }
+    __syncwarp();
+    lstm_store_h<BN>(e, tile, row0, n0, lane, M, steps);
+    __syncwarp();
+    return true;
+  }
   float* const cst = e.c;
-  float* const hst = e.h;
   const float* const bias = e.bias;
-  void* const out = e.out;
-  void* const out2 = e.out2;
-  const int dt = e.out_dtype;
-  const long long ldo = e.ldo, ldo2 = e.ldo2;
 #pragma unroll 1
   for (int it = 0; it < U; ++it) {
     const int row = it * RPI + rsub, m = row0 + row;
@@ -325,41 +405,7 @@ __device__ __forceinline__ bool lstm_tile(const tb_epilogue& e, float* tile, uin
     }
   }
   __syncwarp();
-#pragma unroll
-  for (int it = 0; it < U; ++it) v[it] = tile[(it * RPI + rsub) * TS + j];
-  auto row_ok = [&](int it) {
-    const int row = it * RPI + rsub;
-    return ((steps >> row) & 1u) && row0 + row < M;
-  };
-  auto at = [&](int it, long long ld) { return (long long)(row0 + it * RPI + rsub) * ld + u0 + j; };
-  if (hst) {
-#pragma unroll
-    for (int it = 0; it < U; ++it)
-      if (row_ok(it)) hst[at(it, TB_PRED)] = v[it];
-  }
-  if (dt == TB_BF16) {
-    if (out) {
-#pragma unroll
-      for (int it = 0; it < U; ++it)
-        if (row_ok(it)) reinterpret_cast<__nv_bfloat16*>(out)[at(it, ldo)] = __float2bfloat16_rn(v[it]);
-    }
-    if (out2) {
-#pragma unroll
-      for (int it = 0; it < U; ++it)
-        if (row_ok(it)) reinterpret_cast<__nv_bfloat16*>(out2)[at(it, ldo2)] = __float2bfloat16_rn(v[it]);
-    }
-  } else {
-    if (out) {
-#pragma unroll
-      for (int it = 0; it < U; ++it)
-        if (row_ok(it)) reinterpret_cast<float*>(out)[at(it, ldo)] = v[it];
-    }
-    if (out2) {
-#pragma unroll
-      for (int it = 0; it < U; ++it)
-        if (row_ok(it)) reinterpret_cast<float*>(out2)[at(it, ldo2)] = v[it];
-    }
-  }
+  lstm_store_h<BN>(e, tile, row0, n0, lane, M, steps);
   __syncwarp();
   return true;
 }
@@ -367,53 +413,68 @@ __device__ __forceinline__ bool lstm_tile(const tb_epilogue& e, float* tile, uin
 // The joint head's epilogue for one row (one lane) of a tile: the largest token logit
 // and the largest duration logit with their first column, merged into the row's keys.
 // `bias` holds the tile's BN bias values. Padding columns have bias -inf and never win.
+// Token columns go in 64-column chunks (two tensor-memory loads per wait; a load is
+// warp-collective, so every lane reads the same columns) through four running maxima
+// (columns j = 0..3 mod 4). Each keeps its first column: fmaxf gives the new maximum,
+// and the column changes only when the maximum did, so a tie keeps the earlier column
+// and each chain's dependence is one fmaxf per column. The columns from the last whole
+// chunk on (the token/duration boundary) are compared one by one, in column order.
 template <int BN>
 __device__ __forceinline__ void argmax_tile(const tb_epilogue& e, const float* bias, uint32_t taddr, int m, int n0,
                                             int M) {
   const float neg_inf = __int_as_float(0xff800000);
   const int split = e.split, split_end = e.split_end;
-  // Four running maxima over the columns j = 0, 1, 2, 3 mod 4 (shorter dependent compare
-  // chains), merged at the end; each keeps the first of equal values (strictly greater,
-  // columns ascending).
+  int tok_end = split - n0;  // token columns of this tile: [0, tok_end)
+  tok_end = tok_end < 0 ? 0 : (tok_end > BN ? BN : tok_end);
+  const int whole = tok_end & ~63;
   float best[4] = {neg_inf, neg_inf, neg_inf, neg_inf};
   int idx[4] = {-1, -1, -1, -1};
-  float dbest = neg_inf;
-  int di = -1;
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    const int n = n0 + c;
-    if (n >= split_end) break;  // only padding columns (bias -inf) from here on
-    uint32_t r[32];
-    tmem_ld32(taddr + c, r);
+  for (int c = 0; c < whole; c += 64) {
+    uint32_t r[2][32];
+    tmem_ld32(taddr + c, r[0]);
+    tmem_ld32(taddr + c + 32, r[1]);
     tmem_wait_ld();
-    if (n + 32 <= split) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
-        const float4 b = *reinterpret_cast<const float4*>(bias + c + j);
-        const float x0 = __uint_as_float(r[j]) + b.x, x1 = __uint_as_float(r[j + 1]) + b.y;
-        const float x2 = __uint_as_float(r[j + 2]) + b.z, x3 = __uint_as_float(r[j + 3]) + b.w;
-        if (x0 > best[0]) best[0] = x0, idx[0] = n + j;
-        if (x1 > best[1]) best[1] = x1, idx[1] = n + j + 1;
-        if (x2 > best[2]) best[2] = x2, idx[2] = n + j + 2;
-        if (x3 > best[3]) best[3] = x3, idx[3] = n + j + 3;
-      }
-    } else {  // the chunk holding the token/duration boundary
+        const float4 b = *reinterpret_cast<const float4*>(bias + c + 32 * h + j);
+        const int n = n0 + c + 32 * h + j;
+        const float x[4] = {__uint_as_float(r[h][j]) + b.x, __uint_as_float(r[h][j + 1]) + b.y,
+                            __uint_as_float(r[h][j + 2]) + b.z, __uint_as_float(r[h][j + 3]) + b.w};
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float x = __uint_as_float(r[j]) + bias[c + j];
-        if (n + j < split) {
-          if (x > best[0]) best[0] = x, idx[0] = n + j;
-        } else if (n + j < split_end) {
-          if (x > dbest) dbest = x, di = n + j - split;
+        for (int k = 0; k < 4; ++k) {
+          const float nb = fmaxf(best[k], x[k]);
+          idx[k] = nb != best[k] ? n + k : idx[k];
+          best[k] = nb;
         }
       }
-    }
   }
   float tb = best[0];
   int ti = idx[0];
 #pragma unroll
   for (int k = 1; k < 4; ++k)
     if (idx[k] >= 0 && (ti < 0 || best[k] > tb || (best[k] == tb && idx[k] < ti))) tb = best[k], ti = idx[k];
+  float dbest = neg_inf;
+  int di = -1;
+  const int cols = split_end - n0 < BN ? split_end - n0 : BN;
+#pragma unroll 1
+  for (int c = whole; c < cols; c += 32) {  // the boundary: token, duration and padding columns
+    const int n = n0 + c;
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float x = __uint_as_float(r[j]) + bias[c + j];
+      if (n + j < split) {
+        if (x > tb) tb = x, ti = n + j;
+      } else if (n + j < split_end) {
+        if (x > dbest) dbest = x, di = n + j - split;
+      }
+    }
+  }
   if (m < M) {
     if (ti >= 0) atomicMax(e.keys + m, argmax_key(tb, ti));
     if (di >= 0) atomicMax(e.keys2 + m, argmax_key(dbest, di));
