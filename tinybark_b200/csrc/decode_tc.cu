@@ -239,10 +239,13 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
   return r != 0;
 }
 
-// The ring's stage size in a GEMM phase (both LSTM-phase GEMMs have BN = 128, and so
-// has the W_hh1 product that joins the projector's phase when layer 1 is split).
-__device__ __forceinline__ int phase_stage_gemm(int kind, int split) {
-  return kind == P_JOINT ? G_JOINT : (kind == P_PROJ ? (split ? G_HH1 : G_PROJ) : G_LSTM1);
+// The ring's stage size for this CTA in a GEMM phase (both LSTM-phase GEMMs have
+// BN = 128, and so has the W_hh1 product that joins the projector's phase, on CTAs below
+// layer 1's tile count, when layer 1 is split).
+__device__ __forceinline__ int phase_stage_gemm(int kind, int split, int rows, int cta) {
+  if (kind == P_JOINT) return G_JOINT;
+  if (kind == P_PROJ) return split && cta < lstm1_tiles(rows) ? G_HH1 : G_PROJ;
+  return G_LSTM1;
 }
 
 // The A-operand descriptor of GEMM g. With layer 1 split, layer 1 and the next-P0 GEMM
@@ -434,7 +437,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;  // no lane runs: the loop is over
         if (p.kind == P_CELL) continue;
-        const int sg = phase_stage_gemm(p.kind, args.split), sb = stage_bytes(sg), slots = ring_slots(sg);
+        const int sg = phase_stage_gemm(p.kind, args.split, rows, blockIdx.x), sb = stage_bytes(sg), slots = ring_slots(sg);
         // The new cut may overlap stages of the old one: wait until the MMAs have
         // released every stage in use. They complete in issue order, so the release of
         // the stage filled last implies all the others.
@@ -474,7 +477,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;
         if (p.kind == P_CELL) continue;
-        const int sg = phase_stage_gemm(p.kind, args.split), sb = stage_bytes(sg), slots = ring_slots(sg);
+        const int sg = phase_stage_gemm(p.kind, args.split, rows, blockIdx.x), sb = stage_bytes(sg), slots = ring_slots(sg);
         int s = 0, g, mt, nt;
         for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, args.split, g, mt, nt); ++k) {
           const int kb_count = gemm_k(g, args.split) / 64;

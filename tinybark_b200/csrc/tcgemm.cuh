@@ -252,6 +252,27 @@ __device__ __forceinline__ void lstm_store_h(const tb_epilogue& e, const float* 
   void* const out2 = e.out2;
   const int dt = e.out_dtype;
   const long long ldo = e.ldo, ldo2 = e.ldo2;
+  if (U == 32 && dt == TB_BF16 && !hst) {
+    // 16-byte stores: lane l writes units 8q .. 8q+7 (q = l % 4) of rows l/4 + 8i, so one
+    // warp store covers 8 row segments (4 stores per warp instead of 32).
+    const int q = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = (lane >> 2) + 8 * i, m = row0 + row;
+      const float* t = tile + row * TS + 8 * q;
+      uint4 pk;
+      pk.x = pack_bf16x2(t[0], t[1]);
+      pk.y = pack_bf16x2(t[2], t[3]);
+      pk.z = pack_bf16x2(t[4], t[5]);
+      pk.w = pack_bf16x2(t[6], t[7]);
+      if (((steps >> row) & 1u) && m < M) {
+        if (out) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + (long long)m * ldo + u0 + 8 * q) = pk;
+        if (out2)
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out2) + (long long)m * ldo2 + u0 + 8 * q) = pk;
+      }
+    }
+    return;
+  }
   float v[U];
 #pragma unroll
   for (int it = 0; it < U; ++it) v[it] = tile[(it * RPI + rsub) * TS + j];
