@@ -166,6 +166,35 @@ def test_end_to_end_bf16_batch_consistent():
         assert len(b) > 0
 
 
+def test_tokens_batch_parts_match_whole_batch_path():
+    """bf16, 40 clips of 1-30 s: tokens_batch uploads and encodes the batch in parts (the
+    copy of each part overlapping the previous part's encoder) and turns finished lanes
+    into lists while the persistent decoder still runs; every list equals that of the
+    plain path (one upload, one encoder call over the whole batch, decode, then lists)."""
+    import tinybark_b200
+    from tinybark_b200 import lengths, synthetic, weights
+    from tinybark_b200.engine import lane_order
+
+    sd = state_dict(2)
+    bark = tinybark_b200.load("gpu", weights=(weights.convert(sd, synthetic.config(2)), synthetic.config(2)))
+    eng = bark.engine
+    rng = np.random.default_rng(11)
+    clips = clips_of(tuple(float(x) for x in rng.uniform(1.0, 30.0, 40)), seed=90)
+    got = bark.tokens_batch(clips)
+    frames = [lengths.frames(len(c)) for c in clips]
+    keep = lane_order(list(range(len(clips))), frames)
+    plan = eng.plan([frames[i] for i in keep])
+    s, o = eng.upload([np.asarray(clips[i], np.float32) for i in keep])
+    tokens, counts = eng.decode(eng.encode(eng.features(s, o, plan), plan), plan)
+    eng.check()
+    tk, cn = tokens.cpu().numpy(), counts.cpu().numpy()
+    want = [[] for _ in clips]
+    for j, i in enumerate(keep):
+        want[i] = tk[j, : cn[j]].tolist()
+    assert sum(len(w) for w in want) > 0
+    assert got == want
+
+
 def test_pcm16_ingest_matches_float_path():
     """int16 PCM goes to the GPU as 16-bit and is converted there (pcm / 32768): the same
     features, bit for bit, and the same tokens as the float32 path of the same audio."""

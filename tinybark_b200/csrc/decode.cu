@@ -314,7 +314,7 @@ static int decode_impl(const tb_model& m, const float* enc, const int* enc_off, 
 }
 
 int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
-                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* err, cudaStream_t stream);
+                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, cudaStream_t stream);
 
 int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
@@ -322,7 +322,8 @@ int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const in
   if (lanes <= 0) return TB_OK;
   if (!enc || !enc_off || !cap || !tokens || !counts || !ws || max_cap <= 0) return TB_ERR_ARG;
   if (groups <= 0 && m.dtype == TB_BF16)
-    return tdt_decode_tc(m, enc, enc_off, cap, lanes, max_cap, tokens, counts, ws, ws_bytes, err, stream);
+    return tdt_decode_tc(m, enc, enc_off, cap, lanes, max_cap, tokens, counts, ws, ws_bytes, host_flag, err,
+                         stream);
   groups = std::max(1, std::min(std::min(groups, DECODE_MAX_GROUPS), lanes));
   if (ws_bytes < decode_ws_groups(m.dtype, lanes, groups)) return TB_ERR_WORKSPACE;
   if (m.dtype == TB_BF16)

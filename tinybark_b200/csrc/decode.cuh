@@ -100,10 +100,11 @@ __device__ __forceinline__ void lane_init(const DecodeWs& w, const T* __restrict
 // frame += max(d, 1); otherwise emit, stop on EOS, else frame += d and the LSTM steps on
 // the token; the lane stops when frame >= valid or after cap[l] iterations. On every
 // lane of the warp: returns whether lane l still runs, and sets `step` (the LSTM steps)
-// and `tok`.
+// and `tok`. counts_out (if not NULL) receives the lane's token count when it stops.
 __device__ __forceinline__ bool lane_scalar_step(const DecodeWs& w, const int* __restrict__ enc_off,
                                                  const int* __restrict__ cap, int l, int max_cap,
-                                                 int* __restrict__ tokens, int lane, int& step_out, int& tok_out) {
+                                                 int* __restrict__ tokens, int lane, int& step_out, int& tok_out,
+                                                 int* __restrict__ counts_out = nullptr) {
   int step = 0, tok = 0, running = 0;
   if (lane == 0) {
     // Every scalar the step needs, loaded at once (one memory round trip), then used.
@@ -121,12 +122,13 @@ __device__ __forceinline__ bool lane_scalar_step(const DecodeWs& w, const int* _
       if (tok < 0 || tok >= TB_VOCAB) tok = TB_BLANK;
       if (d < 0 || d >= TB_DURATIONS) d = 1;
       const int valid = off1 - off0;
-      int frame = frame0, it = it0 + 1, done = 0;
+      int frame = frame0, it = it0 + 1, done = 0, n = n0;
       if (tok == TB_BLANK) {
         frame += d > 1 ? d : 1;
       } else {
         if (n0 < max_cap) tokens[(long long)l * max_cap + n0] = tok;
-        w.count[l] = n0 + 1;
+        n = n0 + 1;
+        w.count[l] = n;
         if (tok == TB_EOS) {
           done = 1;
         } else {
@@ -136,6 +138,7 @@ __device__ __forceinline__ bool lane_scalar_step(const DecodeWs& w, const int* _
       }
       if (it >= cap_l || frame >= valid) done = 1;
       if (done) step = 0;
+      if (done && counts_out) counts_out[l] = n;
       w.frame[l] = frame;
       w.it[l] = it;
       w.done[l] = done;

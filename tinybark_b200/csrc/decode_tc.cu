@@ -66,6 +66,8 @@ struct DecodeTcArgs {
   const int* cap;
   int lanes, max_cap, max_iters;
   int* tokens;
+  int* counts;    // each lane's count, written when the lane stops
+  int* progress;  // host-mapped (may be NULL): [0] row bound, [1] iteration
   int* err;
 };
 
@@ -322,6 +324,7 @@ __device__ __forceinline__ void lane_init_tc(const DecodeTcArgs& args, int l, in
     w.keys[l] = 0ull;
     w.keys2[l] = 0ull;
     w.erow[l] = done ? -1 : args.enc_off[l];
+    args.counts[l] = 0;
   }
 }
 
@@ -337,7 +340,7 @@ __device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int i
     step = running;
     tok = TB_BLANK;
   } else {
-    running = lane_scalar_step(w, args.enc_off, args.cap, l, args.max_cap, args.tokens, lane, step, tok);
+    running = lane_scalar_step(w, args.enc_off, args.cap, l, args.max_cap, args.tokens, lane, step, tok, args.counts);
   }
   if (!step) return running;
   const long long L = args.lanes;
@@ -554,6 +557,14 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         rows = phase_rows(p, bounds);
         if (rows <= 0) break;
       }
+      if (p.kind == P_JOINT && args.progress && blockIdx.x == 0 && ew == 0 && lane == 0 && (p.iter & 7) == 0) {
+        // Every lane at or above `rows` has stopped, its tokens and count written before
+        // the last barrier: publish the bound to the host, which may copy those lanes out
+        // while the loop goes on.
+        __threadfence_system();
+        *reinterpret_cast<volatile int*>(args.progress + 1) = p.iter;
+        *reinterpret_cast<volatile int*>(args.progress) = rows;
+      }
       if (p.kind == P_INIT) {
         for (int l = blockIdx.x * 4 + ew; l < args.lanes; l += G * 4) lane_init_tc(args, l, lane);
       } else if (p.kind == P_CELL) {
@@ -649,7 +660,7 @@ int selftest_wait(int kind, unsigned* scratch, int* err, cudaStream_t stream) {
 }
 
 int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
-                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* err, cudaStream_t stream) {
+                  int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err, cudaStream_t stream) {
   if (lanes <= 0) return TB_OK;
   if (m.dtype != TB_BF16 || !m.lstm0_hh || !m.lstm0_emb) return TB_ERR_ARG;
   if (!enc || !enc_off || !cap || !tokens || !counts || !ws || max_cap <= 0) return TB_ERR_ARG;
@@ -727,6 +738,10 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   args.max_iters = max_cap;  // every lane stops after at most cap <= max_cap iterations
   if (max_cap > DECODE_MAX_ITERS) return TB_ERR_ARG;
   args.tokens = tokens;
+  args.counts = counts;
+  args.progress = nullptr;
+  if (host_flag && cudaHostGetDevicePointer(reinterpret_cast<void**>(&args.progress), host_flag, 0) != cudaSuccess)
+    return fail_cuda();
   args.err = err;
 
   // Row bounds: [0] = every lane, the rest zero until their iteration; barrier counter
@@ -748,10 +763,7 @@ int tdt_decode_tc(const tb_model& m, const float* enc, const int* enc_off, const
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, decode_tc_kernel, args);
-  if (int rc = check_launch()) return rc;
-  if (cudaMemcpyAsync(counts, w.count, (size_t)lanes * sizeof(int), cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
-    return fail_cuda();
-  return TB_OK;
+  return check_launch();
 }
 
 }  // namespace tb

@@ -11,6 +11,7 @@ zeroes is a zero-padding position here.
 from __future__ import annotations
 
 import ctypes as C
+import time
 from dataclasses import dataclass
 
 import numpy as np
@@ -113,6 +114,9 @@ class Engine:
         self._pinned: torch.Tensor | None = None  # sample staging buffer of upload()
         self._staged = None  # event after the last copy out of it
         self._threads = None
+        self._side: torch.cuda.Stream | None = None  # copies of finished lanes during decode
+        self._copy: torch.cuda.Stream | None = None  # sample copies of upload_parts()
+        self._tok_host: torch.Tensor | None = None  # pinned token rows of decode_lists()
         with torch.cuda.device(self.device):
             self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.host_flag = torch.zeros(2 * MAX_DECODE_GROUPS, dtype=torch.int32).pin_memory()
@@ -296,10 +300,13 @@ class Engine:
                    _stream(self.device)), "tb_frontend")
         return feats
 
-    def encode(self, feats: torch.Tensor, plan: Plan) -> torch.Tensor:
-        """Packed features to packed encoder frames projected for the joint, [t3_total, 640] float32."""
+    def encode(self, feats: torch.Tensor, plan: Plan, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Packed features to packed encoder frames projected for the joint, [t3_total, 640]
+        float32 (into `out` if given: contiguous rows of that shape)."""
         b = plan.batch
-        enc = torch.empty(b.t3_total, L.PRED, device=self.device, dtype=torch.float32)
+        enc = torch.empty(b.t3_total, L.PRED, device=self.device, dtype=torch.float32) if out is None else out
+        if enc.shape != (b.t3_total, L.PRED) or not enc.is_contiguous() or enc.dtype != torch.float32:
+            raise ValueError("encode: out must be a contiguous float32 [t3_total, 640] tensor")
         nbytes = L.lib.tb_encoder_workspace_bytes(self.dtype, b.t2_total, b.t3_total)
         ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
         L.check(L.lib.tb_encoder_forward(C.byref(self.model), C.byref(b), feats.data_ptr(), enc.data_ptr(),
@@ -367,6 +374,48 @@ class Engine:
         sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
         return samples, sample_off
 
+    def upload_parts(self, clips: list[np.ndarray], fractions=(1 / 16, 1 / 4)):
+        """upload() in parts, for callers that start on each part while the next is still
+        on its way: yields (first clip, end clip, samples, sample_off) per part, the copy
+        of each part (on the engine's copy stream) ordered before the current stream's
+        next work. Parts are contiguous clip ranges ending at these fractions of the
+        samples: a small first part leaves little of the transfer exposed, and each later
+        part is packed and copied while the previous one is computed."""
+        pcm = len(clips) > 0 and all(c.dtype == np.int16 for c in clips)
+        tdt = torch.int16 if pcm else torch.float32
+        sizes = np.array([len(c) for c in clips], np.int64)
+        off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+        total = int(off[-1])
+        if self._staged is not None:
+            self._staged.synchronize()
+        nbytes = (total + 1) * (2 if pcm else 4)
+        if self._pinned is None or self._pinned.numel() < nbytes:
+            self._pinned = torch.empty(max(nbytes, int(nbytes * 1.25)), dtype=torch.uint8).pin_memory()
+        staged = self._pinned[:nbytes].view(tdt)
+        hv = staged.numpy()
+        samples = torch.empty(total, device=self.device, dtype=tdt)
+        if self._copy is None:
+            self._copy = torch.cuda.Stream(self.device)
+        cur = torch.cuda.current_stream(self.device)
+        self._copy.wait_stream(cur)
+        cuts = np.searchsorted(off, [f * total for f in fractions]).tolist()
+        edges = [0, *sorted(set(c for c in cuts if 0 < c < len(clips))), len(clips)]
+
+        def pack(i: int) -> None:
+            hv[off[i] : off[i + 1]] = clips[i]
+
+        for a, b in zip(edges[:-1], edges[1:]):
+            list(self._pool().map(pack, range(a, b)))
+            with torch.cuda.stream(self._copy):
+                samples[off[a] : off[b]].copy_(staged[off[a] : off[b]], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(self._copy)
+            cur.wait_event(ready)
+            sub_off = torch.from_numpy(off[a : b + 1] - off[a]).pin_memory().to(self.device, non_blocking=True)
+            yield a, b, samples[off[a] : off[b]], sub_off
+        self._staged = ready
+        samples.record_stream(self._copy)
+
     def _pool(self):
         if self._threads is None:
             from concurrent.futures import ThreadPoolExecutor
@@ -386,14 +435,60 @@ class Engine:
         if not keep:
             return out
         with torch.cuda.device(self.device):
-            plan = self.plan([frames[i] for i in keep])
-            samples, sample_off = self.upload([clips[i] for i in keep])
-            feats = self.features(samples, sample_off, plan)
-            enc = self.encode(feats, plan)
-            tokens, counts = self.decode(enc, plan)
-            tok = tokens.cpu().numpy()
-            cnt = counts.cpu().numpy()
-            self.check()
+            kf = [frames[i] for i in keep]
+            plan = self.plan(kf)
+            t3_off = np.concatenate([[0], np.cumsum(plan.t3)]).astype(np.int64)
+            enc = torch.empty(plan.batch.t3_total, L.PRED, device=self.device, dtype=torch.float32)
+            # Front-end and encoder part by part, each part's samples copied while the
+            # previous part is computed; one decode over every lane.
+            for a, b, samples, sample_off in self.upload_parts([clips[i] for i in keep]):
+                sub = plan if (a, b) == (0, len(keep)) else self.plan(kf[a:b])
+                feats = self.features(samples, sample_off, sub)
+                self.encode(feats, sub, out=enc[t3_off[a] : t3_off[b]])
+            lists = self.decode_lists(enc, plan)
         for j, i in enumerate(keep):
-            out[i] = tok[j, : cnt[j]].tolist()
+            out[i] = lists[j]
         return out
+
+    def decode_lists(self, enc: torch.Tensor, plan: Plan) -> list[list[int]]:
+        """decode(), with each lane's tokens as a Python list. With the persistent decoder
+        (bf16) the lanes that have stopped are copied out and converted while the loop is
+        still running: the kernel publishes a row bound every few iterations (lanes at or
+        above it are final), so little conversion is left once it ends."""
+        n, cap = plan.batch.clips, plan.max_cap
+        if self.dtype != L.BF16:
+            tokens, counts = self.decode(enc, plan)
+            tok, cnt = tokens.cpu().numpy(), counts.cpu().numpy()
+            self.check()
+            return [tok[j, : cnt[j]].tolist() for j in range(n)]
+        flag = self.host_flag.numpy()
+        flag[0], flag[1] = n, -1
+        tokens, counts = self.decode(enc, plan)
+        done = torch.cuda.Event()
+        done.record()
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        if self._tok_host is None or self._tok_host.numel() < n * cap + n:
+            self._tok_host = torch.empty(int((n * cap + n) * 1.25), dtype=torch.int32).pin_memory()
+        tok_h = self._tok_host[: n * cap].view(n, cap)
+        cnt_h = self._tok_host[n * cap : n * cap + n]
+        tk, cn = tok_h.numpy(), cnt_h.numpy()
+        lists: list[list[int]] = [[] for _ in range(n)]
+        hi = n  # lanes [hi, n) are converted
+        while hi > 0:
+            finished = done.query()
+            bound = 0 if finished else max(0, min(int(flag[0]), hi))
+            if bound < hi:
+                with torch.cuda.stream(self._side):
+                    tok_h[bound:hi].copy_(tokens[bound:hi], non_blocking=True)
+                    cnt_h[bound:hi].copy_(counts[bound:hi], non_blocking=True)
+                    copied = torch.cuda.Event()
+                    copied.record(self._side)
+                copied.synchronize()
+                for j in range(bound, hi):
+                    lists[j] = tk[j, : cn[j]].tolist()
+                hi = bound
+            elif not finished:
+                time.sleep(2e-4)
+        self.check()
+        return lists
