@@ -375,7 +375,9 @@ def run_ours(args):
             "stages_ms_rank0": stages,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
                          "frac": achieved / tflops, "traffic": traffic,
-                         "kernel": f"gemm_tc_kernel<256> FFN up M={M} N=4096 K=1024, timed alone",
+                         "kernel": (f"gemm_tc2_kernel (CTA pairs, 256 x 256 tiles) FFN up M={M} N=4096 K=1024, "
+                                    "timed alone" if M >= 2048 else
+                                    f"gemm_tc_kernel<256> FFN up M={M} N=4096 K=1024, timed alone"),
                          "peak_kind": f"{kind} burst bf16"},
             "cpu_baseline": base,
             "e2e": {"value": total_audio / (e2e_ms / 1000.0), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,

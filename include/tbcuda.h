@@ -231,6 +231,12 @@ int tb_layernorm(const float* x, const float* w, const float* b, float* x_out, c
  * CUDA-core fp32 kernel (K % 16 == 0, N % 128 == 0). */
 int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue* epi,
             int* err, void* stream);
+/* Large bf16 GEMMs (at least 2048 rows, N % 256 == 0, no run-time row bound, epilogue
+ * STORE, SILU, RESIDUAL, BIAS_RELU, GLU or QKV) run on CTA pairs, 256 x 256 tiles with
+ * 256-row MMAs over two SMs' shared memory. on = 0 makes the calling thread's later
+ * GEMMs take one CTA per 128-row tile instead (the same results, bit for bit); returns
+ * the previous setting. No reference counterpart: a tuning and test switch. */
+int tb_set_gemm_pairs(int on);
 
 /* ---- relative-position MHSA core: tinybark/tinygrad/model.py:99-116 (_attention),
  * tinybark/mojo/bark/gpu.mojo:202-224 (softmax_kernel) ----

@@ -80,6 +80,62 @@ def test_gemm_silu_residual_relu(L, dtype, err):
     assert max_rel(out.float().cpu(), torch.relu(ref + bias.double()).cpu()) < TOL[dtype]
 
 
+@pytest.mark.parametrize("m", [2100, 2500])
+@pytest.mark.parametrize("kind", ["store", "silu", "residual", "bias_relu", "glu", "qkv"])
+def test_gemm_pairs_match_single_cta(L, err, kind, m):
+    """bf16 GEMMs of at least 2048 rows run on CTA pairs (256 x 256 tiles, 256-row MMAs
+    over two SMs); with the pairs switched off the same call takes one CTA per 128-row
+    tile. Both give the same bits, and both match the float64 reference. m = 2100 leaves
+    the second CTA of the last row pair entirely past the last row, m = 2500 partly."""
+    n, k = {"store": (512, 256), "silu": (1024, 512), "residual": (256, 1024), "bias_relu": (256, 128),
+            "glu": (2048, 256), "qkv": (3072, 128)}[kind]
+    a, w, ref = operands(1, m, n, k, seed=21)
+    bias = torch.randn(n, device="cuda")
+    u, v = torch.randn(1024, device="cuda"), torch.randn(1024, device="cuda")
+    res0 = torch.randn(m, n, device="cuda")
+    results = []
+    for pairs in (1, 0):
+        outs = [torch.full((m, 1024 if kind == "qkv" else (n // 2 if kind == "glu" else n)), float("nan"),
+                           device="cuda", dtype=torch.float32 if kind in ("store", "residual") else torch.bfloat16)
+                for _ in range(4 if kind == "qkv" else 1)]
+        if kind == "residual":
+            outs[0].copy_(res0)
+        ep = {"store": lambda: L.Epilogue(kind=L.EPI_STORE, out_dtype=0, out=outs[0].data_ptr(), ldo=n,
+                                          bias=bias.data_ptr()),
+              "silu": lambda: L.Epilogue(kind=L.EPI_SILU, out_dtype=1, out=outs[0].data_ptr(), ldo=n),
+              "residual": lambda: L.Epilogue(kind=L.EPI_RESIDUAL, out=outs[0].data_ptr(), ldo=n, alpha=0.5),
+              "bias_relu": lambda: L.Epilogue(kind=L.EPI_BIAS_RELU, out_dtype=1, out=outs[0].data_ptr(), ldo=n,
+                                              bias=bias.data_ptr()),
+              "glu": lambda: L.Epilogue(kind=L.EPI_GLU, out_dtype=1, out=outs[0].data_ptr(), ldo=n // 2),
+              "qkv": lambda: L.Epilogue(kind=L.EPI_QKV, out_dtype=1, out=outs[0].data_ptr(), out2=outs[1].data_ptr(),
+                                        out3=outs[2].data_ptr(), out4=outs[3].data_ptr(), ldo=1024,
+                                        bias_u=u.data_ptr(), bias_v=v.data_ptr())}[kind]()
+        was = L.lib.tb_set_gemm_pairs(pairs)
+        try:
+            gemm(L, 1, a, w, ep, err)
+        finally:
+            L.lib.tb_set_gemm_pairs(was)
+        results.append([o.float().cpu() for o in outs])
+    for x, y in zip(*results):
+        assert torch.equal(x, y)
+    got = results[0]
+    if kind == "store":
+        want = [ref + bias.double()]
+    elif kind == "silu":
+        want = [F.silu(ref)]
+    elif kind == "residual":
+        want = [res0.double() + 0.5 * ref]
+    elif kind == "bias_relu":
+        want = [torch.relu(ref + bias.double())]
+    elif kind == "glu":
+        want = [ref[:, 0::2] * torch.sigmoid(ref[:, 1::2])]
+    else:
+        q = ref[:, :1024]
+        want = [q + u.double(), q + v.double(), ref[:, 1024:2048], ref[:, 2048:]]
+    for g, wnt in zip(got, want):
+        assert max_rel(g, wnt.cpu()) < TOL[1]
+
+
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_gemm_glu(L, dtype, err):
     m, n, k = 200, 2048, 256

@@ -81,6 +81,7 @@ def _load() -> C.CDLL:
         "tb_frontend_static": (i32, [P(Model), vp, vp, vp, i32, i32, vp, vp]),
         "tb_layernorm": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
         "tb_gemm": (i32, [i32, vp, ll, vp, i32, i32, i32, P(Epilogue), vp, vp]),
+        "tb_set_gemm_pairs": (i32, [i32]),
         "tb_relpos_attention": (i32, [i32, vp, vp, vp, vp, vp, vp, i32, P(Batch), vp, vp, vp]),
         "tb_conv_depthwise": (i32, [i32, vp, vp, vp, P(Batch), vp, vp]),
         "tb_subsample_workspace_bytes": (sz, [i32, i32, i32]),
@@ -103,7 +104,7 @@ lib = _load()
 EXPORTS = (
     "tb_version", "tb_tile_rows", "tb_launch_count", "tb_last_cuda_error", "tb_sm_count", "tb_frontend_workspace_bytes", "tb_frontend",
     "tb_frontend_static", "tb_frontend_pcm16",
-    "tb_layernorm", "tb_gemm", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
+    "tb_layernorm", "tb_gemm", "tb_set_gemm_pairs", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
     "tb_selftest_wait",
 )

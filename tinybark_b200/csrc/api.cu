@@ -57,6 +57,9 @@ EncodeTiledFn tensor_map_encoder() {
 
 static thread_local int g_sm_budget = 0;
 void set_sm_budget(int n) { g_sm_budget = n; }
+static thread_local bool g_gemm_pairs = true;
+bool gemm_pairs() { return g_gemm_pairs; }
+void set_gemm_pairs(bool on) { g_gemm_pairs = on; }
 int sm_budget() {
   const int s = sm_count();
   return g_sm_budget > 0 && g_sm_budget < s ? g_sm_budget : s;
@@ -251,6 +254,12 @@ int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n
             int* err, void* stream) {
   if (!epi) return TB_ERR_ARG;
   return gemm(dtype, a, lda, w, m, n, k, *epi, err, as_stream(stream));
+}
+
+int tb_set_gemm_pairs(int on) {
+  const int was = gemm_pairs() ? 1 : 0;
+  set_gemm_pairs(on != 0);
+  return was;
 }
 
 int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,

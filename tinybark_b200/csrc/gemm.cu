@@ -13,6 +13,8 @@
 // over more SMs.
 // fp32: a CUDA-core kernel, 128 x 128 tiles, 8 x 8 outputs per thread, for the fp32
 // parity path.
+#include <algorithm>
+
 #include "host.h"
 #include "tcgemm.cuh"
 
@@ -161,6 +163,164 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------
+// tcgen05 bf16 kernel on CTA pairs: 256 x 256 tiles, each SM of the pair loading its
+// 128 rows of A and 128 of the 256 W rows per k-block (32 KB instead of the 48 KB a
+// 128 x 256 tile on one SM needs), the leader issuing 256-row MMAs over both SMs'
+// shared memory. Roles as in gemm_tc_kernel; the loads of both CTAs complete on the
+// leader's `full` barriers, the leader's commits arrive on both CTAs' `empty` and
+// `tfull` barriers, and both CTAs' epilogue warps release an accumulator on the
+// leader's `tempty`. Every CTA runs the epilogue of its own 128 rows, with eight
+// warps: two per tensor-memory lane quarter, each taking 128 of the 256 columns (a
+// pair waits for the slower of its two epilogues, so they must keep well ahead of the
+// main loop).
+
+struct Tc2Cfg {
+  static constexpr int BM = 128, BN = 256, BK = 64, STAGES = 5, EPI_WARPS = 8, THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int OUT_BYTES = EPI_WARPS * 32 * TC_OUT_STRIDE * 4;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + 256;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(Tc2Cfg::THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
+                    const tb_epilogue e, int* err) {
+  using C = Tc2Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* out_stage = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+  TcBars* bars = reinterpret_cast<TcBars*>(smem + C::STAGES * C::STAGE_BYTES + C::OUT_BYTES);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);   // the leader's: its producer's arrival + both CTAs' bytes
+      mbar_init(&bars->empty[s], 1);  // the leader's commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->tfull[a], 1);   // the leader's commit
+      mbar_init(&bars->tempty[a], 2 * C::EPI_WARPS);  // the leader's: every epilogue warp of both CTAs
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair(&bars->tmem, C::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+  grid_dep_wait();
+  grid_dep_launch();
+
+  const int m_pairs = (M + 2 * C::BM - 1) / (2 * C::BM), n_tiles = N / C::BN, tiles = m_pairs * n_tiles;
+  const int kb_count = K / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tw);
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        const int mt = t / n_tiles, nt = t % n_tiles;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, err, TB_DEV_GEMM_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          if (rank == 0) mbar_expect_tx(&bars->full[s], 2 * C::STAGE_BYTES);
+          const uint32_t full = cluster_addr(&bars->full[s], 0);
+          tma_load_2d_pair(sa, &ta, full, kb * C::BK, mt * 2 * C::BM + (int)rank * C::BM);
+          tma_load_2d_pair(sa + C::A_BYTES, &tw, full, kb * C::BK, nt * C::BN + (int)rank * (C::BN / 2));
+          ++issued;
+          if (++s == C::STAGES) s = 0, ph ^= 1;
+        }
+      }
+      if (!ok && rank == 0) {
+        // Let the copies already in flight land before the CTA exits (both CTAs' copies
+        // complete on the leader's barriers; the peer stays until the final cluster
+        // barrier).
+        long long back = issued < C::STAGES ? issued : C::STAGES;
+        for (long long i = 1; i <= back; ++i) {
+          long long idx = issued - i;
+          drain_wait(&bars->full[idx % C::STAGES], (uint32_t)((idx / C::STAGES) & 1));
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16(2 * C::BM, C::BN);
+      int s = 0, acc = 0;
+      uint32_t ph = 0, acc_ph = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        if (!mbar_wait(&bars->tempty[acc], acc_ph ^ 1, err, TB_DEV_GEMM_TIMEOUT, abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * C::BN;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(&bars->full[s], ph, err, TB_DEV_GEMM_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint64_t ad = sdesc_sw128(sa), bd = sdesc_sw128(sa + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / 16; ++k) umma_f16_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit_pair(cluster_addr(&bars->empty[s], 0));
+          umma_commit_pair(cluster_addr(&bars->empty[s], 1));
+          if (++s == C::STAGES) s = 0, ph ^= 1;
+        }
+        if (!ok) break;
+        umma_commit_pair(cluster_addr(&bars->tfull[acc], 0));
+        umma_commit_pair(cluster_addr(&bars->tfull[acc], 1));
+        if (++acc == 2) acc = 0, acc_ph ^= 1;
+      }
+      // Every MMA issued has completed once this commit arrives.
+      umma_commit_pair(cluster_addr(&bars->done, 0));
+      drain_wait(&bars->done, 0);
+    }
+  } else {
+    const int ew = warp - 2;
+    const int q = warp & 3;      // tensor-memory lane quarter this warp may access
+    const int half = ew >> 2;    // which 128 of the 256 columns
+    float* stage = out_stage + ew * 32 * TC_OUT_STRIDE;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int t = pair; t < tiles; t += pairs) {
+      const int mt = t / n_tiles, nt = t % n_tiles;
+      const int row0 = mt * 2 * C::BM + (int)rank * C::BM + q * 32, n0 = nt * C::BN + half * (C::BN / 2);
+      if (!epilogue_tile<C::BN / 2, EPI>(e, stage,
+                                         tmem + ((uint32_t)(q * 32) << 16) + acc * C::BN + half * (C::BN / 2), row0,
+                                         n0, lane, M, &bars->tfull[acc], acc_ph, err, abort))
+        break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&bars->tempty[acc], 0));
+      if (++acc == 2) acc = 0, acc_ph ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // fp32 CUDA-core kernel
 
 constexpr int SG_BM = 128, SG_BN = 128, SG_BK = 16, SG_PAD = 4;
@@ -300,6 +460,46 @@ static int launch_tc(const void* a, long long lda, const void* w, int m, int n, 
   return launch_pdl(gemm_tc_kernel<BN, EPI>, grid, 192, C::SMEM, stream, ta, tw, m, n, k, e, err);
 }
 
+// The pair kernel: clusters of two CTAs, as many pairs as can be resident at once (at
+// most one per two SMs of the budget) looping over the 256 x 256 tiles.
+template <int EPI>
+static int launch_tc2(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
+                      cudaStream_t stream) {
+  using C = Tc2Cfg;
+  static int max_pairs = -1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (max_pairs < 0) {
+    if (cudaFuncSetAttribute(gemm_tc2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
+      return fail_cuda();
+    int clusters = 0;
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc2_kernel<EPI>, &cfg) != cudaSuccess) return fail_cuda();
+    max_pairs = clusters;
+  }
+  if (max_pairs < 1) return TB_ERR_UNSUPPORTED;
+  CUtensorMap ta, tw;
+  if (!encode_tmap(&ta, a, m, k, lda, C::BM) || !encode_tmap(&tw, w, n, k, k, C::BN / 2)) return TB_ERR_CUDA;
+  const int tiles = ((m + 2 * C::BM - 1) / (2 * C::BM)) * (n / C::BN);
+  int pairs = std::min(std::min(tiles, max_pairs), sm_budget() / 2);
+  if (pairs < 1) pairs = 1;
+  cfg.gridDim = dim3(2 * pairs);
+  cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<EPI>, ta, tw, m, n, k, e, err);
+  return check_launch();
+}
+
 template <int BN>
 static int launch_tc_kind(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e,
                           int* err, cudaStream_t s) {
@@ -318,6 +518,9 @@ static int launch_tc_kind(const void* a, long long lda, const void* w, int m, in
     default: return TB_ERR_ARG;
   }
 }
+
+// Rows from which a GEMM runs on CTA pairs: below, 128-row tiles spread further.
+constexpr int GEMM_PAIR_MIN_ROWS = 2048;
 
 static int pick_bn(int m, int n, int k) {
   // Tile width with the least operand traffic into the busiest SM: waves x (A + B bytes
@@ -345,6 +548,20 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
   if (dtype == TB_BF16) {
     if (k % 64 || lda % 8 || (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
       return TB_ERR_UNSUPPORTED;
+    // Large GEMMs of the encoder on CTA pairs (half the operand traffic per SM); the
+    // decoder's (row bound read at run time, per-row epilogues) on single CTAs.
+    const bool pair_kind = e.kind == TB_EPI_STORE || e.kind == TB_EPI_SILU || e.kind == TB_EPI_RESIDUAL ||
+                           e.kind == TB_EPI_BIAS_RELU || e.kind == TB_EPI_GLU || e.kind == TB_EPI_QKV;
+    if (gemm_pairs() && pair_kind && !e.rows && n % 256 == 0 && m >= GEMM_PAIR_MIN_ROWS) {
+      switch (e.kind) {
+        case TB_EPI_STORE: return launch_tc2<TB_EPI_STORE>(a, lda, w, m, n, k, e, err, stream);
+        case TB_EPI_SILU: return launch_tc2<TB_EPI_SILU>(a, lda, w, m, n, k, e, err, stream);
+        case TB_EPI_RESIDUAL: return launch_tc2<TB_EPI_RESIDUAL>(a, lda, w, m, n, k, e, err, stream);
+        case TB_EPI_BIAS_RELU: return launch_tc2<TB_EPI_BIAS_RELU>(a, lda, w, m, n, k, e, err, stream);
+        case TB_EPI_GLU: return launch_tc2<TB_EPI_GLU>(a, lda, w, m, n, k, e, err, stream);
+        default: return launch_tc2<TB_EPI_QKV>(a, lda, w, m, n, k, e, err, stream);
+      }
+    }
     int bn = pick_bn(m, n, k);
     if (e.kind == TB_EPI_LSTM && bn > 128) bn = n % 128 ? 64 : 128;  // the cell epilogue covers <= 32 units
     switch (bn) {

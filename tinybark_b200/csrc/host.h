@@ -20,6 +20,9 @@ int sm_count();
 // concurrently on several streams each take a share.
 int sm_budget();
 void set_sm_budget(int n);  // 0: all
+// Whether large bf16 GEMMs may run on CTA pairs (this thread's setting; on by default).
+bool gemm_pairs();
+void set_gemm_pairs(bool on);
 int fail_cuda();     // records cudaGetLastError() and returns TB_ERR_CUDA
 int check_launch();  // TB_OK, or fail_cuda() if the last launch failed; counts the launch
 void count_launches(long long n);  // adds kernels run by a graph replay (or removes captured ones)
