@@ -602,7 +602,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
           }
           tc_fence_before();
           __syncwarp();
-          if (ok && lane == 0) mbar_arrive(carried ? &dbars->cempty : &bars->tempty[b]);
+          if (ok && lane == 0) mbar_arrive_relaxed(carried ? &dbars->cempty : &bars->tempty[b]);
           if (carried)
             cph ^= 1;
           else

@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(192, 1)
         break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+      if (lane == 0) mbar_arrive_relaxed(&bars->tempty[acc]);
       if (++acc == 2) acc = 0, acc_ph ^= 1;
     }
   }
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(Tc2Cfg::THREADS, 1)
         break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(cluster_addr(&bars->tempty[acc], 0));
+      if (lane == 0) mbar_arrive_cluster_relaxed(cluster_addr(&bars->tempty[acc], 0));
       if (++acc == 2) acc = 0, acc_ph ^= 1;
     }
   }
