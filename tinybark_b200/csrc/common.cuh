@@ -134,6 +134,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread until the phase completes, for at most
+// `suspend_ns`: a waiting warp then takes no issue slots from the warps sharing its SM
+// sub-partition, and still resumes as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase of `bar` with the given parity to complete. Returns false, with
 // `code` or-ed into *err, after TB_WAIT_NS without completion, or at once if the
 // kernel has already given up (*abort set).
@@ -141,15 +155,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
                                           volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t start = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - start > TB_WAIT_NS) {
-        atomicOr(err, code);
-        *abort = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, 20000)) return true;
+    if (*abort) return false;
+    if (globaltimer() - start > TB_WAIT_NS) {
+      atomicOr(err, code);
+      *abort = 1;
+      return false;
     }
   }
 }

@@ -218,6 +218,9 @@ __device__ bool cta_phase_wait(unsigned* slot, unsigned q, int* err, volatile in
     unsigned v;
     asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(slot)) : "memory");
     if (v >= q) return true;
+    // After a few quick polls, back off briefly between polls: the issue slots go to the
+    // epilogue warp on the same SM sub-partition.
+    if (i >= 8) __nanosleep(32);
     if ((i & 15) == 15) {
       if (*abort) return false;
       if (globaltimer() - start > TB_WAIT_NS) {
