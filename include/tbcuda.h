@@ -34,7 +34,8 @@ enum tb_status {
 enum tb_device_error {
   TB_DEV_GEMM_TIMEOUT = 1 << 0,
   TB_DEV_ATTN_TIMEOUT = 1 << 1,
-  TB_DEV_DECODE_TIMEOUT = 1 << 2
+  TB_DEV_DECODE_TIMEOUT = 1 << 2,
+  TB_DEV_CONV_TIMEOUT = 1 << 3
 };
 
 /* Arithmetic type of a path: fp32 everywhere, or bf16 operands with fp32
@@ -250,9 +251,10 @@ int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k
 
 /* ---- conv module middle: tinybark/tinygrad/model.py:121-124 (_conv: GLU output,
  * depthwise k=9 with folded BatchNorm, SiLU) ----
- * glu: [t3_total, 1024] (dtype) = a * sigmoid(g); out = silu(dw(glu) + b) (dtype). */
+ * glu: [t3_total, 1024] (dtype) = a * sigmoid(g); out = silu(dw(glu) + b) (dtype).
+ * err: device error word (TB_DEV_CONV_TIMEOUT if the bf16 kernel's bounded wait gave up). */
 int tb_conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch* batch, void* out,
-                      void* stream);
+                      int* err, void* stream);
 
 /* ---- subsampling: tinybark/tinygrad/model.py:87-97 (_subsample) ----
  * feats [frames_total, 128] fp32 -> x [t3_total, 1024] fp32. */

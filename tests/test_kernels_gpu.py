@@ -343,17 +343,20 @@ def test_relpos_attention_long_form(L, dtype, err):
 
 
 @pytest.mark.parametrize("dtype", [0, 1])
-def test_depthwise_conv_silu(L, dtype):
-    t3 = [1, 5, 9, 40, 3]
+@pytest.mark.parametrize("t3", [[1, 5, 9, 40, 3], [1, 5, 9, 40, 3, 300, 129, 5000, 33, 700]])
+def test_depthwise_conv_silu(L, dtype, t3, err):
+    """Ragged clips (frames outside a clip read as zero); the second batch has interior
+    tiles and more 32-frame tiles than SMs, so the bf16 kernel's double buffer cycles."""
     b, keep, off = batch_for(L, t3, 32)
     R = off[-1]
     x = torch.randn(R, 1024, device="cuda").to(tdt(dtype))
     w = torch.randn(1024, 9, device="cuda")
     bias = torch.randn(1024, device="cuda")
-    y = torch.empty(R, 1024, device="cuda", dtype=tdt(dtype))
+    y = torch.full((R, 1024), float("nan"), device="cuda", dtype=tdt(dtype))
     L.check(L.lib.tb_conv_depthwise(dtype, x.data_ptr(), w.data_ptr(), bias.data_ptr(), ctypes.byref(b), y.data_ptr(),
-                                    stream()), "tb_conv_depthwise")
+                                    err.data_ptr(), stream()), "tb_conv_depthwise")
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     for c in range(len(t3)):
         s = slice(off[c], off[c + 1])
         ref = F.conv1d(x[s].double().T[None], w.double()[:, None, :], bias.double(), padding=4, groups=1024)[0].T

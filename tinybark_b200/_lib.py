@@ -13,7 +13,8 @@ EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_BIAS_RELU, EPI_GLU, EPI_QKV, EPI_ARGMAX, 
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or dtype", 4: "workspace too small",
           5: "more clips than the library's own scratch holds"}
 FRONTEND_STATIC_MAX_CLIPS = 64
-DEVICE_ERRORS = {1: "GEMM barrier wait timed out", 2: "attention barrier wait timed out", 4: "decode wait timed out"}
+DEVICE_ERRORS = {1: "GEMM barrier wait timed out", 2: "attention barrier wait timed out", 4: "decode wait timed out",
+                 8: "depthwise conv copy wait timed out"}
 
 HIDDEN, HEADS, HEAD_DIM, FFN, KERNEL, CHANNELS, MELS = 1024, 8, 128, 4096, 9, 256, 128
 VOCAB, BLANK, EOS, DURATIONS, PRED = 8193, 8192, 3, 5, 640
@@ -83,7 +84,7 @@ def _load() -> C.CDLL:
         "tb_gemm": (i32, [i32, vp, ll, vp, i32, i32, i32, P(Epilogue), vp, vp]),
         "tb_set_gemm_pairs": (i32, [i32]),
         "tb_relpos_attention": (i32, [i32, vp, vp, vp, vp, vp, vp, i32, P(Batch), vp, vp, vp]),
-        "tb_conv_depthwise": (i32, [i32, vp, vp, vp, P(Batch), vp, vp]),
+        "tb_conv_depthwise": (i32, [i32, vp, vp, vp, P(Batch), vp, vp, vp]),
         "tb_subsample_workspace_bytes": (sz, [i32, i32, i32]),
         "tb_subsample": (i32, [P(Model), P(Batch), vp, vp, vp, sz, vp, vp]),
         "tb_encoder_workspace_bytes": (sz, [i32, i32, i32]),

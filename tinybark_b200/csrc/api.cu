@@ -172,7 +172,7 @@ static int encoder_forward(const tb_model& m, const tb_batch& b, const float* fe
     // x += Conv(LN(x))
     if (int rc = layernorm(w.x, L.norm_w[2], L.norm_b[2], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
     if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.pw1, R, 2 * TB_HIDDEN, TB_HIDDEN, glu, err, s)) return rc;
-    if (int rc = conv_depthwise(dt, w.glu, L.dw_w, L.dw_b, b, w.dwo, s)) return rc;
+    if (int rc = conv_depthwise(dt, w.glu, L.dw_w, L.dw_b, b, w.dwo, err, s)) return rc;
     if (int rc = gemm(dt, w.dwo, TB_HIDDEN, L.pw2, R, TB_HIDDEN, TB_HIDDEN, full, err, s)) return rc;
     // x += 0.5 * FF2(LN(x))
     if (int rc = layernorm(w.x, L.norm_w[3], L.norm_b[3], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
@@ -269,9 +269,9 @@ int tb_relpos_attention(int dtype, const void* qu, const void* qv, const void* k
 }
 
 int tb_conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch* batch, void* out,
-                      void* stream) {
+                      int* err, void* stream) {
   if (!batch) return TB_ERR_ARG;
-  return conv_depthwise(dtype, glu, w, b, *batch, out, as_stream(stream));
+  return conv_depthwise(dtype, glu, w, b, *batch, out, err, as_stream(stream));
 }
 
 size_t tb_subsample_workspace_bytes(int dtype, int t2_total, int t3_total) {

@@ -74,6 +74,48 @@ __device__ __forceinline__ float rcp_newton(float y) {
 __device__ __forceinline__ float fast_sigmoid(float x) { return rcp_newton(1.0f + __expf(fminf(-x, 80.0f))); }
 __device__ __forceinline__ float fast_silu(float x) { return x * fast_sigmoid(x); }
 
+// Two-wide fp32 arithmetic (sm_100 packed f32x2 instructions; each half rounds as the
+// scalar instruction would).
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+  return (unsigned long long)__float_as_uint(v.x) | ((unsigned long long)__float_as_uint(v.y) << 32);
+}
+__device__ __forceinline__ float2 f2_from(unsigned long long b) {
+  return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(r);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(r);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_from(r);
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// Sigmoid of two values: 1 / (1 + 2^(-x log2 e)), the exponential on the MUFU unit (its
+// argument capped at 80 log2 e, where the sigmoid is 0 in fp32 anyway), the reciprocal by
+// the bit-level estimate and two Newton-Raphson steps as rcp_newton, the rest two-wide.
+__device__ __forceinline__ float2 fast_sigmoid2(float2 x) {
+  const float2 t = mul2(x, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 y = add2(make_float2(ex2_approx(fminf(t.x, 115.415f)), ex2_approx(fminf(t.y, 115.415f))),
+                        make_float2(1.0f, 1.0f));
+  float2 r = make_float2(__int_as_float(0x7EF311C3 - __float_as_int(y.x)), __int_as_float(0x7EF311C3 - __float_as_int(y.y)));
+  const float2 ny = make_float2(-y.x, -y.y), two = make_float2(2.0f, 2.0f);
+  r = mul2(r, fma2(ny, r, two));
+  return mul2(r, fma2(ny, r, two));
+}
+__device__ __forceinline__ float2 fast_silu2(float2 x) { return mul2(x, fast_sigmoid2(x)); }
+
 // Float to an unsigned key whose unsigned order is the float order.
 __device__ __forceinline__ uint32_t order_key(float v) {
   uint32_t u = __float_as_uint(v);

@@ -34,7 +34,7 @@ int layernorm(const float* x, const float* w, const float* b, float* x_out, cons
               int y_dtype, int rows, cudaStream_t stream);
 int relpos_attention(int dtype, const void* qu, const void* qv, const void* k, const void* v, const void* rel,
                      const float* rel_c, int max_len, const tb_batch& batch, void* out, int* err, cudaStream_t stream);
-int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch& batch, void* out,
+int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch& batch, void* out, int* err,
                    cudaStream_t stream);
 int subsample(const tb_model& m, const tb_batch& batch, const float* feats, float* x, void* ws, size_t ws_bytes,
               int* err, cudaStream_t stream);

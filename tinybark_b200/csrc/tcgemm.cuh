@@ -174,13 +174,16 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
     // All 32 activations first (independent chains the scheduler can interleave), then
     // the stores.
 #pragma unroll
-    for (int it = 0; it < 8; ++it)
-      v[it] = make_float4(fast_silu(v[it].x), fast_silu(v[it].y), fast_silu(v[it].z), fast_silu(v[it].w));
+    for (int it = 0; it < 8; ++it) {
+      const float2 lo = fast_silu2(make_float2(v[it].x, v[it].y)), hi = fast_silu2(make_float2(v[it].z, v[it].w));
+      v[it] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
     store_rows4(e, v, row0, sub, n, M);
   } else if constexpr (EPI == TB_EPI_GLU) {
     float2 g[8];
 #pragma unroll
-    for (int it = 0; it < 8; ++it) g[it] = make_float2(v[it].x * fast_sigmoid(v[it].y), v[it].z * fast_sigmoid(v[it].w));
+    for (int it = 0; it < 8; ++it)
+      g[it] = mul2(make_float2(v[it].x, v[it].z), fast_sigmoid2(make_float2(v[it].y, v[it].w)));
     if (e.out_dtype == TB_BF16) {
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out);
 #pragma unroll

@@ -82,7 +82,7 @@ def attention(qu, qv, k, v, rel, max_len: int, frames: Frames, out, rel_c=None) 
 
 def depthwise(x, w, b, frames: Frames, y) -> None:
     L.check(L.lib.tb_conv_depthwise(dtype_of(x), x.data_ptr(), w.data_ptr(), b.data_ptr(), C.byref(frames.batch),
-                                    y.data_ptr(), _stream()), "tb_conv_depthwise")
+                                    y.data_ptr(), _err(x.device).data_ptr(), _stream()), "tb_conv_depthwise")
 
 
 def check(device=None) -> None:
