@@ -87,16 +87,17 @@ __global__ void __launch_bounds__(256, 2) depthwise_silu_kernel(const T* __restr
 // bf16: one persistent CTA per SM streams tiles of DWS_R output frames. A tile and its
 // 4-frame halo on each side are one contiguous span of [rows, 1024] bf16 (80 KB), fetched
 // with a single bulk copy (no multicast) into one of two shared-memory buffers while the
-// other tile is computed. Each of 256 threads slides 4 channels down the tile: the 9
+// other tile is computed. Each of 512 threads slides 2 channels down the tile: the 9
 // input frames of the current output frame in registers (fp32), each frame read from
-// shared memory once, two-wide FMAs, and whole 8-byte row segments out (a warp writes
-// 256 contiguous bytes per frame). Tiles whose frames and halo all lie in one clip skip
+// shared memory once, two-wide FMAs, and whole row segments out (a warp writes 128
+// contiguous bytes per frame). Sixteen warps per SM hide the FMA and SiLU latencies. Tiles whose frames and halo all lie in one clip skip
 // the per-tap clip tests.
 constexpr int DWS_R = 32;
 constexpr int DWS_ROWS = DWS_R + 2 * DW_HALO;
 constexpr int DWS_ROW_BYTES = TB_HIDDEN * 2;
 constexpr int DWS_TILE_BYTES = DWS_ROWS * DWS_ROW_BYTES;
 constexpr int DWS_SMEM = 2 * DWS_TILE_BYTES + 64;
+constexpr int DWS_THREADS = TB_HIDDEN / 2;  // two channels per thread
 
 __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -105,7 +106,7 @@ __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_
                : "memory");
 }
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(DWS_THREADS, 1)
     depthwise_stream_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
                             const float* __restrict__ b, const int* __restrict__ row_clip, const int* __restrict__ off,
                             int rows, __nv_bfloat16* __restrict__ y, int* err) {
@@ -113,15 +114,12 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(dws_smem + 2 * DWS_TILE_BYTES);
   int* abort_flag = reinterpret_cast<int*>(dws_smem + 2 * DWS_TILE_BYTES + 16);
   volatile int* abort = abort_flag;
-  const int c0 = threadIdx.x * 4;
-  // This thread's taps and biases as channel pairs (c0, c0+1), (c0+2, c0+3).
-  float2 wk[TB_KERNEL][2];
+  const int c0 = threadIdx.x * 2;
+  // This thread's taps and biases for channels c0, c0 + 1.
+  float2 wk[TB_KERNEL];
 #pragma unroll
-  for (int k = 0; k < TB_KERNEL; ++k) {
-    wk[k][0] = make_float2(w[c0 * TB_KERNEL + k], w[(c0 + 1) * TB_KERNEL + k]);
-    wk[k][1] = make_float2(w[(c0 + 2) * TB_KERNEL + k], w[(c0 + 3) * TB_KERNEL + k]);
-  }
-  const float2 bias0 = make_float2(b[c0], b[c0 + 1]), bias1 = make_float2(b[c0 + 2], b[c0 + 3]);
+  for (int k = 0; k < TB_KERNEL; ++k) wk[k] = make_float2(w[c0 * TB_KERNEL + k], w[(c0 + 1) * TB_KERNEL + k]);
+  const float2 bias0 = make_float2(b[c0], b[c0 + 1]);
   if (threadIdx.x == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
@@ -151,53 +149,47 @@ __global__ void __launch_bounds__(256, 1)
     }
     if (!mbar_wait(&bar[s], (uint32_t)((k >> 1) & 1), err, TB_DEV_CONV_TIMEOUT, abort)) break;
     const uint8_t* tile = dws_smem + s * DWS_TILE_BYTES + c0 * 2;
-    auto frame = [&](int i, float2& lo, float2& hi) {  // smem row i, this thread's 4 channels
-      const uint2 u = *reinterpret_cast<const uint2*>(tile + i * DWS_ROW_BYTES);
-      lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-      hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    auto frame = [&](int i) {  // smem row i, this thread's 2 channels
+      return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(tile + i * DWS_ROW_BYTES));
     };
     const int r0 = t * DWS_R;
     const bool interior = r0 >= DW_HALO && r0 + DWS_R + DW_HALO <= rows &&
                           row_clip[r0 - DW_HALO] == row_clip[r0 + DWS_R + DW_HALO - 1];
-    float2 win[TB_KERNEL][2];  // frames o-4 .. o+4 of output frame o
+    float2 win[TB_KERNEL];  // frames o-4 .. o+4 of output frame o
 #pragma unroll
-    for (int i = 0; i < TB_KERNEL - 1; ++i) frame(i, win[i][0], win[i][1]);
+    for (int i = 0; i < TB_KERNEL - 1; ++i) win[i] = frame(i);
     if (interior) {
 #pragma unroll
       for (int o = 0; o < DWS_R; ++o) {
-        frame(o + TB_KERNEL - 1, win[TB_KERNEL - 1][0], win[TB_KERNEL - 1][1]);
-        float2 a0 = bias0, a1 = bias1;
+        win[TB_KERNEL - 1] = frame(o + TB_KERNEL - 1);
+        float2 a0 = bias0;
 #pragma unroll
-        for (int q = 0; q < TB_KERNEL; ++q) a0 = fma2(wk[q][0], win[q][0], a0), a1 = fma2(wk[q][1], win[q][1], a1);
+        for (int q = 0; q < TB_KERNEL; ++q) a0 = fma2(wk[q], win[q], a0);
         a0 = fast_silu2(a0);
-        a1 = fast_silu2(a1);
-        *reinterpret_cast<uint2*>(y + (long long)(r0 + o) * TB_HIDDEN + c0) =
-            make_uint2(pack_bf16x2(a0.x, a0.y), pack_bf16x2(a1.x, a1.y));
+        *reinterpret_cast<uint32_t*>(y + (long long)(r0 + o) * TB_HIDDEN + c0) = pack_bf16x2(a0.x, a0.y);
 #pragma unroll
-        for (int q = 0; q < TB_KERNEL - 1; ++q) win[q][0] = win[q + 1][0], win[q][1] = win[q + 1][1];
+        for (int q = 0; q < TB_KERNEL - 1; ++q) win[q] = win[q + 1];
       }
     } else {
 #pragma unroll
       for (int o = 0; o < DWS_R; ++o) {
         const int r = r0 + o;
         // Frames past the last are neither loaded nor used (their taps fall outside every clip).
-        if (r + DW_HALO < rows) frame(o + TB_KERNEL - 1, win[TB_KERNEL - 1][0], win[TB_KERNEL - 1][1]);
+        if (r + DW_HALO < rows) win[TB_KERNEL - 1] = frame(o + TB_KERNEL - 1);
         if (r < rows) {
           const int clip = row_clip[r];
           const int lo = off[clip] - r, hi = off[clip + 1] - r;  // valid tap offsets: lo <= q-4 < hi
-          float2 a0 = bias0, a1 = bias1;
+          float2 a0 = bias0;
 #pragma unroll
           for (int q = 0; q < TB_KERNEL; ++q) {
             const int d = q - DW_HALO;
-            if (d >= lo && d < hi) a0 = fma2(wk[q][0], win[q][0], a0), a1 = fma2(wk[q][1], win[q][1], a1);
+            if (d >= lo && d < hi) a0 = fma2(wk[q], win[q], a0);
           }
           a0 = fast_silu2(a0);
-          a1 = fast_silu2(a1);
-          *reinterpret_cast<uint2*>(y + (long long)r * TB_HIDDEN + c0) =
-              make_uint2(pack_bf16x2(a0.x, a0.y), pack_bf16x2(a1.x, a1.y));
+          *reinterpret_cast<uint32_t*>(y + (long long)r * TB_HIDDEN + c0) = pack_bf16x2(a0.x, a0.y);
         }
 #pragma unroll
-        for (int q = 0; q < TB_KERNEL - 1; ++q) win[q][0] = win[q + 1][0], win[q][1] = win[q + 1][1];
+        for (int q = 0; q < TB_KERNEL - 1; ++q) win[q] = win[q + 1];
       }
     }
     __syncthreads();  // every thread is done with buffer s before it is refilled
@@ -230,7 +222,7 @@ int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, c
     }
     const int tiles = (rows + DWS_R - 1) / DWS_R;
     const int grid = std::min(tiles, sm_budget());
-    return launch_pdl(depthwise_stream_kernel, grid, 256, DWS_SMEM, stream, reinterpret_cast<const __nv_bfloat16*>(glu),
+    return launch_pdl(depthwise_stream_kernel, grid, DWS_THREADS, DWS_SMEM, stream, reinterpret_cast<const __nv_bfloat16*>(glu),
                       w, b, bt.t3_clip, bt.t3_off, rows, reinterpret_cast<__nv_bfloat16*>(out), err);
   }
   if (dtype == TB_F32) {

@@ -436,15 +436,22 @@ class Engine:
             return out
         with torch.cuda.device(self.device):
             kf = [frames[i] for i in keep]
-            plan = self.plan(kf)
-            t3_off = np.concatenate([[0], np.cumsum(plan.t3)]).astype(np.int64)
-            enc = torch.empty(plan.batch.t3_total, L.PRED, device=self.device, dtype=torch.float32)
+            t3 = np.asarray(kf, np.int64)
+            for _ in range(3):
+                t3 = (t3 - 1) // 2 + 1  # the three stride-2 subsampling stages
+            t3_off = np.concatenate([[0], np.cumsum(t3)]).astype(np.int64)
+            enc = torch.empty(int(t3_off[-1]), L.PRED, device=self.device, dtype=torch.float32)
             # Front-end and encoder part by part, each part's samples copied while the
-            # previous part is computed; one decode over every lane.
+            # previous part is computed; one decode over every lane. The whole batch's plan
+            # (for the decode) is built once the first part's work is queued.
+            plan = None
             for a, b, samples, sample_off in self.upload_parts([clips[i] for i in keep]):
-                sub = plan if (a, b) == (0, len(keep)) else self.plan(kf[a:b])
+                whole = (a, b) == (0, len(keep))
+                sub = self.plan(kf if whole else kf[a:b])
                 feats = self.features(samples, sample_off, sub)
                 self.encode(feats, sub, out=enc[t3_off[a] : t3_off[b]])
+                if plan is None:
+                    plan = sub if whole else self.plan(kf)
             lists = self.decode_lists(enc, plan)
         for j, i in enumerate(keep):
             out[i] = lists[j]
