@@ -554,6 +554,22 @@ def run_longform(args, dev, tflops):
     print(json.dumps({"kernel": "longform_10min", "dtype": "bf16", "audio_s": seconds, "T": T, "layers": args.layers,
                       "stages_ms": split, "rtfx": seconds / (total / 1000), "encoder_tflops": enc_flop / split["encoder"] / 1e9,
                       "encoder_frac": enc_flop / split["encoder"] / 1e9 / tflops}), flush=True)
+    # The same recording in pieces of at most 30 s (Bark.tokens_long), end to end from the
+    # host array: front-end, encoder and decode of all pieces as one batch.
+    from tinybark_b200 import longform
+
+    cuts = longform.cut_points(clip)
+    for _ in range(2):
+        bark.tokens_long(clip)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        bark.tokens_long(clip)
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1000 / reps
+    print(json.dumps({"kernel": "longform_10min_pieces", "dtype": "bf16", "audio_s": seconds, "pieces": len(cuts) - 1,
+                      "layers": args.layers, "e2e_ms": ms, "rtfx": seconds / (ms / 1000)}), flush=True)
 
 
 def stage_split(eng, samples, sample_off, plan, groups=None):

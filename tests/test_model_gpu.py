@@ -195,6 +195,25 @@ def test_tokens_batch_parts_match_whole_batch_path():
     assert got == want
 
 
+def test_tokens_long_is_the_pieces_transcribed_together():
+    """A 70 s recording through Bark.tokens_long: its pieces (cut at quiet points, at most
+    30 s each) decoded as one batch give the same tokens as each piece through Bark.tokens
+    alone, joined; a 10 s recording is one piece and equals Bark.tokens."""
+    import tinybark_b200
+    from tinybark_b200 import longform, synthetic, weights
+
+    sd = state_dict(2)
+    bark = tinybark_b200.load("gpu", weights=(weights.convert(sd, synthetic.config(2)), synthetic.config(2)))
+    long = synthetic.to_float(synthetic.clip(70.0, 5, segment=2.0))
+    cuts = longform.cut_points(long)
+    assert len(cuts) == 4
+    pieces = [bark.tokens(long[a:b]) for a, b in zip(cuts[:-1], cuts[1:])]
+    got = bark.tokens_long(long)
+    assert got == longform.join(pieces) and len(got) > 0
+    short = long[: 10 * 16000]
+    assert bark.tokens_long(short) == bark.tokens(short)
+
+
 def test_pcm16_ingest_matches_float_path():
     """int16 PCM goes to the GPU as 16-bit and is converted there (pcm / 32768): the same
     features, bit for bit, and the same tokens as the float32 path of the same audio."""

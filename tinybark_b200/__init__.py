@@ -7,7 +7,8 @@ libtbcuda's C ABI; torch only allocates device memory.
     ids = bark.tokens_batch([a, b, c])     # many clips in one pass
 
 Same API as tinybark's backends (tinybark/backends.py:21-26; tinybark/tinygrad/__init__.py:21-35):
-`device`, `tokens`, `transcribe`, `transcribe_pcm`, plus `tokens_batch` and `close`.
+`device`, `tokens`, `transcribe`, `transcribe_pcm`, plus `tokens_batch`, `tokens_long` /
+`transcribe_long` (long recordings in pieces of at most 30 s) and `close`.
 """
 
 from __future__ import annotations
@@ -64,6 +65,21 @@ class Bark:
         """Token ids of many clips, packed into one GPU pass: float32 samples, or int16 PCM
         (then moved to the GPU as 16-bit and converted there, as pcm / 32768)."""
         return self.engine.tokens_batch(clips)
+
+    def tokens_long(self, samples: np.ndarray, max_seconds: float = 30.0) -> list[int]:
+        """Token ids of a recording of any length, transcribed in pieces of at most
+        `max_seconds` (cut at the quietest 100 ms near each piece's end) that are decoded
+        together as one batch. Up to `max_seconds` this is `tokens`; beyond it, each piece
+        has its own context (no reference counterpart: tinybark transcribes a clip in full
+        context, which for ten minutes means one decoder lane of some 75 000 steps)."""
+        from . import longform
+
+        x = np.asarray(samples).reshape(-1)
+        cuts = longform.cut_points(x, max_seconds)
+        return longform.join(self.engine.tokens_batch([x[a:b] for a, b in zip(cuts[:-1], cuts[1:])]))
+
+    def transcribe_long(self, samples: np.ndarray, max_seconds: float = 30.0) -> str:
+        return self.tokenizer.decode(self.tokens_long(samples, max_seconds))
 
     @property
     def tokenizer(self):
