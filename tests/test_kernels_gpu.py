@@ -272,7 +272,8 @@ def batch_for(L, t3_list, attn_rows):
 
 
 @pytest.mark.parametrize("dtype", [0, 1])
-@pytest.mark.parametrize("t3,max_len", [([1, 2, 7, 33, 130, 64], 256), ([300, 65, 128, 129], 384), ([250], 250)])
+@pytest.mark.parametrize("t3,max_len", [([1, 2, 7, 33, 130, 64], 256), ([300, 65, 128, 129], 384), ([250], 250),
+                                        ([375] * 8 + [7, 200], 384)])
 def test_relpos_attention(L, dtype, t3, max_len, err):
     from tinybark_b200 import kernels
 

@@ -175,7 +175,7 @@ constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, COL_P = 384, TMEM_COLS =
 constexpr float SCALE_LOG2 = 0.12751743074f;
 
 struct Bars {
-  uint64_t q_full, kr_full, kr_empty, v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, done;
+  uint64_t q_full, q_empty, kr_full, kr_empty, v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, o_empty, done;
   uint32_t tmem;
   int abort;
 };
@@ -193,11 +193,18 @@ __device__ __forceinline__ bool att_warp_wait(uint64_t* bar, uint32_t parity, in
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// Persistent: one CTA per SM walks the (query tile, head) items t = blockIdx.x + k * gridDim.x
+// (query tiles come longest clips first, so the strided walk balances the SMs). Every
+// per-tile barrier counts key tiles across items (g below, this CTA's running tile index),
+// so the next item's Q, K and band loads and its first S and BD products overlap the
+// current item's last softmax and its output; q_empty (the item's last S and BD products
+// have read Q) and o_empty (the softmax warps have read the finished O) hand Q's buffer
+// and O's columns to the next item.
 __global__ void __launch_bounds__(192, 1)
     relpos_attention_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tr,
                         const float* __restrict__ rel_c, int max_len, const int* __restrict__ t3_off,
-                        const int* __restrict__ tiles, __nv_bfloat16* __restrict__ out, int* err) {
+                        const int* __restrict__ tiles, int n_items, __nv_bfloat16* __restrict__ out, int* err) {
   using namespace att;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -206,13 +213,24 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   grid_dep_wait();
   grid_dep_launch();
-  const int clip = tiles[2 * blockIdx.x], q0 = tiles[2 * blockIdx.x + 1], head = blockIdx.y;
-  const int base = t3_off[clip], T_ = t3_off[clip + 1] - base;
-  const int nk = (T_ + TK - 1) / TK;
-  const int col0 = head * D;
+  struct Item {
+    int q0, head, base, T, nk, col0;
+  };
+  auto item = [&](int t) {
+    Item it;
+    const int tile = t / TB_HEADS, clip = tiles[2 * tile];
+    it.q0 = tiles[2 * tile + 1];
+    it.head = t % TB_HEADS;
+    it.base = t3_off[clip];
+    it.T = t3_off[clip + 1] - it.base;
+    it.nk = (it.T + TK - 1) / TK;
+    it.col0 = it.head * D;
+    return it;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     mbar_init(&bars->kr_full, 1);
     mbar_init(&bars->kr_empty, 1);
     mbar_init(&bars->v_full, 1);
@@ -221,6 +239,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(&bars->sbd_empty, 4);
     mbar_init(&bars->p_full, 4);
     mbar_init(&bars->o_done, 1);
+    mbar_init(&bars->o_empty, 4);
     mbar_init(&bars->done, 1);
     bars->abort = 0;
     fence_mbar_init();
@@ -237,47 +256,52 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tr);
-      int kr_issued = 0, v_issued = 0;
+      int kr_issued = 0, v_issued = 0, q_issued = 0;
       bool ok = true;
-      mbar_expect_tx(&bars->q_full, Q_BYTES);
-      tma_load_2d(smem + OFF_Q, &tq, &bars->q_full, col0, base + q0);
-      tma_load_2d(smem + OFF_Q + Q_SUB, &tq, &bars->q_full, col0 + 64, base + q0);
-      for (int j = 0; j < nk; ++j) {
-        const int k0 = j * TK;
-        const int band0 = max_len - TQ - q0 + k0;  // may be negative: TMA fills zeros
-        if (!mbar_wait(&bars->kr_empty, (j & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
-          ok = false;
-          break;
+      for (int t = blockIdx.x; t < n_items && ok; t += gridDim.x) {
+        const Item it = item(t);
+        // Q's buffer is free once the previous item's last S and BD products are done.
+        if (q_issued > 0 && !mbar_wait(&bars->q_empty, (q_issued - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
+        mbar_expect_tx(&bars->q_full, Q_BYTES);
+        tma_load_2d(smem + OFF_Q, &tq, &bars->q_full, it.col0, it.base + it.q0);
+        tma_load_2d(smem + OFF_Q + Q_SUB, &tq, &bars->q_full, it.col0 + 64, it.base + it.q0);
+        ++q_issued;
+        for (int j = 0; j < it.nk; ++j) {
+          const int k0 = j * TK;
+          const int band0 = max_len - TQ - it.q0 + k0;  // may be negative: TMA fills zeros
+          if (!mbar_wait(&bars->kr_empty, (kr_issued & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars->kr_full, K_BYTES + R_BYTES);
+          tma_load_2d(smem + OFF_K, &tk, &bars->kr_full, it.col0, it.base + k0);
+          tma_load_2d(smem + OFF_K + K_SUB, &tk, &bars->kr_full, it.col0 + 64, it.base + k0);
+          tma_load_2d(smem + OFF_R, &tr, &bars->kr_full, it.col0, band0);
+          tma_load_2d(smem + OFF_R + R_SUB, &tr, &bars->kr_full, it.col0 + 64, band0);
+          ++kr_issued;
+          if (!mbar_wait(&bars->v_empty, (v_issued & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars->v_full, V_BYTES);
+          tma_load_2d(smem + OFF_V, &tv, &bars->v_full, it.col0, it.base + k0);
+          tma_load_2d(smem + OFF_V + V_SUB, &tv, &bars->v_full, it.col0 + 64, it.base + k0);
+          ++v_issued;
         }
-        mbar_expect_tx(&bars->kr_full, K_BYTES + R_BYTES);
-        tma_load_2d(smem + OFF_K, &tk, &bars->kr_full, col0, base + k0);
-        tma_load_2d(smem + OFF_K + K_SUB, &tk, &bars->kr_full, col0 + 64, base + k0);
-        tma_load_2d(smem + OFF_R, &tr, &bars->kr_full, col0, band0);
-        tma_load_2d(smem + OFF_R + R_SUB, &tr, &bars->kr_full, col0 + 64, band0);
-        ++kr_issued;
-        if (!mbar_wait(&bars->v_empty, (j & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
-          ok = false;
-          break;
-        }
-        mbar_expect_tx(&bars->v_full, V_BYTES);
-        tma_load_2d(smem + OFF_V, &tv, &bars->v_full, col0, base + k0);
-        tma_load_2d(smem + OFF_V + V_SUB, &tv, &bars->v_full, col0 + 64, base + k0);
-        ++v_issued;
       }
-      if (!ok) {
-        // Let the copies in flight land before the CTA exits.
-        att_drain(&bars->q_full, 0);
-        if (kr_issued) att_drain(&bars->kr_full, (kr_issued - 1) & 1);
-        if (v_issued) att_drain(&bars->v_full, (v_issued - 1) & 1);
-      }
+      // Let the copies in flight land before the CTA exits (all have, unless the loop was
+      // abandoned).
+      if (q_issued) att_drain(&bars->q_full, (q_issued - 1) & 1);
+      if (kr_issued) att_drain(&bars->kr_full, (kr_issued - 1) & 1);
+      if (v_issued) att_drain(&bars->v_full, (v_issued - 1) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_bf16(TQ, TK), id_bd = idesc_bf16(TQ, BAND), id_pv = idesc_bf16_bmn(TQ, D);
       const uint32_t qa = smem_u32(smem + OFF_Q), ka = smem_u32(smem + OFF_K), ra = smem_u32(smem + OFF_R),
                      va = smem_u32(smem + OFF_V);
-      // S and BD of tile j + 1 are issued as soon as the softmax has read tile j's (before
-      // tile j's PV), so they overlap the softmax of tile j; P has its own columns.
+      // S and BD of tile g + 1 are issued as soon as the softmax has read tile g's (before
+      // tile g's PV), so they overlap the softmax of tile g; P has its own columns.
       auto sbd = [&]() {
         tc_fence_after();
 #pragma unroll
@@ -295,26 +319,52 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit(&bars->sbd_full);
         umma_commit(&bars->kr_empty);
       };
-      bool ok = mbar_wait(&bars->q_full, 0, err, TB_DEV_ATTN_TIMEOUT, abort);
-      if (ok && nk > 0) {
-        ok = mbar_wait(&bars->kr_full, 0, err, TB_DEV_ATTN_TIMEOUT, abort);
-        if (ok) sbd();
-      }
-      for (int j = 0; j < nk && ok; ++j) {
-        if (j + 1 < nk) {
-          if (!mbar_wait(&bars->kr_full, (j + 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
-          if (!mbar_wait(&bars->sbd_empty, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;  // tile j read
-          sbd();
-        }
-        if (!mbar_wait(&bars->p_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
-        if (!mbar_wait(&bars->v_full, j & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) break;
-        tc_fence_after();
+      bool ok = true;
+      int g = 0, n = 0;  // key tiles and items this CTA has done
+      // Item `items`'s first key tile (this CTA's tile gg), issued as soon as possible: Q
+      // loaded, the tile's K and band loaded, the softmax done reading the S and BD before.
+      auto first_sbd = [&](int items, int gg) {
+        if (!mbar_wait(&bars->q_full, items & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
+        if (!mbar_wait(&bars->kr_full, gg & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
+        if (gg > 0 && !mbar_wait(&bars->sbd_empty, (gg - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
+        sbd();
+        return true;
+      };
+      int t = blockIdx.x;
+      if (t < n_items) ok = first_sbd(0, 0);
+      for (; t < n_items && ok; t += gridDim.x, ++n) {
+        const int nk = item(t).nk;
+        for (int j = 0; j < nk && ok; ++j, ++g) {
+          if (j + 1 < nk) {
+            if (!mbar_wait(&bars->kr_full, (g + 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort) ||
+                !mbar_wait(&bars->sbd_empty, g & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {  // tile g read
+              ok = false;
+              break;
+            }
+            sbd();
+          } else {
+            umma_commit(&bars->q_empty);  // this item's S and BD products are issued: Q is free after them
+          }
+          if (!mbar_wait(&bars->p_full, g & 1, err, TB_DEV_ATTN_TIMEOUT, abort) ||
+              !mbar_wait(&bars->v_full, g & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          // O's columns hold the previous item's result until its softmax warps read it.
+          if (j == 0 && n > 0 && !mbar_wait(&bars->o_empty, (n - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk)
-          umma_f16_ts(tmem + COL_O, tmem + COL_P + 8 * kk, sdesc_sw128_mn(va + 2048 * kk, V_SUB), id_pv,
-                      (j | kk) != 0);
-        umma_commit(&bars->o_done);
-        umma_commit(&bars->v_empty);
+          for (int kk = 0; kk < TK / 16; ++kk)
+            umma_f16_ts(tmem + COL_O, tmem + COL_P + 8 * kk, sdesc_sw128_mn(va + 2048 * kk, V_SUB), id_pv,
+                        (j | kk) != 0);
+          umma_commit(&bars->o_done);
+          umma_commit(&bars->v_empty);
+          // After this item's last PV, start the next item's first S and BD.
+          if (j + 1 == nk && t + (int)gridDim.x < n_items) ok = first_sbd(n + 1, g + 1);
+        }
       }
       umma_commit(&bars->done);
       att_drain(&bars->done, 0);
@@ -327,112 +377,118 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
     const int wcol = 96 - 32 * q;  // first BD column this warp's rows need
     const int rel_rows = 2 * max_len - 1;
-    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     uint32_t r[32];
-    // This warp's window of the (bias_v - bias_u) . r term for key tile j, loaded one
-    // tile ahead so its latency hides behind the previous tile.
-    float cnext[WIN / 32];
-    auto load_cband = [&](int j) {
-      const int band0 = max_len - TQ - q0 + j * TK;
+    int g = 0;  // key tiles this CTA has done
+    for (int t = blockIdx.x; t < n_items && ok; t += gridDim.x) {
+      const Item it = item(t);
+      float m_run = -INFINITY, l_run = 0.f;
+      // This warp's window of the (bias_v - bias_u) . r term for key tile j, loaded one
+      // tile ahead so its latency hides behind the previous tile.
+      float cnext[WIN / 32];
+      auto load_cband = [&](int j) {
+        const int band0 = max_len - TQ - it.q0 + j * TK;
 #pragma unroll
-      for (int t = 0; t < WIN / 32; ++t) {
-        const int n = band0 + wcol + t * 32 + lane;
-        cnext[t] = (n >= 0 && n < rel_rows) ? rel_c[(long long)n * 128 + head] : 0.f;
-      }
-    };
-    load_cband(0);
-    for (int j = 0; j < nk; ++j) {
-      const int k0 = j * TK;
-      __syncwarp();  // every lane is done with the previous tile's cband
+        for (int u = 0; u < WIN / 32; ++u) {
+          const int nn = band0 + wcol + u * 32 + lane;
+          cnext[u] = (nn >= 0 && nn < rel_rows) ? rel_c[(long long)nn * 128 + it.head] : 0.f;
+        }
+      };
+      load_cband(0);
+      for (int j = 0; j < it.nk; ++j, ++g) {
+        const int k0 = j * TK;
+        __syncwarp();  // every lane is done with the previous tile's cband
 #pragma unroll
-      for (int t = 0; t < WIN / 32; ++t) cband[t * 32 + lane] = cnext[t];
-      __syncwarp();
-      if (j + 1 < nk) load_cband(j + 1);
-      if (!att_warp_wait(&bars->sbd_full, j & 1, err, abort)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sc[TK];
-      tmem_ld32(tl + COL_S, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int k = 0; k < 32; ++k) sc[k] = __uint_as_float(r[k]);
-      tmem_ld32(tl + COL_S + 32, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(r[k]);
-#pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
-        tmem_wait_ld();
-        float4* dst = reinterpret_cast<float4*>(stage + lane * ST_STRIDE + 32 * c);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          dst[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]), __uint_as_float(r[4 * k + 2]),
-                               __uint_as_float(r[4 * k + 3]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sbd_empty);
-      // Scores: content + shifted position term, scaled into the base-2 domain.
-      const float* srow = stage + lane * ST_STRIDE + (31 - lane);
-      const float* crow = cband + (31 - lane);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int jj = 0; jj < TK; ++jj) {
-        const float v = (sc[jj] + srow[jj] + crow[jj]) * SCALE_LOG2;
-        sc[jj] = k0 + jj < T_ ? v : -INFINITY;
-        mx = fmaxf(mx, sc[jj]);
-      }
-      // The running max moves only when the row max grows by more than 8 (a factor 256 in
-      // the exponentials, which bf16 P and the fp32 sums hold exactly): O is rescaled far
-      // less often, and the final O / l is the same for any reference max.
-      float corr = 1.0f;
-      if (mx > m_run + 8.0f) {
-        corr = exp2f(m_run - mx);
-        m_run = mx;
-      }
-      const float m_new = m_run;
-      float sum = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < TK; jj += 2) {
-        const float p0 = exp2f(sc[jj] - m_new), p1 = exp2f(sc[jj + 1] - m_new);
-        sum += p0 + p1;
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-        r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      l_run = l_run * corr + sum;
-      if (j > 0) {
-        if (!att_warp_wait(&bars->o_done, (j - 1) & 1, err, abort)) {
+        for (int u = 0; u < WIN / 32; ++u) cband[u * 32 + lane] = cnext[u];
+        __syncwarp();
+        if (j + 1 < it.nk) load_cband(j + 1);
+        if (!att_warp_wait(&bars->sbd_full, g & 1, err, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, corr != 1.0f)) {
-          uint32_t o[32];
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(tl + COL_O + 32 * c, o);
-            tmem_wait_ld();
+        float sc[TK];
+        tmem_ld32(tl + COL_S, r);
+        tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * corr);
-            tmem_st32(tl + COL_O + 32 * c, o);
+        for (int k = 0; k < 32; ++k) sc[k] = __uint_as_float(r[k]);
+        tmem_ld32(tl + COL_S + 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(r[k]);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(stage + lane * ST_STRIDE + 32 * c);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
+                                 __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->sbd_empty);
+        // Scores: content + shifted position term, scaled into the base-2 domain.
+        const float* srow = stage + lane * ST_STRIDE + (31 - lane);
+        const float* crow = cband + (31 - lane);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int jj = 0; jj < TK; ++jj) {
+          const float v = (sc[jj] + srow[jj] + crow[jj]) * SCALE_LOG2;
+          sc[jj] = k0 + jj < it.T ? v : -INFINITY;
+          mx = fmaxf(mx, sc[jj]);
+        }
+        // The running max moves only when the row max grows by more than 8 (a factor 256 in
+        // the exponentials, which bf16 P and the fp32 sums hold exactly): O is rescaled far
+        // less often, and the final O / l is the same for any reference max.
+        float corr = 1.0f;
+        if (mx > m_run + 8.0f) {
+          corr = exp2f(m_run - mx);
+          m_run = mx;
+        }
+        const float m_new = m_run;
+        float sum = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < TK; jj += 2) {
+          const float p0 = exp2f(sc[jj] - m_new), p1 = exp2f(sc[jj + 1] - m_new);
+          sum += p0 + p1;
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+          r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        l_run = l_run * corr + sum;
+        if (j > 0) {
+          if (!att_warp_wait(&bars->o_done, (g - 1) & 1, err, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, corr != 1.0f)) {
+            uint32_t o[32];
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              tmem_ld32(tl + COL_O + 32 * c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * corr);
+              tmem_st32(tl + COL_O + 32 * c, o);
+            }
           }
         }
+        tmem_st32(tl + COL_P, r);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full);
       }
-      tmem_st32(tl + COL_P, r);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full);
-    }
-    if (ok && nk > 0 && att_warp_wait(&bars->o_done, (nk - 1) & 1, err, abort)) {
+      if (!ok || !att_warp_wait(&bars->o_done, (g - 1) & 1, err, abort)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float inv = 1.0f / l_run;
-      const bool valid = q0 + il < T_;
-      __nv_bfloat16* dst = out + (long long)(base + q0 + il) * TB_HIDDEN + col0;
+      const bool valid = it.q0 + il < it.T;
+      __nv_bfloat16* dst = out + (long long)(it.base + it.q0 + il) * TB_HIDDEN + it.col0;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         tmem_ld32(tl + COL_O + 32 * c, r);
@@ -444,6 +500,9 @@ __global__ void __launch_bounds__(192, 1)
                    __uint_as_float(r[k + 2]) * inv, __uint_as_float(r[k + 3]) * inv);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->o_empty);  // O's columns are free for the next item
     }
   }
 
@@ -473,9 +532,10 @@ static int launch_attn_tc(const void* qu, const void* k, const void* v, const vo
       !encode_tmap_2d(&mv, v, rows, TB_HIDDEN, TB_HIDDEN, 64, att::TK) ||
       !encode_tmap_2d(&mr, rel, 2LL * max_len - 1, TB_HIDDEN, TB_HIDDEN, 64, att::BAND))
     return TB_ERR_CUDA;
-  dim3 grid(b.n_attn_tiles, TB_HEADS);
+  const int items = b.n_attn_tiles * TB_HEADS;
+  const int grid = items < sm_budget() ? items : sm_budget();
   return launch_pdl(relpos_attention_tc, grid, 192, att::SMEM, stream, mq, mk, mv, mr, rel_c, max_len, b.t3_off,
-                    b.attn_tiles, reinterpret_cast<__nv_bfloat16*>(out), err);
+                    b.attn_tiles, items, reinterpret_cast<__nv_bfloat16*>(out), err);
 }
 
 template <typename T>
