@@ -283,7 +283,7 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
  * clips (longest first) round-robin into groups gives balanced groups. host_flag:
  * pinned host memory (may be NULL). Graph decoder: 2 ints per group, used to stop a group
  * early once all its lanes are done (NULL: every group runs its longest cap). Persistent
- * decoder: every 8 iterations it stores [1] = the iteration and then [0] = a row bound
+ * decoder: every 32 iterations it stores [1] = the iteration and then [0] = a row bound
  * R such that every lane >= R has stopped with its tokens and counts[] final (the caller
  * may copy those lanes out while the loop goes on; set [0] = lanes before the call).
  * Lanes ordered longest first let the GEMMs shrink to the lanes still running. Both

@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         rows = phase_rows(p, bounds);
         if (rows <= 0) break;
       }
-      if (p.kind == P_JOINT && args.progress && blockIdx.x == 0 && ew == 0 && lane == 0 && (p.iter & 7) == 0) {
+      if (p.kind == P_JOINT && args.progress && blockIdx.x == 0 && ew == 0 && lane == 0 && (p.iter & 31) == 0) {
         // Every lane at or above `rows` has stopped, its tokens and count written before
         // the last barrier: publish the bound to the host, which may copy those lanes out
         // while the loop goes on.

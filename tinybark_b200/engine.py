@@ -374,13 +374,16 @@ class Engine:
         sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
         return samples, sample_off
 
-    def upload_parts(self, clips: list[np.ndarray], fractions=(1 / 16, 1 / 4)):
+    def upload_parts(self, clips: list[np.ndarray], fractions=(1 / 16, 1 / 4, 1 / 2), slice_bytes=64 << 20):
         """upload() in parts, for callers that start on each part while the next is still
         on its way: yields (first clip, end clip, samples, sample_off) per part, the copy
         of each part (on the engine's copy stream) ordered before the current stream's
         next work. Parts are contiguous clip ranges ending at these fractions of the
         samples: a small first part leaves little of the transfer exposed, and each later
-        part is packed and copied while the previous one is computed."""
+        part (at most about three times the one before, the ratio of encoder time to transfer
+        time) is packed and copied while the previous one is computed. Within a part the
+        clips are packed in slices of about `slice_bytes`, each copied as soon as it is
+        packed, so packing and copying overlap."""
         pcm = len(clips) > 0 and all(c.dtype == np.int16 for c in clips)
         tdt = torch.int16 if pcm else torch.float32
         sizes = np.array([len(c) for c in clips], np.int64)
@@ -404,10 +407,17 @@ class Engine:
         def pack(i: int) -> None:
             hv[off[i] : off[i + 1]] = clips[i]
 
+        per = 2 if pcm else 4
         for a, b in zip(edges[:-1], edges[1:]):
-            list(self._pool().map(pack, range(a, b)))
+            # Slices of whole clips, about slice_bytes each.
+            want = max(1, int((off[b] - off[a]) * per // slice_bytes))
+            marks = np.searchsorted(off, np.linspace(off[a], off[b], want + 1)[1:-1]).tolist()
+            sl = [a, *sorted(set(m for m in marks if a < m < b)), b]
+            for c, d in zip(sl[:-1], sl[1:]):
+                list(self._pool().map(pack, range(c, d)))
+                with torch.cuda.stream(self._copy):
+                    samples[off[c] : off[d]].copy_(staged[off[c] : off[d]], non_blocking=True)
             with torch.cuda.stream(self._copy):
-                samples[off[a] : off[b]].copy_(staged[off[a] : off[b]], non_blocking=True)
                 ready = torch.cuda.Event()
                 ready.record(self._copy)
             cur.wait_event(ready)
