@@ -49,7 +49,7 @@ def args_parser():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform,load)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -526,6 +526,61 @@ def run_micro(args):
     K.check(dev)
     if want("longform"):
         run_longform(args, dev, tflops)
+    if want("load"):
+        run_load(args, dev, hbm)
+
+
+def run_load(args, dev, hbm):
+    """Weight loading, tinybark's every-start cost: the converted weights written as
+    tinybark's fp16 cache file (1.25 GB at 24 layers), then that file to a ready bf16
+    engine (data block read into pinned slices and copied to the GPU, one repack kernel,
+    the decoder's input table, position tables up to 30 s), page cache warm from the
+    write. Then the repack kernel on its own against the HBM roofline: algorithmic bytes =
+    the f16 elements read plus the bf16 / f32 elements written."""
+    import tempfile
+
+    import torch
+
+    from tinybark_b200 import _lib as L
+    from tinybark_b200 import lengths, pack
+    from tinybark_b200 import weights as w
+    from tinybark_b200.engine import Engine
+
+    tensors, cfg = weights(args.layers)
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "bark.safetensors"
+        w.save(tensors, path)
+        del tensors
+        size = path.stat().st_size
+        runs = []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            eng = Engine(path, cfg, dtype="bf16", device=dev, max_len=lengths.subsampled(3000, 3))
+            torch.cuda.synchronize()
+            runs.append({"total_s": time.perf_counter() - t0, **{k + "_s": v for k, v in eng.load_seconds.items()}})
+            del eng
+        best = min(runs, key=lambda r: r["total_s"])
+        print(json.dumps({"kernel": "load_cache_file", "layers": args.layers, "file_gb": size / 1e9,
+                          "runs_s": [round(r["total_s"], 4) for r in runs], **{k: round(v, 4) for k, v in best.items()},
+                          "read_copy_gbs": size / 1e9 / best["upload_s"]}), flush=True)
+        src, index = pack.upload_cache(path, dev)
+    lay = pack.model_layout(index, args.layers, L.BF16)
+    out = torch.empty(lay.size, dtype=torch.uint8, device=dev)
+    table, jobs_dev = lay.table(), torch.empty(len(lay.jobs) * 88, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def call():
+        L.check(L.lib.tb_repack(table, len(lay.jobs), jobs_dev.data_ptr(), src.data_ptr(), src.numel(), out.data_ptr(),
+                                out.numel(), stream), "tb_repack")
+
+    for _ in range(3):
+        call()
+    s = timed(call, iters=10)
+    moved = sum(int(np.prod(j[3])) * ((0 if j[6] else (2 if j[4] == L.SRC_F16 else 4)) + (2 if j[5] == L.BF16 else 4))
+                for j in lay.jobs)
+    print(json.dumps({"kernel": "repack_kernel", "layers": args.layers, "jobs": len(lay.jobs), "bytes": moved,
+                      "us": s * 1e6, "gbs": moved / s / 1e9, "frac": moved / s / 1e9 / hbm}), flush=True)
 
 
 def run_longform(args, dev, tflops):

@@ -302,6 +302,37 @@ int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const
                   int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
                   void* stream);
 
+/* ---- weight loading: the fp16 cache (tinybark/weights.py:92-120), read whole as
+ * tinybark/tinygrad/weights.py:10-26 reads it, then split into the kernels' layout ----
+ * tb_repack writes the packed weights from one source buffer: the cache file's data block
+ * uploaded as is (or any buffer of f16 / f32 tensors). Job j writes one contiguous
+ * destination tensor at dst + dst_off of extents dims[0..3] (dims[3] innermost): element
+ * (i0, i1, i2, i3) is source element src_off / size + i0 * stride[0] + i1 * stride[1] +
+ * i2 * stride[2] + i3 * stride[3], converted to dst_type (bf16 rounded to nearest even), or
+ * `value` when fill is 1. Reorderings (gate interleaving, column permutations, slices)
+ * are strides; padding rows are fill jobs.
+ * Every job is checked against src_bytes and dst_bytes before anything runs (TB_ERR_ARG:
+ * a type, an offset not a multiple of its element size, a negative stride, a read or a
+ * write out of range, more than 2^31 - 1 elements). The table is then copied into
+ * jobs_dev (device, at least n_jobs * sizeof(tb_repack_job) bytes, 8-byte aligned) and one
+ * kernel runs, in chunks of TB_REPACK_CHUNK elements spread over the SMs. first_chunk is
+ * filled in by the library. */
+#define TB_REPACK_CHUNK 16384
+enum tb_src_type { TB_SRC_F16 = 0, TB_SRC_F32 = 1 };
+typedef struct {
+  long long src_off;     /* source byte offset */
+  long long dst_off;     /* destination byte offset */
+  long long stride[4];   /* source element stride of each destination index, >= 0 */
+  long long first_chunk; /* set by tb_repack */
+  int dims[4];           /* destination extents, >= 0 */
+  int src_type;          /* TB_SRC_F16 or TB_SRC_F32 (ignored by fill jobs) */
+  int dst_type;          /* TB_F32 or TB_BF16 */
+  int fill;              /* 1: every element is `value` */
+  float value;
+} tb_repack_job;
+int tb_repack(const tb_repack_job* jobs, int n_jobs, void* jobs_dev, const void* src, size_t src_bytes, void* dst,
+              size_t dst_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,3 +47,33 @@ def sd2():
 @pytest.fixture(scope="session")
 def sd24():
     return state_dict(24)
+
+
+def repack_numpy(jobs, source: np.ndarray, size: int) -> np.ndarray:
+    """tb_repack's job semantics restated in numpy (the checker of its kernel and of the
+    packed layout): jobs as pack.Layout.jobs tuples, `source` the source bytes (uint8);
+    returns the `size` destination bytes, zero where no job writes."""
+    import torch
+
+    out = np.zeros(size, np.uint8)
+    for src_off, dst_off, strides, dims, src_type, dst_type, fill, value in jobs:
+        n = int(np.prod(dims))
+        if n == 0:
+            continue
+        if fill:
+            vals = np.full(n, value, np.float32)
+        else:
+            dt = np.float16 if src_type == 0 else np.float32
+            src = source[src_off : src_off + (len(source) - src_off) // dt().itemsize * dt().itemsize].view(dt)
+            idx = np.zeros((1, 1, 1, 1), np.int64)
+            for k, (d, s) in enumerate(zip(dims, strides)):
+                shape = [1, 1, 1, 1]
+                shape[k] = d
+                idx = idx + (np.arange(d, dtype=np.int64) * s).reshape(shape)
+            vals = src[idx.reshape(-1)].astype(np.float32)
+        if dst_type == 1:
+            raw = torch.from_numpy(vals).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint8)
+        else:
+            raw = vals.view(np.uint8)
+        out[dst_off : dst_off + raw.size] = raw
+    return out

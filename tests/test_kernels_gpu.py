@@ -436,3 +436,69 @@ def test_bounded_wait_gives_up_and_reports(L, kind, bit, err):
     gemm(L, 1, a, w, L.Epilogue(kind=L.EPI_STORE, out_dtype=L.F32, out=out.data_ptr(), ldo=256), err)
     assert int(err.item()) == 0
     assert max_rel(out.cpu(), ref.cpu()) < TOL[1]
+
+
+def random_repack_jobs(rng, n16: int, n32: int, off32: int):
+    """Jobs over a source of n16 f16 values at byte 0 and n32 f32 values at byte off32:
+    random 4-D strided reads (repeats and transposes included), a job of many chunks, an
+    empty job, and fills; destinations packed at element-size alignment."""
+    jobs, dst = [], 0
+    for t in range(48):
+        dst_type = int(rng.integers(0, 2))
+        esz = 2 if dst_type == 1 else 4
+        dst = -(-dst // esz) * esz
+        if t == 7:
+            dims = (1, 1, 300, 257)  # 77100 elements: 19 chunks
+        elif t == 20:
+            dims = (3, 0, 5, 2)  # no elements
+        else:
+            dims = tuple(int(d) for d in rng.integers(1, 13, 4))
+        if t % 9 == 4:
+            value = float(rng.choice([0.0, -np.inf, np.inf, 1.5, -3.25e38]))
+            jobs.append((0, dst, (0, 0, 0, 0), dims, 0, dst_type, 1, value))
+        else:
+            f16 = bool(rng.integers(0, 2))
+            n = n16 if f16 else n32
+            strides = tuple(int(s) for s in rng.integers(0, 40, 4)) if t != 7 else (0, 0, 257, 1)
+            reach = sum((d - 1) * s for d, s in zip(dims, strides) if d > 0)
+            base = int(rng.integers(0, n - reach))
+            src_off = (0 if f16 else off32) + base * (2 if f16 else 4)
+            jobs.append((src_off, dst, strides, dims, 0 if f16 else 1, dst_type, 0, 0.0))
+        dst += int(np.prod(dims)) * esz
+    return jobs, dst
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_repack_matches_numpy_on_random_jobs(L, seed):
+    """tb_repack against its numpy restatement, bit for bit: f16 and f32 sources (f16
+    infinities and subnormals; f32 values at bf16 rounding ties and near the f32 maximum,
+    which round to infinity) into f32 and bf16 destinations."""
+    from conftest import repack_numpy
+    from tinybark_b200 import pack
+
+    rng = np.random.default_rng(seed)
+    n16, n32 = 300_000, 200_000
+    a16 = rng.standard_normal(n16).astype(np.float16)
+    a16[:4] = [np.inf, -np.inf, 6e-8, -1e-5]
+    a32 = (rng.standard_normal(n32) * 1e3).astype(np.float32)
+    bits = a32.view(np.uint32)
+    bits[:64] = (bits[:64] & 0xFFFF0000) | 0x8000  # ties: even and odd bf16 mantissas
+    a32[64:66] = [3.4028235e38, -3.4e38]
+    off32 = -(-a16.nbytes // 256) * 256
+    src = np.zeros(off32 + a32.nbytes, np.uint8)
+    src[: a16.nbytes] = a16.view(np.uint8)
+    src[off32:] = a32.view(np.uint8)
+    jobs, size = random_repack_jobs(rng, n16, n32, off32)
+    lay = pack.Layout({}, L.BF16)
+    lay.jobs, lay.size = jobs, size
+    out = torch.full((size + 64,), 0xA5, dtype=torch.uint8, device="cuda")
+    lay.run(torch.from_numpy(src).cuda(), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    want = repack_numpy(jobs, src, size)
+    written = np.zeros(size, bool)
+    for j in jobs:
+        esz = 2 if j[5] == 1 else 4
+        written[j[1] : j[1] + int(np.prod(j[3])) * esz] = True
+    assert np.array_equal(got[:size][written], want[written])
+    assert (got[:size][~written] == 0xA5).all() and (got[size:] == 0xA5).all()  # nothing else touched

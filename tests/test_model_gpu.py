@@ -233,3 +233,35 @@ def test_pcm16_ingest_matches_float_path():
         feats.append(eng.features(s, o, plan).cpu())
     assert torch.equal(feats[0], feats[1])
     assert bark.tokens_batch(pcm) == bark.tokens_batch(flt)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+def test_engine_from_cache_file_equals_engine_from_arrays(tmp_path, dtype):
+    """2 layers written as tinybark's fp16 cache file: the engine that uploads the file's
+    data block as is and repacks it on the GPU holds, byte for byte, the packed weights of
+    the engine built from the same tensors as float32 arrays, and both equal the packed
+    layout's numpy restatement; transcription through tinybark_b200.load on the file gives
+    the same tokens."""
+    import tinybark_b200
+    from conftest import repack_numpy
+    from tinybark_b200 import pack, synthetic, weights
+    from tinybark_b200.engine import Engine
+
+    cfg = synthetic.config(2)
+    path = tmp_path / "bark.safetensors"
+    weights.save(weights.convert(state_dict(2), cfg), path)
+    a = Engine(path, cfg, dtype=dtype)
+    arrays = weights.load(path)
+    b = Engine(arrays, cfg, dtype=dtype)
+    assert a.layout.regions == b.layout.regions
+    assert torch.equal(a._blob, b._blob)
+    offset, _, index = pack.cache_index(path)
+    body = np.fromfile(path, np.uint8)[offset:]
+    pieces, dev_bytes, _ = pack.aligned_runs(index)
+    image = np.zeros(dev_bytes, np.uint8)  # the data block as placed in device memory
+    for start, end, dev in pieces:
+        image[dev : dev + end - start] = body[start:end]
+    assert np.array_equal(a._blob.cpu().numpy(), repack_numpy(a.layout.jobs, image, a.layout.size))
+    clips = clips_of((3.0, 7.0), seed=80)
+    got = tinybark_b200.load("gpu", dtype=dtype, weights=(path, cfg)).tokens_batch(clips)
+    assert got == tinybark_b200.load("gpu", dtype=dtype, weights=(arrays, cfg)).tokens_batch(clips)

@@ -27,17 +27,24 @@ CONVERTED = "bark-6d34ed8639b2-v2"
 TOKENIZER_REPO = "nvidia/parakeet-tdt-0.6b-v3"
 
 
-def converted_weights(path: str | Path | None = None) -> tuple[dict[str, np.ndarray], dict]:
-    """tinybark's converted fp16 cache (tinybark/weights.py:106-120) and its config."""
-    from . import weights
-
+def converted(path: str | Path | None = None) -> tuple[Path, dict]:
+    """tinybark's converted fp16 cache file and its config (tinybark/weights.py:106-120),
+    as tinybark's weights.converted() returns them."""
     base = Path(path) if path else CACHE / CONVERTED
     tensors_path, config_path = base.with_suffix(".safetensors"), base.with_suffix(".json")
     if not tensors_path.exists() or not config_path.exists():
         raise FileNotFoundError(
             f"{tensors_path} not found: run tinybark's weights.converted() once, or pass weights=(tensors, config)"
         )
-    return weights.load(tensors_path), json.loads(config_path.read_text())
+    return tensors_path, json.loads(config_path.read_text())
+
+
+def converted_weights(path: str | Path | None = None) -> tuple[dict[str, np.ndarray], dict]:
+    """The converted cache's tensors as float32 arrays, and its config."""
+    from . import weights
+
+    tensors_path, config = converted(path)
+    return weights.load(tensors_path), config
 
 
 class Bark:
@@ -50,7 +57,8 @@ class Bark:
         from . import lengths
         from .engine import Engine
 
-        tensors, config = weights if weights is not None else converted_weights()
+        # The cache file goes to the GPU as it is and is repacked there.
+        tensors, config = weights if weights is not None else converted()
         max_len = lengths.subsampled(int(max_seconds * 100), 3)
         self.engine = Engine(tensors, config, dtype=dtype, device="cuda", max_len=max_len)
         self.device = torch.cuda.get_device_name(self.engine.device)
@@ -108,5 +116,6 @@ class Bark:
 
 def load(device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None) -> Bark:
     """The cuda backend on this process's current GPU, bf16 by default ("fp32" for the
-    fp32 parity path)."""
+    fp32 parity path). `weights` is (tensors, config): tensors the path of a converted
+    fp16 cache file or a dict of the converted arrays; by default tinybark's own cache."""
     return Bark(device, dtype=dtype, weights=weights, tokenizer=tokenizer)

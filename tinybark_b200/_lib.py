@@ -9,6 +9,8 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libtbcuda.so"
 
 F32, BF16 = 0, 1
+SRC_F16, SRC_F32 = 0, 1
+REPACK_CHUNK = 16384
 EPI_STORE, EPI_SILU, EPI_RESIDUAL, EPI_BIAS_RELU, EPI_GLU, EPI_QKV, EPI_ARGMAX, EPI_LSTM, EPI_JOINT_IN = range(9)
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or dtype", 4: "workspace too small",
           5: "more clips than the library's own scratch holds"}
@@ -61,6 +63,15 @@ class Batch(C.Structure):
     ]
 
 
+class RepackJob(C.Structure):
+    """tb_repack_job: one destination tensor of tb_repack."""
+
+    _fields_ = [
+        ("src_off", ll), ("dst_off", ll), ("stride", ll * 4), ("first_chunk", ll), ("dims", i32 * 4),
+        ("src_type", i32), ("dst_type", i32), ("fill", i32), ("value", f32),
+    ]
+
+
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
         raise RuntimeError(
@@ -92,6 +103,7 @@ def _load() -> C.CDLL:
         "tb_decode_workspace_bytes": (sz, [i32, i32, i32]),
         "tb_selftest_wait": (i32, [i32, vp, vp, vp]),
         "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
+        "tb_repack": (i32, [P(RepackJob), i32, vp, vp, sz, vp, sz, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -107,7 +119,7 @@ EXPORTS = (
     "tb_frontend_static", "tb_frontend_pcm16",
     "tb_layernorm", "tb_gemm", "tb_set_gemm_pairs", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
-    "tb_selftest_wait",
+    "tb_selftest_wait", "tb_repack",
 )
 
 

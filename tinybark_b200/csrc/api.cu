@@ -256,6 +256,11 @@ int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n
   return gemm(dtype, a, lda, w, m, n, k, *epi, err, as_stream(stream));
 }
 
+int tb_repack(const tb_repack_job* jobs, int n_jobs, void* jobs_dev, const void* src, size_t src_bytes, void* dst,
+              size_t dst_bytes, void* stream) {
+  return repack(jobs, n_jobs, jobs_dev, src, src_bytes, dst, dst_bytes, as_stream(stream));
+}
+
 int tb_set_gemm_pairs(int on) {
   const int was = gemm_pairs() ? 1 : 0;
   set_gemm_pairs(on != 0);

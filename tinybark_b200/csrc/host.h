@@ -41,6 +41,8 @@ int subsample(const tb_model& m, const tb_batch& batch, const float* feats, floa
 size_t subsample_ws(int dtype, int t2_total, int t3_total);
 int subsample_tile_rows();  // depthwise-1 rows per work item of the fused conv-0 kernel
 int attention_tile_rows(int dtype);
+int repack(const tb_repack_job* jobs, int n_jobs, void* jobs_dev, const void* src, size_t src_bytes, void* dst,
+           size_t dst_bytes, cudaStream_t stream);
 
 // Launches `kernel` with programmatic stream serialization (see grid_dep_wait in
 // common.cuh): its prologue may overlap the end of the previous kernel on the stream.

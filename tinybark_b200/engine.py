@@ -11,6 +11,7 @@ zeroes is a zero-padding position here.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import time
 from dataclasses import dataclass
 
@@ -18,7 +19,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
-from . import lengths, tables
+from . import lengths, pack, tables
 
 DTYPES = {"fp32": L.F32, "bf16": L.BF16}
 MAX_DECODE_GROUPS = 8
@@ -96,8 +97,10 @@ def plan_arrays(frames, sub_rows: int, attn_rows: int) -> dict[str, np.ndarray]:
 
 
 class Engine:
-    """The model on one GPU. `tensors` is the converted layout (tinybark/weights.py:62-89)
-    as float32 arrays; `dtype` is "fp32" (parity) or "bf16" (throughput)."""
+    """The model on one GPU. `tensors` is the converted layout (tinybark/weights.py:62-89):
+    the path of tinybark's fp16 cache file of it (tinybark/weights.py:92-120), read
+    straight into GPU memory, or a dict of float32 arrays; `dtype` is "fp32" (parity) or
+    "bf16" (throughput)."""
 
     def __init__(self, tensors: dict[str, np.ndarray], config: dict, dtype: str = "bf16", device="cuda",
                  max_len: int = 512):
@@ -126,94 +129,77 @@ class Engine:
 
     # ------------------------------------------------------------------ weights
 
-    def _mat(self, a: np.ndarray) -> torch.Tensor:
-        t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(self.device, self.tdtype).contiguous()
-        self._keep.append(t)
-        return t
-
     def _vec(self, a: np.ndarray, dtype=torch.float32) -> torch.Tensor:
         t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device, dtype).contiguous()
         self._keep.append(t)
         return t
 
-    def _pack(self, w: dict[str, np.ndarray]) -> None:
+    def _pack(self, w) -> None:
+        """The weights into one packed device buffer (pack.model_layout), from a path of
+        tinybark's fp16 cache file (its data block uploaded as is) or from a dict of the
+        converted tensors; then the kernels' pointers into it."""
+        t0 = time.perf_counter()
+        if isinstance(w, (str, os.PathLike)):
+            source, index = pack.upload_cache(w, self.device)
+        else:
+            source, index = pack.upload_arrays(w, self.device)
+        lay = pack.model_layout(index, self.layers, self.dtype)
+        blob = torch.zeros(lay.size, dtype=torch.uint8, device=self.device)
+        torch.cuda.synchronize(self.device)
+        t1 = time.perf_counter()
+        lay.run(source, blob)
+        torch.cuda.synchronize(self.device)
+        t2 = time.perf_counter()
+        del source
+        self.layout, self._blob = lay, blob
+        base = blob.data_ptr()
+
+        def at(key: str) -> int:
+            return base + lay.regions[key].off
+
         m = L.Model()
         m.dtype, m.layers = self.dtype, self.layers
-        p = "encoder.subsampling."
-        m.sub0_w = _ptr(self._vec(w[p + "layers.0.weight"].reshape(L.CHANNELS, 9)))
-        m.sub0_b = _ptr(self._vec(w[p + "layers.0.bias"]))
-        for i, (dw, pw) in enumerate(((2, 3), (5, 6))):
-            m.sub_dw_w[i] = _ptr(self._vec(w[p + f"layers.{dw}.weight"].reshape(L.CHANNELS, 9)))
-            m.sub_dw_b[i] = _ptr(self._vec(w[p + f"layers.{dw}.bias"]))
-            m.sub_pw_w[i] = _ptr(self._mat(w[p + f"layers.{pw}.weight"].reshape(L.CHANNELS, L.CHANNELS)))
-            m.sub_pw_b[i] = _ptr(self._vec(w[p + f"layers.{pw}.bias"]))
-        # Linear input columns: the reference's (channel, frequency) to (frequency, channel).
-        lin = w[p + "linear.weight"].reshape(L.HIDDEN, L.CHANNELS, 16).transpose(0, 2, 1).reshape(L.HIDDEN, -1)
-        m.sub_linear_w = _ptr(self._mat(lin))
-        m.sub_linear_b = _ptr(self._vec(w[p + "linear.bias"]))
+        m.sub0_w, m.sub0_b = at("sub0_w"), at("sub0_b")
+        for i in range(2):
+            m.sub_dw_w[i], m.sub_dw_b[i] = at(f"sub_dw_w{i}"), at(f"sub_dw_b{i}")
+            m.sub_pw_w[i], m.sub_pw_b[i] = at(f"sub_pw_w{i}"), at(f"sub_pw_b{i}")
+        m.sub_linear_w, m.sub_linear_b = at("sub_linear_w"), at("sub_linear_b")
 
         self._layer_arr = (L.Layer * self.layers)()
         self._rel_w: list[torch.Tensor] = []
         self._pos_bias: list[tuple[torch.Tensor, torch.Tensor]] = []
-        norms = ("norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2", "norm_out")
         for i in range(self.layers):
-            q = f"encoder.layers.{i}."
-            lay = self._layer_arr[i]
-            for j, n in enumerate(norms):
-                lay.norm_w[j] = _ptr(self._vec(w[q + n + ".weight"]))
-                lay.norm_b[j] = _ptr(self._vec(w[q + n + ".bias"]))
-            lay.ff1_w1 = _ptr(self._mat(w[q + "feed_forward1.linear1.weight"]))
-            lay.ff1_w2 = _ptr(self._mat(w[q + "feed_forward1.linear2.weight"]))
-            lay.ff2_w1 = _ptr(self._mat(w[q + "feed_forward2.linear1.weight"]))
-            lay.ff2_w2 = _ptr(self._mat(w[q + "feed_forward2.linear2.weight"]))
-            a = q + "self_attn."
-            lay.qkv = _ptr(self._mat(w[a + "qkv"]))
-            lay.o_proj = _ptr(self._mat(w[a + "o_proj.weight"]))
-            bu, bv = self._vec(w[a + "bias_u"].reshape(-1)), self._vec(w[a + "bias_v"].reshape(-1))
-            lay.bias_u, lay.bias_v = _ptr(bu), _ptr(bv)
-            self._pos_bias.append((bu, bv))
-            self._rel_w.append(self._mat(w[a + "relative_k_proj.weight"]))
-            c = q + "conv."
-            pw1 = w[c + "pointwise_conv1.weight"].reshape(2 * L.HIDDEN, L.HIDDEN)
-            # GLU pairs side by side: row 2c is a_c, row 2c+1 is its gate g_c.
-            lay.pw1 = _ptr(self._mat(np.stack([pw1[: L.HIDDEN], pw1[L.HIDDEN :]], 1).reshape(2 * L.HIDDEN, L.HIDDEN)))
-            lay.pw2 = _ptr(self._mat(w[c + "pointwise_conv2.weight"].reshape(L.HIDDEN, L.HIDDEN)))
-            lay.dw_w = _ptr(self._vec(w[c + "depthwise.weight"].reshape(L.HIDDEN, L.KERNEL)))
-            lay.dw_b = _ptr(self._vec(w[c + "depthwise.bias"]))
+            lay_i = self._layer_arr[i]
+            for j in range(len(pack.NORMS)):
+                lay_i.norm_w[j], lay_i.norm_b[j] = at(f"{i}.norm_w{j}"), at(f"{i}.norm_b{j}")
+            lay_i.ff1_w1, lay_i.ff1_w2 = at(f"{i}.ff1_w1"), at(f"{i}.ff1_w2")
+            lay_i.ff2_w1, lay_i.ff2_w2 = at(f"{i}.ff2_w1"), at(f"{i}.ff2_w2")
+            lay_i.qkv, lay_i.o_proj = at(f"{i}.qkv"), at(f"{i}.o_proj")
+            lay_i.bias_u, lay_i.bias_v = at(f"{i}.bias_u"), at(f"{i}.bias_v")
+            self._pos_bias.append((lay.tensor_of(blob, f"{i}.bias_u"), lay.tensor_of(blob, f"{i}.bias_v")))
+            self._rel_w.append(lay.tensor_of(blob, f"{i}.rel_w"))
+            lay_i.pw1, lay_i.pw2 = at(f"{i}.pw1"), at(f"{i}.pw2")
+            lay_i.dw_w, lay_i.dw_b = at(f"{i}.dw_w"), at(f"{i}.dw_b")
         m.layer = C.cast(self._layer_arr, C.POINTER(L.Layer))
-        m.enc_proj_w = _ptr(self._mat(w["encoder_projector.weight"]))
-        m.enc_proj_b = _ptr(self._vec(w["encoder_projector.bias"]))
-
-        emb = self._mat(w["decoder.embedding.weight"])
-        m.embedding = _ptr(emb)
+        m.enc_proj_w, m.enc_proj_b = at("enc_proj_w"), at("enc_proj_b")
+        m.embedding = at("embedding")
         for l in range(2):
-            # Gates side by side per unit: row 4u+g is gate g (i, f, g, o) of unit u.
-            wl = w[f"decoder.lstm.weight_l{l}"].reshape(4, L.PRED, 2 * L.PRED).transpose(1, 0, 2).reshape(4 * L.PRED, -1)
-            bl = w[f"decoder.lstm.bias_l{l}"].reshape(4, L.PRED).T.reshape(-1)
-            m.lstm_w[l] = _ptr(self._mat(wl))
-            m.lstm_b[l] = _ptr(self._vec(bl))
-            if l == 0 and self.dtype == L.BF16:
-                # The persistent decoder takes layer 0's gates as E[token] + W_hh . h0: the
-                # input term of every token, E = embedding . W_ih^T, computed once here.
-                m.lstm0_hh = _ptr(self._mat(wl[:, L.PRED :]))
-                w_ih = torch.from_numpy(np.ascontiguousarray(wl[:, : L.PRED], np.float32)).to(self.device, self.tdtype)
-                table = torch.empty(L.VOCAB, 4 * L.PRED, device=self.device, dtype=torch.float32)
-                self._keep.append(table)
-                from . import kernels
+            m.lstm_w[l], m.lstm_b[l] = at(f"lstm_w{l}"), at(f"lstm_b{l}")
+        if self.dtype == L.BF16:
+            # The persistent decoder takes layer 0's gates as E[token] + W_hh . h0: the
+            # input term of every token, E = embedding . W_ih^T, computed once here.
+            m.lstm0_hh = at("lstm0_hh")
+            emb = lay.tensor_of(blob, "embedding")
+            w_ih = lay.tensor_of(blob, "lstm0_ih").view(4 * L.PRED, L.PRED)
+            table = torch.empty(L.VOCAB, 4 * L.PRED, device=self.device, dtype=torch.float32)
+            self._keep.append(table)
+            from . import kernels
 
-                kernels.gemm(emb, w_ih, L.Epilogue(kind=L.EPI_STORE, out_dtype=L.F32, out=table.data_ptr(),
-                                                   ldo=4 * L.PRED))
-                m.lstm0_emb = _ptr(table)
-        m.dec_proj_w = _ptr(self._mat(w["decoder.decoder_projector.weight"]))
-        m.dec_proj_b = _ptr(self._vec(w["decoder.decoder_projector.bias"]))
-        joint = np.zeros((L.JOINT_ROWS, L.PRED), np.float32)
-        bias = np.full(L.JOINT_ROWS, -np.inf, np.float32)
-        joint[: L.TOKEN_ROWS] = w["joint.token_head.weight"]
-        bias[: L.TOKEN_ROWS] = w["joint.token_head.bias"]
-        joint[L.TOKEN_ROWS : L.TOKEN_ROWS + L.DURATIONS] = w["joint.duration_head.weight"]
-        bias[L.TOKEN_ROWS : L.TOKEN_ROWS + L.DURATIONS] = w["joint.duration_head.bias"]
-        m.joint_w = _ptr(self._mat(joint))
-        m.joint_b = _ptr(self._vec(bias))
+            kernels.gemm(emb, w_ih, L.Epilogue(kind=L.EPI_STORE, out_dtype=L.F32, out=table.data_ptr(),
+                                               ldo=4 * L.PRED))
+            m.lstm0_emb = _ptr(table)
+        m.dec_proj_w, m.dec_proj_b = at("dec_proj_w"), at("dec_proj_b")
+        m.joint_w, m.joint_b = at("joint_w"), at("joint_b")
 
         mel_w, mel_start, mel_off = tables.sparse_mel()
         m.window = _ptr(self._vec(tables.window()))
@@ -221,6 +207,7 @@ class Engine:
         m.mel_start = _ptr(self._vec(mel_start, torch.int32))
         m.mel_off = _ptr(self._vec(mel_off, torch.int32))
         self.model = m
+        self.load_seconds = {"upload": t1 - t0, "repack": t2 - t1}
 
     def ensure_len(self, t3: int) -> None:
         """Projected position tables (pos @ relative_k_proj^T, one per layer) covering
