@@ -35,7 +35,8 @@ enum tb_device_error {
   TB_DEV_GEMM_TIMEOUT = 1 << 0,
   TB_DEV_ATTN_TIMEOUT = 1 << 1,
   TB_DEV_DECODE_TIMEOUT = 1 << 2,
-  TB_DEV_CONV_TIMEOUT = 1 << 3
+  TB_DEV_CONV_TIMEOUT = 1 << 3,
+  TB_DEV_TEXT_TOKEN = 1 << 4 /* tb_text_offsets: a token id outside the piece table (it adds no bytes) */
 };
 
 /* Arithmetic type of a path: fp32 everywhere, or bf16 operands with fp32
@@ -332,6 +333,24 @@ typedef struct {
 } tb_repack_job;
 int tb_repack(const tb_repack_job* jobs, int n_jobs, void* jobs_dev, const void* src, size_t src_bytes, void* dst,
               size_t dst_bytes, void* stream);
+
+/* ---- text: tinybark/text.py:19-34 (Tokenizer.decode, special tokens skipped) ----
+ * Token rows to UTF-8 bytes. The piece table gives each id's bytes as the text joins them:
+ * a SentencePiece piece with "\u2581" as a space, a byte-fallback piece <0xNN> as the byte
+ * NN, a special token as nothing (piece_off [vocab + 1] and piece_bytes, device). Lane l's
+ * bytes are those of tokens[l * ld + t] for t < counts[l] (clamped to [0, ld]), joined;
+ * decoded as UTF-8 with invalid sequences replaced, "\u2581" turned into a space and the
+ * ends stripped, they are the reference's text for those ids.
+ * tb_text_offsets writes text_off [lanes + 1] (int64, device): lane l's bytes are
+ * [text_off[l], text_off[l + 1]). An id outside [0, vocab) adds nothing and sets
+ * TB_DEV_TEXT_TOKEN in err (may be NULL). tb_text_bytes then writes the bytes into text
+ * (text_len bytes, at least text_off[lanes]; nothing is written past it or read outside
+ * piece_bytes [piece_bytes_len]). */
+int tb_text_offsets(const int* tokens, int ld, const int* counts, int lanes, const int* piece_off, int vocab,
+                    long long* text_off, int* err, void* stream);
+int tb_text_bytes(const int* tokens, int ld, const int* counts, int lanes, const int* piece_off,
+                  const uint8_t* piece_bytes, long long piece_bytes_len, int vocab, const long long* text_off,
+                  uint8_t* text, long long text_len, void* stream);
 
 #ifdef __cplusplus
 }

@@ -75,6 +75,29 @@ def test_tokenizer_decodes_pieces_bytes_and_specials(tmp_path):
     assert tok.decode([7]) == ""
 
 
+def test_joined_piece_bytes_are_the_tokenizers_text(tmp_path):
+    """The GPU's join, restated: every id's bytes from Tokenizer.table joined and finished
+    once give Tokenizer.decode's text, over random id lists heavy in byte-fallback runs
+    (invalid UTF-8 included) and special tokens between them."""
+    import random
+
+    from conftest import synthetic_tokenizer
+    from tinybark_b200.text import finish
+
+    tok = Tokenizer(synthetic_tokenizer(tmp_path / "tokenizer.json", vocab=600))
+    off, data = tok.table()
+    assert len(off) == 601 and off[0] == 0 and off[-1] == len(data)
+    assert bytes(data[off[3 + 0xC3] : off[4 + 0xC3]]) == b"\xc3" and off[1] == off[0]  # a byte piece; a special
+    rng = random.Random(1)
+    for _ in range(20000):
+        ids = []
+        for _ in range(rng.randint(0, 12)):
+            r = rng.random()
+            ids.append(rng.randrange(3, 259) if r < 0.5 else (rng.choice([0, 1, 2, 599]) if r < 0.6 else rng.randrange(259, 599)))
+        joined = b"".join(bytes(data[off[i] : off[i + 1]]) for i in ids)
+        assert finish(joined) == tok.decode(ids), ids
+
+
 def test_registry_has_cuda_backend():
     b = backends.BACKENDS["cuda"]
     assert b.name == "cuda" and set(b.descriptions) <= set(backends.DEVICES)

@@ -502,3 +502,39 @@ def test_repack_matches_numpy_on_random_jobs(L, seed):
         written[j[1] : j[1] + int(np.prod(j[3])) * esz] = True
     assert np.array_equal(got[:size][written], want[written])
     assert (got[:size][~written] == 0xA5).all() and (got[size:] == 0xA5).all()  # nothing else touched
+
+
+def test_text_join_matches_numpy(L):
+    """tb_text_offsets + tb_text_bytes against the numpy join of each lane's piece bytes:
+    empty pieces, empty / full / over-long / negative counts (clamped to [0, ld]), and ids
+    outside the table, which add nothing and set the text error bit."""
+    rng = np.random.default_rng(3)
+    vocab, lanes, ld = 500, 300, 60
+    lens = rng.integers(0, 7, vocab)
+    lens[::17] = 0
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    data = rng.integers(0, 256, int(off[-1]), dtype=np.uint8)
+    tokens = rng.integers(0, vocab, (lanes, ld)).astype(np.int32)
+    counts = rng.integers(0, ld + 1, lanes).astype(np.int32)
+    counts[:4] = [0, ld, ld + 5, -2]
+    tokens[7, 0], tokens[8, 0] = vocab + 4, -1
+    counts[7:9] = 5
+    want = []
+    for l in range(lanes):
+        n = min(max(int(counts[l]), 0), ld)
+        want.append(b"".join(data[off[i] : off[i + 1]].tobytes() for i in tokens[l, :n] if 0 <= i < vocab))
+    dev = lambda a: torch.from_numpy(a).cuda()
+    tk, cn, po, pb = dev(tokens), dev(counts), dev(off), dev(data)
+    text_off = torch.full((lanes + 1,), -1, dtype=torch.int64, device="cuda")
+    e = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert L.lib.tb_text_offsets(tk.data_ptr(), ld, cn.data_ptr(), lanes, po.data_ptr(), vocab, text_off.data_ptr(),
+                                 e.data_ptr(), stream()) == 0
+    o = text_off.cpu().numpy()
+    assert list(np.diff(o)) == [len(w) for w in want] and o[0] == 0
+    text = torch.full((int(o[-1]) + 16,), 0xA5, dtype=torch.uint8, device="cuda")
+    assert L.lib.tb_text_bytes(tk.data_ptr(), ld, cn.data_ptr(), lanes, po.data_ptr(), pb.data_ptr(), pb.numel(), vocab,
+                               text_off.data_ptr(), text.data_ptr(), int(o[-1]), stream()) == 0
+    raw = text.cpu().numpy().tobytes()
+    assert [raw[o[l] : o[l + 1]] for l in range(lanes)] == want
+    assert raw[int(o[-1]) :] == b"\xa5" * 16  # nothing past the end
+    assert int(e.item()) == 16

@@ -265,3 +265,25 @@ def test_engine_from_cache_file_equals_engine_from_arrays(tmp_path, dtype):
     clips = clips_of((3.0, 7.0), seed=80)
     got = tinybark_b200.load("gpu", dtype=dtype, weights=(path, cfg)).tokens_batch(clips)
     assert got == tinybark_b200.load("gpu", dtype=dtype, weights=(arrays, cfg)).tokens_batch(clips)
+
+
+def test_transcribe_batch_is_the_tokenizers_text(tmp_path):
+    """transcribe_batch joins every clip's piece bytes on the GPU: its texts equal the
+    tokenizer's host decode of the same clips' tokens (a seeded tokenizer of 8193 ids with
+    byte-fallback pieces, since the real vocabulary is not available offline); a clip too
+    short for any frame gives ""."""
+    import tinybark_b200
+    from conftest import synthetic_tokenizer
+    from tinybark_b200 import synthetic, weights
+    from tinybark_b200.text import Tokenizer
+
+    cfg = synthetic.config(2)
+    path = synthetic_tokenizer(tmp_path / "tokenizer.json")
+    bark = tinybark_b200.load("gpu", weights=(weights.convert(state_dict(2), cfg), cfg), tokenizer=path)
+    clips = clips_of((1.0, 4.0, 9.5, 0.005, 2.2), seed=30)
+    tokens = bark.tokens_batch(clips)
+    assert sum(len(t) for t in tokens) > 0 and tokens[3] == []
+    tok = Tokenizer(path)
+    texts = bark.transcribe_batch(clips)
+    assert texts == [tok.decode(t) for t in tokens] and texts[3] == ""
+    assert bark.transcribe(clips[2]) == texts[2]

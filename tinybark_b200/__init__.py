@@ -7,7 +7,8 @@ libtbcuda's C ABI; torch only allocates device memory.
     ids = bark.tokens_batch([a, b, c])     # many clips in one pass
 
 Same API as tinybark's backends (tinybark/backends.py:21-26; tinybark/tinygrad/__init__.py:21-35):
-`device`, `tokens`, `transcribe`, `transcribe_pcm`, plus `tokens_batch`, `tokens_long` /
+`device`, `tokens`, `transcribe`, `transcribe_pcm`, plus `tokens_batch`, `transcribe_batch`
+(transcripts joined into bytes on the GPU), `tokens_long` /
 `transcribe_long` (long recordings in pieces of at most 30 s) and `close`.
 """
 
@@ -64,6 +65,7 @@ class Bark:
         self.device = torch.cuda.get_device_name(self.engine.device)
         self._tokenizer_path = tokenizer
         self._tokenizer = None
+        self._text_table = None
 
     def tokens(self, samples: np.ndarray) -> list[int]:
         """Token ids of one clip (16 kHz mono float32), without start/blank/pad; EOS kept if hit."""
@@ -103,12 +105,21 @@ class Bark:
         return self._tokenizer
 
     def transcribe(self, samples: np.ndarray) -> str:
-        return self.tokenizer.decode(self.tokens(samples))
+        return self.transcribe_batch([samples])[0]
+
+    def transcribe_batch(self, clips: list[np.ndarray]) -> list[str]:
+        """The text of many clips in one pass: each clip's tokens are joined into bytes on
+        the GPU (the tokenizer's piece table held there), and only the bytes come back."""
+        from .text import finish
+
+        if self._text_table is None:
+            self._text_table = self.engine.text_table(*self.tokenizer.table())
+        return [finish(raw) for raw in self.engine.texts_batch(clips, self._text_table)]
 
     def transcribe_pcm(self, pcm: bytes) -> str:
         """16 kHz s16le mono PCM (tinybark/tinygrad/__init__.py:33-35), converted to float on
         the GPU."""
-        return self.tokenizer.decode(self.tokens(np.frombuffer(pcm, dtype="<i2").astype(np.int16)))
+        return self.transcribe(np.frombuffer(pcm, dtype="<i2").astype(np.int16))
 
     def close(self) -> None:
         self.engine = None

@@ -16,7 +16,7 @@ STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "unsupported shape or 
           5: "more clips than the library's own scratch holds"}
 FRONTEND_STATIC_MAX_CLIPS = 64
 DEVICE_ERRORS = {1: "GEMM barrier wait timed out", 2: "attention barrier wait timed out", 4: "decode wait timed out",
-                 8: "depthwise conv copy wait timed out"}
+                 8: "depthwise conv copy wait timed out", 16: "token id outside the text piece table"}
 
 HIDDEN, HEADS, HEAD_DIM, FFN, KERNEL, CHANNELS, MELS = 1024, 8, 128, 4096, 9, 256, 128
 VOCAB, BLANK, EOS, DURATIONS, PRED = 8193, 8192, 3, 5, 640
@@ -104,6 +104,8 @@ def _load() -> C.CDLL:
         "tb_selftest_wait": (i32, [i32, vp, vp, vp]),
         "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
         "tb_repack": (i32, [P(RepackJob), i32, vp, vp, sz, vp, sz, vp]),
+        "tb_text_offsets": (i32, [vp, i32, vp, i32, vp, i32, vp, vp, vp]),
+        "tb_text_bytes": (i32, [vp, i32, vp, i32, vp, vp, ll, i32, vp, vp, ll, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -119,7 +121,7 @@ EXPORTS = (
     "tb_frontend_static", "tb_frontend_pcm16",
     "tb_layernorm", "tb_gemm", "tb_set_gemm_pairs", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
-    "tb_selftest_wait", "tb_repack",
+    "tb_selftest_wait", "tb_repack", "tb_text_offsets", "tb_text_bytes",
 )
 
 

@@ -256,6 +256,18 @@ int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n
   return gemm(dtype, a, lda, w, m, n, k, *epi, err, as_stream(stream));
 }
 
+int tb_text_offsets(const int* tokens, int ld, const int* counts, int lanes, const int* piece_off, int vocab,
+                    long long* text_off, int* err, void* stream) {
+  return text_offsets(tokens, ld, counts, lanes, piece_off, vocab, text_off, err, as_stream(stream));
+}
+
+int tb_text_bytes(const int* tokens, int ld, const int* counts, int lanes, const int* piece_off,
+                  const uint8_t* piece_bytes, long long piece_bytes_len, int vocab, const long long* text_off,
+                  uint8_t* text, long long text_len, void* stream) {
+  return text_bytes(tokens, ld, counts, lanes, piece_off, piece_bytes, piece_bytes_len, vocab, text_off, text,
+                    text_len, as_stream(stream));
+}
+
 int tb_repack(const tb_repack_job* jobs, int n_jobs, void* jobs_dev, const void* src, size_t src_bytes, void* dst,
               size_t dst_bytes, void* stream) {
   return repack(jobs, n_jobs, jobs_dev, src, src_bytes, dst, dst_bytes, as_stream(stream));

@@ -41,6 +41,11 @@ int subsample(const tb_model& m, const tb_batch& batch, const float* feats, floa
 size_t subsample_ws(int dtype, int t2_total, int t3_total);
 int subsample_tile_rows();  // depthwise-1 rows per work item of the fused conv-0 kernel
 int attention_tile_rows(int dtype);
+int text_offsets(const int* tokens, int ld, const int* counts, int lanes, const int* piece_off, int vocab,
+                 long long* text_off, int* err, cudaStream_t stream);
+int text_bytes(const int* tokens, int ld, const int* counts, int lanes, const int* piece_off,
+               const uint8_t* piece_bytes, long long piece_bytes_len, int vocab, const long long* text_off,
+               uint8_t* text, long long text_len, cudaStream_t stream);
 int repack(const tb_repack_job* jobs, int n_jobs, void* jobs_dev, const void* src, size_t src_bytes, void* dst,
            size_t dst_bytes, cudaStream_t stream);
 

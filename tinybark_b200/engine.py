@@ -420,38 +420,88 @@ class Engine:
             self._threads = ThreadPoolExecutor(max_workers=8)
         return self._threads
 
-    def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
-        """Token ids of every clip (16 kHz mono float32 samples), as the reference's
-        Bark.tokens returns them one clip at a time (tinybark/tinygrad/model.py:196-234)."""
+    def _encode_batch(self, clips: list[np.ndarray]):
+        """Front-end and encoder of every clip of at least 2 frames: (kept clip indices in
+        lane order, encoder rows, plan), or None if no clip is kept."""
         clips = [np.asarray(c).reshape(-1) for c in clips]
         if not all(c.dtype == np.int16 for c in clips):  # 16-bit PCM stays 16-bit up to the GPU
             clips = [np.asarray(c, np.float32) for c in clips]
         frames = [lengths.frames(len(c)) for c in clips]
         keep = lane_order([i for i, f in enumerate(frames) if f >= 2], frames)
-        out: list[list[int]] = [[] for _ in clips]
         if not keep:
-            return out
+            return None
+        kf = [frames[i] for i in keep]
+        t3 = np.asarray(kf, np.int64)
+        for _ in range(3):
+            t3 = (t3 - 1) // 2 + 1  # the three stride-2 subsampling stages
+        t3_off = np.concatenate([[0], np.cumsum(t3)]).astype(np.int64)
+        enc = torch.empty(int(t3_off[-1]), L.PRED, device=self.device, dtype=torch.float32)
+        # Front-end and encoder part by part, each part's samples copied while the
+        # previous part is computed. The whole batch's plan (for the decode) is built once
+        # the first part's work is queued.
+        plan = None
+        for a, b, samples, sample_off in self.upload_parts([clips[i] for i in keep]):
+            whole = (a, b) == (0, len(keep))
+            sub = self.plan(kf if whole else kf[a:b])
+            feats = self.features(samples, sample_off, sub)
+            self.encode(feats, sub, out=enc[t3_off[a] : t3_off[b]])
+            if plan is None:
+                plan = sub if whole else self.plan(kf)
+        return keep, enc, plan
+
+    def tokens_batch(self, clips: list[np.ndarray]) -> list[list[int]]:
+        """Token ids of every clip (16 kHz mono float32 samples), as the reference's
+        Bark.tokens returns them one clip at a time (tinybark/tinygrad/model.py:196-234)."""
+        out: list[list[int]] = [[] for _ in clips]
         with torch.cuda.device(self.device):
-            kf = [frames[i] for i in keep]
-            t3 = np.asarray(kf, np.int64)
-            for _ in range(3):
-                t3 = (t3 - 1) // 2 + 1  # the three stride-2 subsampling stages
-            t3_off = np.concatenate([[0], np.cumsum(t3)]).astype(np.int64)
-            enc = torch.empty(int(t3_off[-1]), L.PRED, device=self.device, dtype=torch.float32)
-            # Front-end and encoder part by part, each part's samples copied while the
-            # previous part is computed; one decode over every lane. The whole batch's plan
-            # (for the decode) is built once the first part's work is queued.
-            plan = None
-            for a, b, samples, sample_off in self.upload_parts([clips[i] for i in keep]):
-                whole = (a, b) == (0, len(keep))
-                sub = self.plan(kf if whole else kf[a:b])
-                feats = self.features(samples, sample_off, sub)
-                self.encode(feats, sub, out=enc[t3_off[a] : t3_off[b]])
-                if plan is None:
-                    plan = sub if whole else self.plan(kf)
+            batch = self._encode_batch(clips)
+            if batch is None:
+                return out
+            keep, enc, plan = batch
             lists = self.decode_lists(enc, plan)
         for j, i in enumerate(keep):
             out[i] = lists[j]
+        return out
+
+    def text_table(self, off: np.ndarray, data: np.ndarray) -> tuple[torch.Tensor, torch.Tensor]:
+        """A tokenizer's piece table (text.Tokenizer.table) on this GPU."""
+        return (torch.from_numpy(np.ascontiguousarray(off, np.int32)).to(self.device),
+                torch.from_numpy(np.ascontiguousarray(data, np.uint8)).to(self.device))
+
+    def texts(self, tokens: torch.Tensor, counts: torch.Tensor, table) -> list[bytes]:
+        """Each lane's piece bytes joined on the GPU (tb_text_offsets, tb_text_bytes):
+        token rows [lanes, ld] and counts [lanes] int32 on this GPU, `table` from
+        text_table. text.finish turns one into its text."""
+        off_t, data = table
+        n, ld = tokens.shape
+        stream = _stream(self.device)
+        off = torch.empty(n + 1, dtype=torch.int64, device=self.device)
+        L.check(L.lib.tb_text_offsets(tokens.data_ptr(), ld, counts.data_ptr(), n, off_t.data_ptr(), off_t.numel() - 1,
+                                      off.data_ptr(), self.err.data_ptr(), stream), "tb_text_offsets")
+        o = off.cpu().numpy()
+        text = torch.empty(max(int(o[-1]), 1), dtype=torch.uint8, device=self.device)
+        L.check(L.lib.tb_text_bytes(tokens.data_ptr(), ld, counts.data_ptr(), n, off_t.data_ptr(), data.data_ptr(),
+                                    data.numel(), off_t.numel() - 1, off.data_ptr(), text.data_ptr(), int(o[-1]),
+                                    stream), "tb_text_bytes")
+        raw = text[: int(o[-1])].cpu().numpy().tobytes()
+        self.check()
+        return [raw[o[i] : o[i + 1]] for i in range(n)]
+
+    def texts_batch(self, clips: list[np.ndarray], table) -> list[bytes]:
+        """The joined piece bytes of every clip's transcript: the tokens_batch pipeline, with
+        the token rows turned into bytes on the GPU instead of copied out as lists."""
+        out = [b"" for _ in clips]
+        with torch.cuda.device(self.device):
+            batch = self._encode_batch(clips)
+            if batch is None:
+                return out
+            keep, enc, plan = batch
+            flag = self.host_flag.numpy()
+            flag[0], flag[1] = plan.batch.clips, -1
+            tokens, counts = self.decode(enc, plan)
+            texts = self.texts(tokens, counts, table)
+        for j, i in enumerate(keep):
+            out[i] = texts[j]
         return out
 
     def decode_lists(self, enc: torch.Tensor, plan: Plan) -> list[list[int]]:
