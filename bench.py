@@ -18,6 +18,7 @@ transformers' ParakeetEncoder, the TDT loop restated in torch) on the host cores
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -567,7 +568,8 @@ def run_load(args, dev, hbm):
         src, index = pack.upload_cache(path, dev)
     lay = pack.model_layout(index, args.layers, L.BF16)
     out = torch.empty(lay.size, dtype=torch.uint8, device=dev)
-    table, jobs_dev = lay.table(), torch.empty(len(lay.jobs) * 88, dtype=torch.uint8, device=dev)
+    table = lay.table()
+    jobs_dev = torch.empty(ctypes.sizeof(table), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
 
     def call():
