@@ -155,6 +155,39 @@ def test_aligned_runs_put_every_tensor_on_a_16_byte_boundary(converted2, tmp_pat
     assert np.array_equal(repack_numpy(lay.jobs, body, lay.size), repack_numpy(lay2.jobs, image, lay2.size))
 
 
+@pytest.mark.parametrize("seed", range(5))
+def test_slice_copies_place_every_byte_once(seed):
+    """upload_file's copies, slice by slice: for random runs (gaps between them, runs
+    straddling slice boundaries) and slice sizes, every byte of every run arrives once at
+    its device offset and nothing else is written."""
+    from tinybark_b200 import pack
+
+    rng = np.random.default_rng(seed)
+    pieces, at, dev = [], 0, 0
+    for _ in range(int(rng.integers(1, 8))):
+        at += int(rng.integers(0, 40))
+        n = int(rng.integers(1, 300))
+        dev += int(rng.integers(0, 16))
+        pieces.append((at, at + n, at + dev))
+        at += n
+    nbytes = at + int(rng.integers(0, 30))
+    body = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    dev_bytes = pieces[-1][2] + pieces[-1][1] - pieces[-1][0]
+    image, hits = np.zeros(dev_bytes, np.uint8), np.zeros(dev_bytes, np.int64)
+    slice_bytes = int(rng.integers(1, 97))
+    for start in range(0, nbytes, slice_bytes):
+        length = min(slice_bytes, nbytes - start)
+        for off, to, n in pack.slice_copies(start, length, pieces):
+            assert 0 <= off and off + n <= length
+            image[to : to + n] = body[start + off : start + off + n]
+            hits[to : to + n] += 1
+    want, covered = np.zeros(dev_bytes, np.uint8), np.zeros(dev_bytes, np.int64)
+    for a, b, d in pieces:
+        want[d : d + b - a] = body[a:b]
+        covered[d : d + b - a] = 1
+    assert np.array_equal(hits, covered) and np.array_equal(image, want)
+
+
 def test_cache_index_rejects_what_it_cannot_read(tmp_path):
     import json
 

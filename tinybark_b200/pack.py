@@ -273,6 +273,18 @@ def aligned_runs(index: dict[str, Source]) -> tuple[list[tuple[int, int, int]], 
     return pieces, (pieces[-1][2] + pieces[-1][1] - pieces[-1][0]) if pieces else 0, moved
 
 
+def slice_copies(start: int, length: int, pieces) -> list[tuple[int, int, int]]:
+    """The copies that move bytes [start, start + length) of a block to device memory, as
+    (offset in the slice, device offset, bytes): the part of each piece (start, end,
+    device start) that the slice holds."""
+    out = []
+    for a, e, d in pieces:
+        lo, hi = max(a, start), min(e, start + length)
+        if lo < hi:
+            out.append((lo - start, d + lo - a, hi - lo))
+    return out
+
+
 def upload_file(path: str | Path, offset: int, nbytes: int, device, pieces=None, dev_bytes: int | None = None,
                 slice_bytes: int = 8 << 20, threads: int | None = None) -> torch.Tensor:
     """Bytes [offset, offset + nbytes) of a file in device memory (uint8): each piece
@@ -315,11 +327,8 @@ def upload_file(path: str | Path, offset: int, nbytes: int, device, pieces=None,
             for k in range(n_slices):
                 b, start, length = pending[k].result()
                 with torch.cuda.stream(stream):
-                    for a, e, d in pieces:
-                        lo, hi = max(a, start), min(e, start + length)
-                        if lo < hi:
-                            dst.narrow(0, d + lo - a, hi - lo).copy_(bufs[b].narrow(0, lo - start, hi - lo),
-                                                                     non_blocking=True)
+                    for at, to, n in slice_copies(start, length, pieces):
+                        dst.narrow(0, to, n).copy_(bufs[b].narrow(0, at, n), non_blocking=True)
                     ev = torch.cuda.Event()
                     ev.record(stream)
                 copied[b] = ev
