@@ -51,6 +51,10 @@ def test_bad_arguments_are_rejected_without_touching_the_device():
     assert _lib.lib.tb_gemm(7, 1, 64, 1, 4, 128, 64, ctypes.byref(ep), None, None) == 1
     assert _lib.lib.tb_gemm(_lib.BF16, None, 64, None, 4, 128, 64, ctypes.byref(ep), None, None) == 1
     assert _lib.lib.tb_gemm(_lib.F32, 8, 64, 8, 4, 100, 64, ctypes.byref(ep), None, None) == 3
+    # text: negative lanes, a missing piece table
+    assert _lib.lib.tb_text_offsets(None, 8, None, -1, None, 10, 8, None, None) == 1
+    assert _lib.lib.tb_text_offsets(8, 8, 8, 4, None, 10, 8, None, None) == 1
+    assert _lib.lib.tb_text_bytes(8, 8, 8, 4, 8, None, 5, 10, 8, 8, 100, None) == 1
     with pytest.raises(RuntimeError, match="bad argument"):
         _lib.check(1, "tb_gemm")
 
@@ -59,7 +63,8 @@ def test_bad_arguments_are_rejected_without_touching_the_device():
 def test_struct_layouts_match_the_header(tmp_path):
     from tinybark_b200 import _lib
 
-    structs = {"tb_epilogue": _lib.Epilogue, "tb_layer": _lib.Layer, "tb_model": _lib.Model, "tb_batch": _lib.Batch}
+    structs = {"tb_epilogue": _lib.Epilogue, "tb_layer": _lib.Layer, "tb_model": _lib.Model, "tb_batch": _lib.Batch,
+               "tb_repack_job": _lib.RepackJob}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
