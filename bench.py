@@ -50,7 +50,7 @@ def args_parser():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform,load)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform,load,text)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -529,6 +529,52 @@ def run_micro(args):
         run_longform(args, dev, tflops)
     if want("load"):
         run_load(args, dev, hbm)
+    if want("text"):
+        run_text(args, dev)
+
+
+def run_text(args, dev):
+    """Transcripts as text for a batch of 512 lanes of 50-300 tokens (seeded ids of a seeded
+    8193-id tokenizer): joined into bytes on the GPU (tb_text_offsets, tb_text_bytes, one
+    copy back, one UTF-8 decode per lane), against the host path (token rows copied back,
+    then the tokenizer's decode per lane). Best of 5 each, wall clock."""
+    import tempfile
+
+    import torch
+
+    from tinybark_b200 import synthetic
+    from tinybark_b200 import weights as w
+    from tinybark_b200.engine import Engine
+    from tinybark_b200.text import Tokenizer, finish
+
+    cfg = synthetic.config(2)
+    eng = Engine(w.convert(synthetic.state_dict(0, layers=2), cfg), cfg, dtype="bf16", device=dev)
+    with tempfile.TemporaryDirectory() as d:
+        tok = Tokenizer(synthetic.tokenizer(Path(d) / "tokenizer.json"))
+    table = eng.text_table(*tok.table())
+    rng = np.random.default_rng(0)
+    lanes, ld = 512, 400
+    counts = torch.from_numpy(rng.integers(50, 301, lanes).astype(np.int32)).to(dev)
+    tokens = torch.from_numpy(rng.integers(3, 8192, (lanes, ld)).astype(np.int32)).to(dev)
+
+    def gpu():
+        return [finish(raw) for raw in eng.texts(tokens, counts, table)]
+
+    def host():
+        tk, cn = tokens.cpu().numpy(), counts.cpu().numpy()
+        return [tok.decode(tk[j, : cn[j]].tolist()) for j in range(lanes)]
+
+    assert gpu() == host()
+    times = {}
+    for name, fn in (("gpu_join_ms", gpu), ("host_decode_ms", host)):
+        best = float("inf")
+        for _ in range(5):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            best = min(best, time.perf_counter() - t0)
+        times[name] = best * 1e3
+    print(json.dumps({"kernel": "text_join", "lanes": lanes, "tokens": int(counts.sum()), **times}), flush=True)
 
 
 def run_load(args, dev, hbm):

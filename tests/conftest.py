@@ -79,31 +79,8 @@ def repack_numpy(jobs, source: np.ndarray, size: int) -> np.ndarray:
     return out
 
 
-def synthetic_tokenizer(path, vocab: int = 8193, seed: int = 0) -> str:
-    """A tokenizer.json of `vocab` ids in the Parakeet tokenizer's form (no real vocabulary
-    is available offline): the 256 byte-fallback pieces <0x00>..<0xFF> at ids 3..258, three
-    special tokens (ids 0-2 and the last id), and seeded pieces of 1-4 characters from a set
-    with "▁", multi-byte and combining characters elsewhere. Returns the path."""
-    import random
 
-    rng = random.Random(seed)
-    chars = ["a", "e", "n", "t", "é", "ß", "中", "😀", "▁", "▁", "x", "́", "�", " "]
-    pieces, used = {}, set()
-    for i in range(vocab):
-        if 3 <= i < 259:
-            p = f"<0x{i - 3:02X}>"
-        else:
-            p = "".join(rng.choice(chars) for _ in range(rng.randint(1, 4)))
-            while p in used:
-                p += rng.choice(chars)
-        used.add(p)
-        pieces[p] = i
-    special = {0: "<unk>", 1: "<pad>", 2: "<|endoftext|>", vocab - 1: "<blank>"}
-    for i, content in special.items():
-        pieces = {p: j for p, j in pieces.items() if j != i}
-    spec = {
-        "model": {"vocab": pieces},
-        "added_tokens": [{"id": i, "content": c, "special": True} for i, c in special.items()],
-    }
-    Path(path).write_text(json.dumps(spec))
-    return str(path)
+def synthetic_tokenizer(path, vocab: int = 8193, seed: int = 0) -> str:
+    from tinybark_b200 import synthetic
+
+    return synthetic.tokenizer(path, vocab, seed)

@@ -169,3 +169,34 @@ def state_dict(seed: int = 0, layers: int = LAYERS) -> dict[str, np.ndarray]:
     sd["joint.head.weight"] = _xavier(rng, (VOCAB + len(DURATIONS), DECODER_HIDDEN))
     sd["joint.head.bias"] = zeros(VOCAB + len(DURATIONS))
     return sd
+
+
+def tokenizer(path, vocab: int = 8193, seed: int = 0) -> str:
+    """A tokenizer.json of `vocab` ids in the Parakeet tokenizer's form, since no real
+    vocabulary is available offline: the 256 byte-fallback pieces <0x00>..<0xFF> at ids
+    3..258, special tokens at ids 0-2 and the last id, and seeded pieces of 1-4 characters
+    from a set with "▁", multi-byte and combining characters elsewhere. Returns the path."""
+    import json
+    import random
+    from pathlib import Path
+
+    rng = random.Random(seed)
+    chars = ["a", "e", "n", "t", "é", "ß", "中", "😀", "▁", "▁", "x", "\u0301", "\ufffd", " "]
+    special = {0: "<unk>", 1: "<pad>", 2: "<|endoftext|>", vocab - 1: "<blank>"}
+    pieces, used = {}, set()
+    for i in range(vocab):
+        if 3 <= i < 259:
+            p = f"<0x{i - 3:02X}>"
+        else:
+            p = "".join(rng.choice(chars) for _ in range(rng.randint(1, 4)))
+            while p in used:
+                p += rng.choice(chars)
+        used.add(p)
+        if i not in special:
+            pieces[p] = i
+    spec = {
+        "model": {"vocab": pieces},
+        "added_tokens": [{"id": i, "content": c, "special": True} for i, c in special.items()],
+    }
+    Path(path).write_text(json.dumps(spec))
+    return str(path)
