@@ -208,6 +208,9 @@ def test_cache_index_rejects_what_it_cannot_read(tmp_path):
         pack.cache_index(write({"a": {"dtype": "F16", "shape": [4], "data_offsets": [0, 8]}}, bytes(6)))
     with pytest.raises(ValueError):
         pack.cache_index(write({"a": {"dtype": "F32", "shape": [1], "data_offsets": [2, 6]}}, bytes(6)))
+    with pytest.raises(ValueError, match="overlap"):
+        pack.cache_index(write({"a": {"dtype": "F16", "shape": [4], "data_offsets": [0, 8]},
+                                "b": {"dtype": "F16", "shape": [2], "data_offsets": [6, 10]}}, bytes(10)))
 
 
 def test_layout_refuses_reads_outside_a_tensor():

@@ -245,6 +245,10 @@ def cache_index(path: str | Path) -> tuple[int, int, dict[str, Source]]:
         if end - start != prod(shape) * SRC_SIZE[t] or end > size - body or start % SRC_SIZE[t]:
             raise ValueError(f"{name}: data offsets {start}..{end} do not hold {info['dtype']} {shape}")
         index[name] = Source(start, shape, t)
+    spans = sorted((s.off, s.off + prod(s.shape) * SRC_SIZE[s.type], n) for n, s in index.items())
+    for (_, end, a), (start, _, b) in zip(spans, spans[1:]):
+        if start < end:
+            raise ValueError(f"{a} and {b} overlap in the data block")
     return body, size - body, index
 
 
