@@ -213,7 +213,8 @@ int tb_frontend_pcm16(const tb_model* m, const int16_t* pcm, const long long* sa
  * call; more returns TB_ERR_TOO_LARGE before anything runs. The caller still allocates
  * samples, offsets and feats. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current: make it before any stream
- * capture. All calls share the array: calls that can overlap on the GPU (other streams,
+ * capture. The address is kept for the life of the process: after a device reset
+ * (cudaDeviceReset), which unloads the library's device code, do not call it again. All calls share the array: calls that can overlap on the GPU (other streams,
  * other threads) race and must be serialized by the caller. Nothing in it needs to start
  * at zero: every scratch value is written before it is read. Allocates nothing. */
 #define TB_FRONTEND_STATIC_MAX_CLIPS 64
@@ -297,6 +298,11 @@ int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* fe
  * TB_DEV_DECODE_TIMEOUT (kind 1) into *err and the kernel returns: no hang, no fault, and
  * the context stays usable. */
 int tb_selftest_wait(int kind, void* scratch, int* err, void* stream);
+/* Self-test of the epilogues' fast arithmetic (no reference counterpart): y[i] = f(x[i])
+ * for n float32 values on the device, f by kind: 0 the Newton reciprocal (x >= 1),
+ * 1 sigmoid and 2 SiLU with one special-function operation, 3 and 4 their two-wide forms,
+ * 5 the tanh-based sigmoid and 6 the hardware tanh of the LSTM cells. */
+int tb_selftest_math(int kind, const float* x, float* y, long long n, void* stream);
 
 size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups);
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,

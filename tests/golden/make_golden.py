@@ -1,11 +1,15 @@
-"""Generates the golden fixtures in this directory from the reference itself. Run in a
-checkout next to the reference (it is not needed afterwards):
+"""Generates the golden fixtures in this directory from the reference itself. The path of
+a tinybark checkout is a required argument (the checkout is not needed afterwards):
 
     python tests/golden/make_golden.py /path/to/tinybark
 
 - frontend.npz: tinybark.audio.features on short synthetic clips.
 - convert.json: shape and checksums of every tensor tinybark.weights._convert produces
   from the 2-layer synthetic state dict (seed 0).
+- cache_file.json: sha256 and tensor order of the fp16 cache file tinybark.weights._save
+  writes from that conversion.
+- text.json: tinybark.text.Tokenizer.decode of seeded id lists (text_cases) under the
+  seeded 8193-id tokenizer of tinybark_b200.synthetic.tokenizer.
 - lengths.json: tinybark.ort.subsampled and the greedy loop's cap for many lengths.
 - encoder.npz: transformers' ParakeetEncoder (the module family ParakeetForTDT wraps)
   with Bark's config on the synthetic weights: 2 layers on a 1 s clip, 24 layers on a 2 s
@@ -63,6 +67,20 @@ def decode_frames(case: dict) -> np.ndarray:
     return (rng.standard_normal((case["frames"], synthetic.DECODER_HIDDEN)) * case["scale"]).astype(np.float32)
 
 
+def text_cases(count: int = 300, seed: int = 5) -> list[list[int]]:
+    """Seeded id lists for the detokeniser fixture: 0-120 ids each, about 40 % of them
+    byte-fallback pieces (ids 3..258, so byte runs, split multi-byte sequences and
+    invalid UTF-8 occur), the rest any id of the 8193 (special tokens included)."""
+    rng = np.random.default_rng(seed)
+    cases = []
+    for _ in range(count):
+        n = int(rng.integers(0, 121))
+        byte = rng.random(n) < 0.4
+        ids = np.where(byte, rng.integers(3, 259, n), rng.integers(0, 8193, n))
+        cases.append([int(i) for i in ids])
+    return cases
+
+
 def digest(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a, np.float32).tobytes()).hexdigest()[:16]
 
@@ -76,7 +94,7 @@ def main(ref: Path) -> None:
     stub.__spec__ = importlib.machinery.ModuleSpec("onnxruntime", None)
     sys.modules.setdefault("onnxruntime", stub)
     sys.path.insert(0, str(ref))
-    from tinybark import audio, ort, weights
+    from tinybark import audio, ort, text, weights
 
     torch.set_num_threads(8)
 
@@ -94,6 +112,18 @@ def main(ref: Path) -> None:
     summary = {k: {"shape": list(v.shape), "sha": digest(v), "sum": float(np.nansum(v[np.isfinite(v)]))}
                for k, v in conv.items()}
     (HERE / "convert.json").write_text(json.dumps(summary, indent=1, sort_keys=True))
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "bark.safetensors"
+        weights._save(conv, path)
+        sha = hashlib.sha256(path.read_bytes()).hexdigest()
+        (HERE / "cache_file.json").write_text(json.dumps({"sha256": sha, "order": list(conv)}, indent=1))
+
+        # Detokeniser: the reference's Tokenizer on the seeded tokenizer.
+        tok = text.Tokenizer(synthetic.tokenizer(Path(d) / "tokenizer.json"))
+        texts = [tok.decode(ids) for ids in text_cases()]
+    (HERE / "text.json").write_text(json.dumps({"texts": texts}, ensure_ascii=False, indent=0))
 
     # Length helpers.
     ns = list(range(0, 70)) + [99, 100, 101, 255, 256, 257, 1000, 3000, 60000]
@@ -152,4 +182,6 @@ def main(ref: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py /path/to/tinybark")
+    main(Path(sys.argv[1]))

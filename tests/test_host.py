@@ -98,6 +98,50 @@ def test_joined_piece_bytes_are_the_tokenizers_text(tmp_path):
         assert finish(joined) == tok.decode(ids), ids
 
 
+def test_piece_table_refuses_what_the_join_cannot_match(tmp_path):
+    """An empty ordinary piece or an id without a piece below the largest id: the GPU
+    join would not equal decode (merged byte runs; no KeyError), so table() refuses."""
+    for vocab in ({"a": 0, "": 1, "b": 2}, {"a": 0, "b": 2}):
+        path = tmp_path / "tokenizer.json"
+        path.write_text(json.dumps({"model": {"vocab": vocab}, "added_tokens": []}))
+        with pytest.raises(ValueError):
+            Tokenizer(str(path)).table()
+
+
+def test_detokeniser_matches_reference_tokenizer(tmp_path):
+    """tinybark.text.Tokenizer.decode's texts (tests/golden/text.json) on 300 seeded id
+    lists under the seeded 8193-id tokenizer: this module's decode, and the GPU join
+    restated (the piece table's bytes joined, then finish), give the same texts."""
+    from conftest import golden_json, synthetic_tokenizer
+    from golden.make_golden import text_cases
+    from tinybark_b200.text import finish
+
+    want = golden_json("text.json")["texts"]
+    tok = Tokenizer(synthetic_tokenizer(tmp_path / "tokenizer.json"))
+    off, data = tok.table()
+    cases = text_cases()
+    assert len(cases) == len(want)
+    for ids, text in zip(cases, want):
+        assert tok.decode(ids) == text
+        assert finish(b"".join(bytes(data[off[i] : off[i + 1]]) for i in ids)) == text
+
+
+def test_cache_file_is_the_references(tmp_path):
+    """convert + save of the 2-layer synthetic weights write the same bytes, tensor order
+    and header included, as tinybark's _convert + _save (tests/golden/cache_file.json)."""
+    import hashlib
+
+    from conftest import golden_json, state_dict
+    from tinybark_b200 import synthetic, weights
+
+    want = golden_json("cache_file.json")
+    conv = weights.convert(state_dict(2), synthetic.config(2))
+    assert list(conv) == want["order"]
+    path = tmp_path / "bark.safetensors"
+    weights.save(conv, path)
+    assert hashlib.sha256(path.read_bytes()).hexdigest() == want["sha256"]
+
+
 def test_registry_has_cuda_backend():
     b = backends.BACKENDS["cuda"]
     assert b.name == "cuda" and set(b.descriptions) <= set(backends.DEVICES)
@@ -109,3 +153,38 @@ def test_cpu_device_is_refused():
 
     with pytest.raises(RuntimeError):
         tinybark_b200.Bark("cpu", weights=({}, {}))
+
+
+def _csource_constant(name: str) -> int:
+    import re
+
+    from conftest import ROOT
+
+    text = (ROOT / "tinybark_b200" / "csrc" / "common.cuh").read_text()
+    return int(re.search(rf"constexpr int {name} = (0x[0-9A-Fa-f]+);", text).group(1), 16)
+
+
+def test_reciprocal_seed_is_minimax_and_newton_bound():
+    """rcp_newton's seed constant minimises max |1 - y r0| over every float mantissa (its
+    neighbours do worse), and the seed refined by two Newton steps, restated in float32
+    with numpy, is within 8e-6 of 1/y for every mantissa at several exponents."""
+    seed = _csource_constant("RCP_SEED")
+    m = np.arange(1 << 23, dtype=np.int64)
+    bits = (127 << 23) | m
+    y = bits.astype(np.uint32).view(np.float32)
+
+    def worst(c):
+        r0 = (np.int64(c) - bits).astype(np.uint32).view(np.float32).astype(np.float64)
+        return np.abs(1 - y.astype(np.float64) * r0).max()
+
+    e = worst(seed)
+    assert e < 0.0506 and e <= worst(seed - 1) and e <= worst(seed + 1)
+    for shift in (0, 5, 40, 110):
+        yb = bits + (shift << 23)
+        ys = yb.astype(np.uint32).view(np.float32)
+        r = (np.int64(seed) - yb).astype(np.uint32).view(np.float32)
+        two = np.float32(2)
+        for _ in range(2):
+            r = r * (two - ys * r)
+        rel = np.abs(r.astype(np.float64) * ys.astype(np.float64) - 1)
+        assert rel.max() < 8e-6, shift

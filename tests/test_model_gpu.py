@@ -287,3 +287,47 @@ def test_transcribe_batch_is_the_tokenizers_text(tmp_path):
     texts = bark.transcribe_batch(clips)
     assert texts == [tok.decode(t) for t in tokens] and texts[3] == ""
     assert bark.transcribe(clips[2]) == texts[2]
+
+
+def test_gpu_text_join_is_the_reference_detokeniser(tmp_path):
+    """The GPU join (tb_text_offsets / tb_text_bytes, then text.finish) on 300 seeded id
+    lists gives tinybark.text.Tokenizer.decode's texts (tests/golden/text.json, made by
+    the reference itself under the seeded 8193-id tokenizer)."""
+    from conftest import golden_json, synthetic_tokenizer
+    from golden.make_golden import text_cases
+    from tinybark_b200.text import Tokenizer, finish
+
+    want = golden_json("text.json")["texts"]
+    cases = text_cases()
+    eng = make_engine(2, "bf16")
+    table = eng.text_table(*Tokenizer(synthetic_tokenizer(tmp_path / "tokenizer.json")).table())
+    ld = max(len(c) for c in cases)
+    rows = np.zeros((len(cases), ld), np.int32)
+    for i, c in enumerate(cases):
+        rows[i, : len(c)] = c
+    counts = np.array([len(c) for c in cases], np.int32)
+    raw = eng.texts(torch.from_numpy(rows).cuda(), torch.from_numpy(counts).cuda(), table)
+    assert [finish(r) for r in raw] == want
+
+
+def test_tokens_long_matches_oracle_piece_by_piece():
+    """fp32, a 40 s recording through Bark.tokens_long: the oracle pipeline (front-end,
+    encoder, greedy loop) run on each piece at the same cut points, joined, gives the
+    same tokens."""
+    import tinybark_b200
+    from oracle import decoder, frontend
+    from oracle import encoder as oenc
+    from tinybark_b200 import longform, synthetic, weights
+
+    sd = state_dict(2)
+    bark = tinybark_b200.load("gpu", dtype="fp32", weights=(weights.convert(sd, synthetic.config(2)), synthetic.config(2)))
+    long = synthetic.to_float(synthetic.clip(40.0, 6, segment=2.0))
+    cuts = longform.cut_points(long)
+    assert len(cuts) >= 3
+    dec = decoder.Decoder(sd)
+    pieces = []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        feats = frontend.features(long[a:b])
+        pieces.append(dec.greedy(oenc.encode(sd, feats), len(feats)) if len(feats) >= 2 else [])
+    got = bark.tokens_long(long)
+    assert got == longform.join(pieces) and len(got) > 0

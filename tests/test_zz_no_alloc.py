@@ -3,7 +3,7 @@
 stream; a host whose device memory belongs to another allocator). It keeps its scratch in
 a fixed array inside the library instead of a caller-supplied workspace; its features
 must equal tb_frontend's, call after call, since the array keeps the previous call's
-contents. Collected last, so a run that stops at the first failure has run the rest."""
+contents; the same kernels run on the same inputs, so bit for bit. Collected last, so a run that stops at the first failure has run the rest."""
 
 import ctypes
 
@@ -43,9 +43,14 @@ def test_static_front_end_matches_workspace_front_end_twice():
     keep = []
     model = front_end_model(L, keep)
     stream = torch.cuda.current_stream().cuda_stream
+    rng = np.random.default_rng(4)
+    full = [synthetic.to_float(synthetic.clip(float(s), 200 + i))
+            for i, s in enumerate(rng.uniform(0.02, 12.0, L.FRONTEND_STATIC_MAX_CLIPS))]
     batches = [
         [synthetic.to_float(synthetic.clip(s, 70 + i)) for i, s in enumerate((3.1, 0.02, 12.0, 7.77, 1.0))],
         [synthetic.to_float(synthetic.clip(s, 90 + i)) for i, s in enumerate((0.5, 29.9, 2.2))],
+        full,  # exactly as many clips as the scratch holds
+        full[:2],
     ]
     for clips in batches:
         samples, soff, foff, frames = packed(clips)
@@ -58,7 +63,8 @@ def test_static_front_end_matches_workspace_front_end_twice():
         L.check(L.lib.tb_frontend_static(ctypes.byref(model), samples.data_ptr(), soff.data_ptr(), foff.data_ptr(),
                                          len(clips), frames, got.data_ptr(), stream), "tb_frontend_static")
         torch.cuda.synchronize()
-        np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), rtol=0, atol=2e-4)
+        # The same kernels on the same inputs: the same bits.
+        np.testing.assert_array_equal(got.cpu().numpy(), ref.cpu().numpy())
 
 
 def test_static_front_end_rejects_batches_beyond_its_scratch():

@@ -50,15 +50,25 @@ class Tokenizer:
 
     def table(self) -> tuple[np.ndarray, np.ndarray]:
         """The piece table of the GPU join: offsets [vocab + 1] (int32) into the bytes
-        (uint8) of every id, vocab = the largest id + 1. A special token (or an id without a
-        piece) has no bytes, a byte-fallback piece is its byte, any other piece is its UTF-8
-        with "▁" as a space."""
+        (uint8) of every id, vocab = the largest id + 1. A special token has no bytes, a
+        byte-fallback piece is its byte, any other piece is its UTF-8 with "▁" as a space.
+
+        The join equals `decode` only if no other piece is empty (an empty piece between
+        two byte runs would merge them into one UTF-8 sequence) and every id below vocab has
+        a piece (decode raises KeyError on one without; the GPU join cannot tell it from a
+        special token): a tokenizer breaking either rule raises ValueError here. Ids at or
+        above vocab are flagged by the GPU join (TB_DEV_TEXT_TOKEN)."""
         vocab = max(self.pieces) + 1
+        missing = [i for i in range(vocab) if i not in self.pieces]
+        if missing:
+            raise ValueError(f"tokenizer has no piece for ids {missing[:8]}: the GPU join needs one for every id")
         parts = []
         for i in range(vocab):
-            piece = self.pieces.get(i)
-            if piece is None or i in self.special:
+            piece = self.pieces[i]
+            if i in self.special:
                 parts.append(b"")
+            elif piece == "":
+                raise ValueError(f"tokenizer piece {i} is empty: the GPU join needs non-empty pieces")
             elif m := _BYTE.fullmatch(piece):
                 parts.append(bytes([int(m.group(1), 16)]))
             else:
