@@ -1,18 +1,24 @@
 """Throughput of the cuda backend: RTFx (audio seconds per wall second) of the whole path
-(log-mel front-end, 24-layer encoder, TDT greedy decode) on synthetic speech-like clips
-of 2-30 s (seeded, uniform), with seeded random-init weights of the Parakeet-TDT-0.6B-v3
-architecture, bf16. One process per GPU; each rank decodes its own shard of clips with
-no collective on the data path (weak scaling: `--clips-per-rank` per GPU, 512 by
-default, so 8 GPUs process the 4096-clip set of the whole-box workload).
+(log-mel front-end, 24-layer encoder, TDT greedy decode) on the whole-box workload: 4096
+synthetic speech-like clips of 2-30 s (durations uniform, seeded), with seeded random-init
+weights of the Parakeet-TDT-0.6B-v3 architecture, bf16. One process per GPU: the clips are
+dealt to the GPUs longest processing time first (tinybark_b200.dp.deal) and each rank
+transcribes its shard end to end with no collective on the data path (strong scaling: the
+same 4096 clips at every GPU count; one GPU runs them all as one batch).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Prints one JSON line (rank 0). `value` is device-timed with inputs resident in HBM;
-`e2e` is the same metric through the public API (Bark.tokens_batch on host arrays,
-host<->device copies inside the timed region). `--impl reference` times the reference
-path's CPU implementation (the CPU oracle: tinybark's front-end restated in numpy,
-transformers' ParakeetEncoder, the TDT loop restated in torch) on the host cores.
+Prints one JSON line (rank 0). `value` is device-timed with the samples resident in HBM
+(16-bit PCM, as tinybark's transcribe_pcm takes it); `e2e` is the same metric through the
+public API (Bark.tokens_batch on host int16 arrays, host<->device copies inside the timed
+region). `roofline` is the persistent TDT decoder (the step's largest kernel), timed
+inside the timed region; `roofline_kernels` adds the encoder's FFN GEMM, attention,
+depthwise conv and LayerNorm timed alone at the step's shapes; `config0` is the batch-1
+fp32 end-to-end transcription of one 10 s clip (cold run, then warm runs).
+`--impl reference` times the reference path's CPU implementation (the CPU oracle:
+tinybark's front-end restated in numpy, transformers' ParakeetEncoder, the TDT loop
+restated in torch) on the host cores.
 """
 
 from __future__ import annotations
@@ -35,8 +41,15 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "RTFx (audio-s per wall-s) per box at 1/2/4/8 B200; encoder ms per 10 s clip"
-WORKLOAD = "whole-box: synthetic clips 2-30 s (uniform, seeded), packed end to end, front-end + encoder + TDT decode"
+WORKLOAD = ("whole-box: 4096 synthetic clips 2-30 s (uniform, seeded) dealt to the GPUs longest processing time "
+            "first, packed end to end, front-end + encoder + TDT decode")
 SEED = 4
+CLIPS = 4096
+# Algorithmic work of the greedy loop (tinybark/tinygrad/model.py:162-233): the joint on
+# every iteration (8193 token + 5 duration logits from 640 inputs) and, for every emitted
+# token, the prediction step (two LSTM layers of [x | h] 1280 -> 2560 gates, projector 640 -> 640).
+JOINT_FLOP = 2 * (8193 + 5) * 640
+STEP_FLOP = 2 * 2 * 2560 * 1280 + 2 * 640 * 640
 
 
 def args_parser():
@@ -45,10 +58,11 @@ def args_parser():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--clips-per-rank", type=int, default=512)
+    p.add_argument("--clips", type=int, default=CLIPS, help="clips of the whole-box set, dealt over the GPUs")
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-config0", action="store_true", help="skip the batch-1 fp32 end-to-end line")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
     p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform,load,text)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
@@ -64,17 +78,26 @@ def rank_info():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
-def shard(rank: int, count: int):
-    """This rank's clips: durations uniform in [2, 30) s and audio, both seeded by rank."""
-    from tinybark_b200 import synthetic
+def box_frames(count: int) -> list[int]:
+    """Feature frames of every clip of the whole-box set (durations uniform in [2, 30) s)."""
+    from tinybark_b200 import lengths, synthetic
 
-    durs = synthetic.durations(count, SEED * 1000 + rank)
-    seeds = [SEED * 10_000_000 + rank * 100_000 + i for i in range(count)]
-    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4)) as pool:
-        pcm = list(pool.map(lambda a: synthetic.clip(*a), zip(durs, seeds)))
-    # Longest first, as Bark.tokens_batch orders a batch.
-    order = np.argsort(-durs, kind="stable")
-    return [synthetic.to_float(pcm[i]) for i in order], durs[order]
+    return [lengths.frames(int(round(d * 16000))) for d in synthetic.durations(count, SEED * 1000)]
+
+
+def shard(rank: int, world: int, count: int = CLIPS):
+    """This rank's clips of the whole-box set, as int16 PCM, longest first (the order
+    Bark.tokens_batch gives a batch), with their durations: the set's clips dealt over
+    `world` GPUs by dp.deal; each clip's audio seeded by its index in the set, so a clip
+    is the same whichever rank draws it."""
+    from tinybark_b200 import dp, synthetic
+
+    durs_all = synthetic.durations(count, SEED * 1000)
+    mine = dp.deal(box_frames(count), world)[rank]
+    mine = sorted(mine, key=lambda i: (-durs_all[i], i))
+    with ThreadPoolExecutor(max_workers=min(32, os.cpu_count() or 4)) as pool:
+        pcm = list(pool.map(lambda i: synthetic.clip(float(durs_all[i]), SEED * 10_000_000 + i), mine))
+    return pcm, np.asarray([durs_all[i] for i in mine])
 
 
 def reduce_over_ranks(x: float, op: str, device) -> float:
@@ -177,6 +200,8 @@ def cpu_pipeline_factory(layers: int):
     dec = decoder.Decoder(sd)
 
     def run(samples: np.ndarray) -> list[int]:
+        if samples.dtype == np.int16:
+            samples = synthetic.to_float(samples)
         feats = frontend.features(samples)
         if len(feats) < 2:
             return []
@@ -194,22 +219,32 @@ def cpu_pipeline_factory(layers: int):
 def cpu_baseline(clips, durs, layers: int, budget_s: float):
     run, dtype, threads = cpu_pipeline_factory(layers)
     run(clips[0][:16000])  # warm-up
+    # Clips spread over the shard's lengths (it is ordered longest first), until the budget.
+    pick = np.unique(np.linspace(0, len(clips) - 1, min(len(clips), 64)).round().astype(int))
+    order = [int(i) for k in range(4) for i in pick[k::4]]
     audio, start, n = 0.0, time.perf_counter(), 0
-    while n < len(clips) and (n == 0 or time.perf_counter() - start < budget_s):
-        run(clips[n])
-        audio += durs[n]
+    while n < len(order) and (n == 0 or time.perf_counter() - start < budget_s):
+        run(clips[order[n]])
+        audio += durs[order[n]]
         n += 1
     wall = time.perf_counter() - start
     return {"value": audio / wall, "unit": "audio-s/s", "cores": threads, "kind": "port",
-            "sample": f"{n} clips ({audio:.1f} s of audio) of the same workload, one at a time, {dtype}, "
-                      f"tinybark front-end restated + transformers ParakeetEncoder + TDT loop restated"}
+            "sample": f"{n} clips ({audio:.1f} s of audio) spread over the lengths of the same workload, one at a "
+                      f"time, {dtype}, tinybark front-end restated + transformers ParakeetEncoder + TDT loop restated"}
 
 
 def run_reference(args):
     rank, world, _ = rank_info()
     if rank != 0:
         return
-    clips, durs = shard(0, max(8, args.steps + args.warmup))
+    # A bounded sample of the same set: the first clips of rank 0's shard at this GPU
+    # count, one clip per step.
+    from tinybark_b200 import dp
+
+    n = max(8, args.steps + args.warmup)
+    clips, durs = shard(0, 1, args.clips) if world == 1 else shard(0, world, args.clips)
+    pick = np.linspace(0, len(clips) - 1, n).round().astype(int)
+    clips, durs = [clips[i] for i in pick], durs[pick]
     run, dtype, threads = cpu_pipeline_factory(args.layers)
     for i in range(args.warmup):
         run(clips[i % len(clips)][:32000])
@@ -221,12 +256,13 @@ def run_reference(args):
         audio += durs[i % len(clips)]
     wall = sum(times)
     value = audio / wall
+    del dp
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "audio-s/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * wall / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": "one clip per step, clips of rank 0's shard",
-                   "layers": args.layers},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": {"workload": WORKLOAD, "clips": args.clips, "layers": args.layers,
+                   "sample": "one clip per step, spread over the lengths of rank 0's shard, on one host process"},
         "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} clips ({audio:.1f} s audio), {dtype}"},
         "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -248,12 +284,9 @@ def run_ours(args):
 
     import tinybark_b200
     from tinybark_b200 import _lib as L
-    from tinybark_b200.engine import Engine, lane_order
+    from tinybark_b200.engine import Engine
 
-    clips, durs = shard(rank, args.clips_per_rank)
-    # The decoder's lane order, as Bark.tokens_batch orders a batch.
-    order = lane_order(list(range(len(clips))), [len(c) // 160 for c in clips], args.decode_groups or None)
-    clips, durs = [clips[i] for i in order], durs[order]
+    clips, durs = shard(rank, world, args.clips)
     tensors, cfg = weights(args.layers)
     bark = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg))
     eng: Engine = bark.engine
@@ -261,11 +294,19 @@ def run_ours(args):
     plan = eng.plan([len(c) // 160 for c in clips])
     samples, sample_off = eng.upload(clips)
     torch.cuda.synchronize()
+    dec_ev = []  # (start, end) of each decode in the timed region
 
-    def step():
+    def step(events=None):
         feats = eng.features(samples, sample_off, plan)
         enc = eng.encode(feats, plan)
-        return eng.decode(enc, plan, groups=args.decode_groups or None)
+        if events is not None:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        out = eng.decode(enc, plan, groups=args.decode_groups or None)
+        if events is not None:
+            b.record()
+            events.append((a, b))
+        return out
 
     def barrier():
         torch.cuda.synchronize()
@@ -287,35 +328,37 @@ def run_ours(args):
     with Clocks(local) as clocks:
         start.record()
         for _ in range(args.steps):
-            tokens, counts = step()
+            tokens, counts = step(dec_ev)
         end.record()
         torch.cuda.synchronize()
     launches = (L.lib.tb_launch_count() - launches0) // args.steps
     eng.check()
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
+    decode_s = sum(a.elapsed_time(b) for a, b in dec_ev) / len(dec_ev) / 1000
+    iters = int(eng.lane_iterations().sum().item()) if not args.decode_groups else None
+    emitted = int(counts.sum().item())
     barrier()
     stages = stage_split(eng, samples, sample_off, plan, args.decode_groups or None)
     total_audio = reduce_over_ranks(audio_rank, "sum", dev)
     value = total_audio / (ms / 1000.0)
 
-    # End to end through the public API: host float32 arrays in, token lists out.
-    for _ in range(1):
-        bark.tokens_batch(clips)
+    # End to end through the public API: host int16 arrays in, token lists out.
+    bark.tokens_batch(clips)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        out = bark.tokens_batch(clips)
+        bark.tokens_batch(clips)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    h2d = int(sum(len(c) for c in clips) * 4 + (len(clips) + 1) * 8 + plan.meta.numel() * 4)
+    h2d = int(sum(len(c) for c in clips) * 2 + (len(clips) + 1) * 8 + plan.meta.numel() * 4)
     d2h = int(len(clips) * plan.max_cap * 4 + len(clips) * 4)
 
-    # Encoder ms per 10 s clip, batch 1.
+    # Encoder ms per 10 s clip, batch 1 (bf16).
     from tinybark_b200 import synthetic
 
-    one = [synthetic.to_float(synthetic.clip(10.0, 0))]
+    one = [synthetic.clip(10.0, 0)]
     p1 = eng.plan([1000])
     s1, o1 = eng.upload(one)
     f1 = eng.features(s1, o1, p1)
@@ -329,35 +372,23 @@ def run_ours(args):
     torch.cuda.synchronize()
     enc10_ms = a.elapsed_time(b) / 10
 
-    # Roofline of the dominant kernel (the tcgen05 GEMM), timed alone at the FFN
-    # up-projection of this step: M = encoder frames of the shard, N = 4096, K = 1024.
-    M = plan.batch.t3_total
-    x = torch.randn(M, 1024, device=dev).to(torch.bfloat16)
-    w = (torch.randn(4096, 1024, device=dev) / 32).to(torch.bfloat16)
-    h = torch.empty(M, 4096, device=dev, dtype=torch.bfloat16)
-    ep = L.Epilogue(kind=L.EPI_SILU, out_dtype=L.BF16, out=h.data_ptr(), ldo=4096)
-    import ctypes
-
-    def ffn():
-        L.check(L.lib.tb_gemm(L.BF16, x.data_ptr(), 1024, w.data_ptr(), M, 4096, 1024, ctypes.byref(ep),
-                              eng.err.data_ptr(), torch.cuda.current_stream().cuda_stream), "tb_gemm")
-
-    for _ in range(3):
-        ffn()
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record()
-    for _ in range(20):
-        ffn()
-    g1.record()
-    torch.cuda.synchronize()
-    gemm_s = g0.elapsed_time(g1) / 20 / 1000
     hbm, tflops, kind = peaks()
-    achieved = 2.0 * M * 4096 * 1024 / gemm_s / 1e12
-    traffic = None
-    tpath = ROOT / "profiles" / "traffic.json"
-    if tpath.exists():
-        t = json.loads(tpath.read_text()).get("gemm_ffn_up_bytes_per_row")
-        traffic = None if t is None else t * M
+    sustained = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops_sustained") \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else None
+    dec_flop = (iters * JOINT_FLOP + emitted * STEP_FLOP) if iters is not None else None
+    roof_peak = sustained or 1400.0
+    roofline = {
+        "bound": "tensor", "unit": "TFLOP/s", "peak": roof_peak,
+        "peak_kind": f"{'measured' if sustained else 'fallback'} sustained bf16 (timed inside the step)",
+        "kernel": f"decode_tc_kernel (persistent TDT greedy decode, {len(clips)} lanes)",
+        "achieved": None if dec_flop is None else dec_flop / decode_s / 1e12,
+        "frac": None if dec_flop is None else dec_flop / decode_s / 1e12 / roof_peak,
+        "traffic": traffic_of("decode_tc_kernel_bytes_per_lane_iter", iters),
+        "work": {"lane_iterations": iters, "emitted_tokens": emitted, "flop": dec_flop,
+                 "flop_per_iteration": JOINT_FLOP, "flop_per_token": STEP_FLOP},
+        "launch_ms": decode_s * 1000,
+    }
+    kernels = roofline_kernels(eng, plan, dev, hbm, tflops, kind)
 
     if world > 1:
         dist.barrier()
@@ -365,24 +396,24 @@ def run_ours(args):
         base = None
         if world == 1 and not args.no_cpu_baseline:
             base = cpu_baseline(clips, durs, args.layers, args.cpu_seconds)
+        config0 = None if (world > 1 or args.no_config0) else run_config0(args, tensors, cfg)
         line = {
             "metric": METRIC, "value": value, "unit": "audio-s/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "clips_per_rank": len(clips), "audio_s_per_rank": round(audio_rank, 2),
-                       "encoder_frames_per_rank": int(M), "layers": args.layers, "parallelism": f"dp{world}",
+            "config": {"workload": WORKLOAD, "clips": args.clips, "clips_rank0": len(clips),
+                       "audio_s_rank0": round(audio_rank, 2), "audio_s_total": round(total_audio, 2),
+                       "encoder_frames_rank0": int(plan.batch.t3_total), "layers": args.layers,
+                       "parallelism": f"dp{world}", "input": "int16 PCM",
                        "l2": "inputs larger than L2 (samples and weights, >126 MB per step)"},
             "encoder_ms_per_10s_clip": enc10_ms,
             "stages_ms_rank0": stages,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
-                         "frac": achieved / tflops, "traffic": traffic,
-                         "kernel": (f"gemm_tc2_kernel (CTA pairs, 256 x 256 tiles) FFN up M={M} N=4096 K=1024, "
-                                    "timed alone" if M >= 2048 else
-                                    f"gemm_tc_kernel<256> FFN up M={M} N=4096 K=1024, timed alone"),
-                         "peak_kind": f"{kind} burst bf16"},
+            "roofline": roofline,
+            "roofline_kernels": kernels,
             "cpu_baseline": base,
             "e2e": {"value": total_audio / (e2e_ms / 1000.0), "unit": "audio-s/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "config0": config0,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
@@ -390,6 +421,114 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def traffic_of(key: str, units):
+    """DRAM bytes per launch from profiles/traffic.json (bytes per unit, from one ncu
+    capture) scaled to `units`, or None."""
+    path = ROOT / "profiles" / "traffic.json"
+    if units is None or not path.exists():
+        return None
+    per = json.loads(path.read_text()).get(key)
+    return None if per is None else per * units
+
+
+def roofline_kernels(eng, plan, dev, hbm, tflops, kind):
+    """The encoder's kernels timed alone (median of launches with L2 flushed) at this
+    step's shapes: FFN up (tcgen05 GEMM, SiLU epilogue), rel-pos attention over the step's
+    clips, depthwise conv + SiLU, LayerNorm; each against its roofline (burst bf16 peak or
+    HBM copy bandwidth)."""
+    import torch
+
+    from tinybark_b200 import _lib as L
+    from tinybark_b200 import kernels as K
+
+    M = plan.batch.t3_total
+    g = torch.Generator(device=dev).manual_seed(0)
+    rnd = lambda *s, dt=torch.bfloat16: torch.randn(*s, device=dev, generator=g).to(dt)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = []
+    x, w1 = rnd(M, 1024), rnd(4096, 1024) / 32
+    h = torch.empty(M, 4096, device=dev, dtype=torch.bfloat16)
+    ep = L.Epilogue(kind=L.EPI_SILU, out_dtype=L.BF16, out=h.data_ptr(), ldo=4096)
+    s = timed(lambda: K.gemm(x, w1, ep), iters=10, flush=flush)
+    fl = 2.0 * M * 4096 * 1024
+    out.append({"kernel": "gemm_tc2_kernel FFN up + SiLU" if M >= 2048 else "gemm_tc_kernel FFN up + SiLU",
+                "rows": M, "bound": "tensor", "us": s * 1e6, "achieved": fl / s / 1e12, "peak": tflops,
+                "unit": "TFLOP/s", "frac": fl / s / 1e12 / tflops, "peak_kind": f"{kind} burst bf16",
+                "traffic": traffic_of("gemm_ffn_up_bytes_per_row", M)})
+    del h
+    t3 = [int(t) for t in plan.t3]
+    frames = K.Frames(t3, L.BF16, dev)
+    qu, qv, k, v = (rnd(M, 1024) for _ in range(4))
+    T = max(t3)
+    eng.ensure_len(T)
+    rel = rnd(2 * eng.max_len - 1, 1024)
+    rel_c = K.rel_bias(rel, rnd(1024, dt=torch.float32), rnd(1024, dt=torch.float32))
+    att = torch.empty(M, 1024, device=dev, dtype=torch.bfloat16)
+    s = timed(lambda: K.attention(qu, qv, k, v, rel, eng.max_len, frames, att, rel_c), iters=5, flush=flush)
+    fl = 6.0 * 1024 * sum(t * t for t in t3)
+    out.append({"kernel": "relpos_attention_tc", "rows": M, "clips": len(t3), "bound": "tensor", "us": s * 1e6,
+                "achieved": fl / s / 1e12, "peak": tflops, "unit": "TFLOP/s", "frac": fl / s / 1e12 / tflops,
+                "peak_kind": f"{kind} burst bf16", "work": "6 T^2 1024 FLOP per clip (QK, banded position scores, PV)"})
+    del qu, qv, k, v, att
+    glu, dwo = rnd(M, 1024), torch.empty(M, 1024, device=dev, dtype=torch.bfloat16)
+    dww, dwb = rnd(1024, 9, dt=torch.float32), rnd(1024, dt=torch.float32)
+    s = timed(lambda: K.depthwise(glu, dww, dwb, frames, dwo), iters=10, flush=flush)
+    nb = 2.0 * M * 1024 * 2
+    out.append({"kernel": "depthwise_stream_kernel (k=9, folded BN, SiLU)", "rows": M, "bound": "hbm",
+                "us": s * 1e6, "achieved": nb / s / 1e9, "peak": hbm, "unit": "GB/s", "frac": nb / s / 1e9 / hbm,
+                "work": "bf16 rows read once and written once"})
+    del glu, dwo
+    xf, lw, lb = rnd(M, 1024, dt=torch.float32), rnd(1024, dt=torch.float32), rnd(1024, dt=torch.float32)
+    y = torch.empty(M, 1024, device=dev, dtype=torch.bfloat16)
+    s = timed(lambda: K.layernorm(xf, lw, lb, y), iters=10, flush=flush)
+    nb = M * 1024 * (4.0 + 2.0)
+    out.append({"kernel": "layernorm_kernel (fp32 in, bf16 out)", "rows": M, "bound": "hbm", "us": s * 1e6,
+                "achieved": nb / s / 1e9, "peak": hbm, "unit": "GB/s", "frac": nb / s / 1e9 / hbm})
+    K.check(dev)
+    return out
+
+
+def run_config0(args, tensors, cfg):
+    """Config 0: batch 1, fp32, one 10 s clip (seed 0) end to end through Bark.tokens, timed
+    as tinybark's benchmark worker times a clip (a first, cold call after loading, then warm
+    calls; tinybark/bench/worker.py:37-44); plus the fp32 encoder alone."""
+    import torch
+
+    import tinybark_b200
+    from tinybark_b200 import synthetic
+
+    bark = tinybark_b200.load("gpu", dtype="fp32", weights=(tensors, cfg))
+    clip = synthetic.to_float(synthetic.clip(10.0, 0))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = bark.tokens(clip)
+    cold = time.perf_counter() - t0
+    warm = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        tokens = bark.tokens(clip)
+        warm.append(time.perf_counter() - t0)
+    assert tokens == first
+    eng = bark.engine
+    plan = eng.plan([1000])
+    s1, o1 = eng.upload([clip])
+    f1 = eng.features(s1, o1, plan)
+    for _ in range(2):
+        eng.encode(f1, plan)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        eng.encode(f1, plan)
+    b.record()
+    torch.cuda.synchronize()
+    enc_ms = a.elapsed_time(b) / 5
+    del bark
+    torch.cuda.empty_cache()
+    return {"workload": "batch 1, fp32, one 10 s clip (seed 0), Bark.tokens from a host float32 array",
+            "cold_ms": cold * 1000, "warm_ms_best": min(warm) * 1000, "warm_ms_mean": statistics.mean(warm) * 1000,
+            "rtfx_warm": 10.0 / min(warm), "encoder_ms": enc_ms, "tokens": len(first)}
 
 
 def timed(fn, iters: int = 10, flush=None) -> float:
@@ -701,7 +840,7 @@ def run_profile(args):
     from tinybark_b200.engine import lane_order
 
     groups = args.decode_groups or None
-    clips, durs = shard(0, args.clips_per_rank)
+    clips, durs = shard(0, 1, args.clips)
     order = lane_order(list(range(len(clips))), [len(c) // 160 for c in clips], groups)
     clips, durs = [clips[i] for i in order], durs[order]
     tensors, cfg = weights(args.layers)

@@ -305,6 +305,12 @@ int tb_selftest_wait(int kind, void* scratch, int* err, void* stream);
 int tb_selftest_math(int kind, const float* x, float* y, long long n, void* stream);
 
 size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups);
+/* After a tb_tdt_decode with groups 0 or 1 on this workspace (and stream): the greedy-loop
+ * iterations each lane ran (tinybark/tinygrad/model.py:222-233 counts them against the
+ * cap), copied into iters [lanes] (device int32). The algorithmic work of a decode is these
+ * iterations times the work of one (joint on every iteration, prediction step on each
+ * emitted token); measurement only. TB_ERR_ARG for other groups. */
+int tb_decode_lane_iterations(const void* ws, int dtype, int lanes, int groups, int* iters, void* stream);
 int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                   int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
                   void* stream);

@@ -1,6 +1,7 @@
 """The multi-rank host logic of bench.py on CPU: two gloo ranks, as torchrun launches the
-GPU ranks. Each rank's shard is its own seeded set of clips (no collective on the data
-path), the step time is the max over ranks and the audio total the sum."""
+GPU ranks. The whole-box set is dealt over the ranks (every clip on exactly one rank, the
+same clip audio whichever rank draws it; no collective on the data path), the step time
+is the max over ranks and the audio total the sum."""
 
 import os
 import socket
@@ -29,16 +30,22 @@ def _rank(rank: int, world: int, port: int, out) -> None:
     import torch.distributed as dist
 
     import bench
+    from tinybark_b200 import dp
 
     dist.init_process_group("gloo", timeout=timedelta(seconds=60))
     try:
         r, w, local = bench.rank_info()
-        clips, durs = bench.shard(r, 3)
+        clips, durs = bench.shard(r, w, 24)
         step_ms = 100.0 + 10.0 * r  # rank 1 is the slower one
+        ids = torch.zeros(24, dtype=torch.int64)
+        mine = dp.deal(bench.box_frames(24), w)[r]
+        ids[mine] = 1
+        dist.all_reduce(ids)  # how many ranks hold each clip
         out.put({
             "rank": r, "world": w, "local": local,
             "durs": [float(d) for d in durs],
             "lens": [len(c) for c in clips],
+            "holders": ids.tolist(),
             "max": bench.reduce_over_ranks(step_ms, "max", torch.device("cpu")),
             "sum": bench.reduce_over_ranks(float(np.sum(durs)), "sum", torch.device("cpu")),
         })
@@ -58,8 +65,10 @@ def test_two_gloo_ranks_shard_and_reduce():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert [g["rank"] for g in got] == [0, 1] and all(g["world"] == 2 for g in got)
-    # Shards differ between ranks, are longest first and hold 2-30 s clips of 16 kHz audio.
-    assert got[0]["durs"] != got[1]["durs"]
+    # Every clip of the set on exactly one rank; shards longest first, 2-30 s of 16 kHz
+    # audio, balanced in length.
+    assert all(h == 1 for h in got[0]["holders"]) and got[0]["holders"] == got[1]["holders"]
+    assert abs(sum(got[0]["durs"]) - sum(got[1]["durs"])) < 0.1 * sum(got[0]["durs"])
     for g in got:
         assert g["durs"] == sorted(g["durs"], reverse=True)
         assert all(2.0 <= d < 30.0 for d in g["durs"])
@@ -70,11 +79,19 @@ def test_two_gloo_ranks_shard_and_reduce():
     assert all(abs(g["sum"] - total) < 1e-6 for g in got)
 
 
-def test_shard_is_deterministic():
+def test_shard_is_deterministic_and_independent_of_the_deal():
+    """A clip's audio depends only on its index in the set: rank 0 of 1 holds every
+    clip, and the clips rank 1 of 2 draws are the same arrays."""
     sys.path.insert(0, str(ROOT))
     import bench
+    from tinybark_b200 import dp
 
-    a, da = bench.shard(0, 2)
-    b, db = bench.shard(0, 2)
-    assert list(da) == list(db)
+    a, da = bench.shard(0, 1, 12)
+    b, db = bench.shard(0, 1, 12)
+    assert list(da) == list(db) and len(a) == 12
     assert all(np.array_equal(x, y) for x, y in zip(a, b))
+    assert all(x.dtype == np.int16 for x in a)
+    c, dc = bench.shard(1, 2, 12)
+    whole = {(len(x), x[:64].tobytes()) for x in a}
+    assert all((len(x), x[:64].tobytes()) in whole for x in c)
+    assert len(c) == len(dp.deal(bench.box_frames(12), 2)[1])

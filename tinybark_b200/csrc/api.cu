@@ -6,6 +6,7 @@
 #include <mutex>
 #include <string>
 
+#include "decode.cuh"
 #include "host.h"
 
 namespace tb {
@@ -315,6 +316,15 @@ size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups) {
   if (lanes <= 0) return 0;  // groups <= 0: the persistent decoder's workspace, that of one group
   groups = groups < 1 ? 1 : (groups > 8 ? 8 : groups);
   return decode_ws_groups(dtype, lanes, groups < lanes ? groups : lanes);
+}
+
+int tb_decode_lane_iterations(const void* ws, int dtype, int lanes, int groups, int* iters, void* stream) {
+  if (!ws || !iters || lanes <= 0 || groups > 1 || (dtype != TB_F32 && dtype != TB_BF16)) return TB_ERR_ARG;
+  const DecodeWs w = carve(const_cast<void*>(ws), dtype, lanes);
+  if (cudaMemcpyAsync(iters, w.it, (size_t)lanes * sizeof(int), cudaMemcpyDeviceToDevice, as_stream(stream)) !=
+      cudaSuccess)
+    return fail_cuda();
+  return TB_OK;
 }
 
 int tb_selftest_wait(int kind, void* scratch, int* err, void* stream) {

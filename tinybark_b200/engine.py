@@ -318,7 +318,18 @@ class Engine:
         L.check(L.lib.tb_tdt_decode(C.byref(self.model), enc.data_ptr(), plan.t3_off.data_ptr(), plan.caps.data_ptr(),
                                     b.clips, plan.max_cap, g, tokens.data_ptr(), counts.data_ptr(), ws.data_ptr(),
                                     nbytes, flag, self.err.data_ptr(), _stream(self.device)), "tb_tdt_decode")
+        self._last_decode = (ws, b.clips, g)
         return tokens, counts
+
+    def lane_iterations(self) -> torch.Tensor:
+        """Greedy-loop iterations each lane ran in the last decode (groups 0 or 1), [clips]
+        int32 on the device: the decode's algorithmic work is their sum times the work of
+        one iteration."""
+        ws, lanes, g = self._last_decode
+        it = torch.empty(lanes, dtype=torch.int32, device=self.device)
+        L.check(L.lib.tb_decode_lane_iterations(ws.data_ptr(), self.dtype, lanes, g, it.data_ptr(),
+                                                _stream(self.device)), "tb_decode_lane_iterations")
+        return it
 
     # ------------------------------------------------------------------ end to end
 

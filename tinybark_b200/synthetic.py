@@ -75,17 +75,34 @@ def clip(seconds: float, seed: int, segment: float | None = None) -> np.ndarray:
         f0 = np.repeat(rng.uniform(100.0, 250.0, -(-n // per)), per)[:n]
     else:
         f0 = np.full(n, rng.uniform(100.0, 250.0))
-    phase = 2.0 * np.pi * np.cumsum(f0) / SAMPLE_RATE
+    phase = np.cumsum(f0)
+    phase *= 2.0 * np.pi / SAMPLE_RATE
     offsets = rng.uniform(0.0, 2.0 * np.pi, 10)
-    signal = np.zeros(n)
-    for k in range(1, 11):
-        signal += np.sin(k * phase + offsets[k - 1]) / k
-    t = np.arange(n) / SAMPLE_RATE
-    signal *= 0.5 * (1.0 - np.cos(2.0 * np.pi * 4.0 * t + rng.uniform(0.0, 2.0 * np.pi)))
+    # sin(k phase + o_k) = sin(k phase) cos(o_k) + cos(k phase) sin(o_k), with sin and cos
+    # of k phase from those of (k-1) phase by the angle-addition formulas: two
+    # transcendental evaluations per sample instead of ten, in place.
+    s1, c1 = np.sin(phase), np.cos(phase)
+    sk, ck, t1, t2 = s1.copy(), c1.copy(), np.empty(n), np.empty(n)
+    signal = sk * np.cos(offsets[0])
+    signal += ck * np.sin(offsets[0])
+    for k in range(2, 11):
+        np.multiply(sk, c1, out=t1)
+        t1 += ck * s1
+        np.multiply(ck, c1, out=t2)
+        t2 -= sk * s1
+        sk, t1 = t1, sk
+        ck, t2 = t2, ck
+        signal += sk * (np.cos(offsets[k - 1]) / k)
+        signal += ck * (np.sin(offsets[k - 1]) / k)
+    env = np.arange(n, dtype=np.float64)
+    env *= 2.0 * np.pi * 4.0 / SAMPLE_RATE
+    env += rng.uniform(0.0, 2.0 * np.pi)
+    np.cos(env, out=env)
+    signal *= 0.5 * (1.0 - env)
     rms = np.sqrt(np.mean(signal**2)) or 1.0
-    signal += rng.standard_normal(n) * rms * 10.0 ** (-30.0 / 20.0)
-    signal *= 0.5 / max(np.abs(signal).max(), 1e-12)
-    return np.round(signal * 32767.0).astype(np.int16)
+    signal += rng.standard_normal(n) * (rms * 10.0 ** (-30.0 / 20.0))
+    signal *= 0.5 * 32767.0 / max(np.abs(signal).max(), 1e-12)
+    return np.round(signal).astype(np.int16)
 
 
 def to_float(pcm: np.ndarray) -> np.ndarray:
