@@ -315,6 +315,24 @@ int tb_tdt_decode(const tb_model* m, const float* enc, const int* enc_off, const
                   int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
                   void* stream);
 
+/* ---- block-scaled FP8 FFN GEMM (MXFP8): the low-precision weight option of
+ * tinybark/docs/2026-10-24-learnings.md:133-146 (no reference kernel; the bf16 GEMM,
+ * tb_gemm, is the default path) ----
+ * tb_mx_quantize: rows x k values (src_dtype TB_F32 or TB_BF16, row stride ld elements,
+ * 16-byte aligned, k a multiple of 512) to E4M3 codes [ceil(rows / 128) * 128, k] (row
+ * stride k; rows past `rows` get zero codes) and E8M0 scales, one per 32 values along k:
+ * e = floor(log2 max |x|) - 8 clamped to [-127, 127] (-127 for an all-zero block), codes
+ * E4M3(x * 2^-e) rounded to nearest even, saturated to +-448, scale byte e + 127. The
+ * scales are stored tiled as [rows / 128][k / 512][128][16] bytes: tb_mx_scale_bytes.
+ * tb_gemm_mx: C = A * W^T from two such matrices (m rows of A, n of W, n a multiple of
+ * 128, k a multiple of 512), fp32 accumulation, epilogue TB_EPI_STORE, TB_EPI_SILU or
+ * TB_EPI_RESIDUAL as tb_gemm's (no run-time row bound). */
+size_t tb_mx_scale_bytes(int rows, int k);
+int tb_mx_quantize(int src_dtype, const void* src, long long ld, int rows, int k, void* codes, void* scales,
+                   void* stream);
+int tb_gemm_mx(const void* a, const void* a_scales, const void* w, const void* w_scales, int m, int n, int k,
+               const tb_epilogue* e, int* err, void* stream);
+
 /* ---- weight loading: the fp16 cache (tinybark/weights.py:92-120), read whole as
  * tinybark/tinygrad/weights.py:10-26 reads it, then split into the kernels' layout ----
  * tb_repack writes the packed weights from one source buffer: the cache file's data block

@@ -104,6 +104,9 @@ def _load() -> C.CDLL:
         "tb_selftest_wait": (i32, [i32, vp, vp, vp]),
         "tb_selftest_math": (i32, [i32, vp, vp, ll, vp]),
         "tb_decode_lane_iterations": (i32, [vp, i32, i32, i32, vp, vp]),
+        "tb_mx_scale_bytes": (sz, [i32, i32]),
+        "tb_mx_quantize": (i32, [i32, vp, ll, i32, i32, vp, vp, vp]),
+        "tb_gemm_mx": (i32, [vp, vp, vp, vp, i32, i32, i32, P(Epilogue), vp, vp]),
         "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
         "tb_repack": (i32, [P(RepackJob), i32, vp, vp, sz, vp, sz, vp]),
         "tb_text_offsets": (i32, [vp, i32, vp, i32, vp, i32, vp, vp, vp]),
@@ -123,7 +126,8 @@ EXPORTS = (
     "tb_frontend_static", "tb_frontend_pcm16",
     "tb_layernorm", "tb_gemm", "tb_set_gemm_pairs", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
-    "tb_selftest_wait", "tb_selftest_math", "tb_decode_lane_iterations", "tb_repack", "tb_text_offsets", "tb_text_bytes",
+    "tb_selftest_wait", "tb_selftest_math", "tb_decode_lane_iterations", "tb_mx_scale_bytes", "tb_mx_quantize",
+    "tb_gemm_mx", "tb_repack", "tb_text_offsets", "tb_text_bytes",
 )
 
 

@@ -85,6 +85,32 @@ def depthwise(x, w, b, frames: Frames, y) -> None:
                                     y.data_ptr(), _err(x.device).data_ptr(), _stream()), "tb_conv_depthwise")
 
 
+class MX:
+    """A matrix [rows, K] in MXFP8 on the GPU (tb_mx_quantize): E4M3 codes [rows padded to
+    128, K] and E8M0 scales in the MMA's tiled layout (tb_mx_scale_bytes)."""
+
+    def __init__(self, x: torch.Tensor):
+        rows, k = x.shape
+        pad = -(-rows // 128) * 128
+        self.rows, self.k = rows, k
+        self.codes = torch.empty(pad, k, dtype=torch.uint8, device=x.device)
+        self.scales = torch.empty(L.lib.tb_mx_scale_bytes(rows, k), dtype=torch.uint8, device=x.device)
+        L.check(L.lib.tb_mx_quantize(dtype_of(x), x.data_ptr(), x.stride(0), rows, k, self.codes.data_ptr(),
+                                     self.scales.data_ptr(), _stream()), "tb_mx_quantize")
+
+    def scale_exponents(self) -> torch.Tensor:
+        """The E8M0 scale exponents (byte - 127) as [rows, K / 32] int, untiled."""
+        groups = self.k // 512
+        t = self.scales.view(-1, groups, 128, 16).permute(0, 2, 1, 3).reshape(-1, self.k // 32)
+        return t[: self.rows].to(torch.int32) - 127
+
+
+def gemm_mx(a: MX, w: MX, ep: L.Epilogue) -> None:
+    """A [M, K] times W [N, K]^T, both MXFP8, with epilogue `ep`."""
+    L.check(L.lib.tb_gemm_mx(a.codes.data_ptr(), a.scales.data_ptr(), w.codes.data_ptr(), w.scales.data_ptr(), a.rows,
+                             w.rows, a.k, C.byref(ep), _err(a.codes.device).data_ptr(), _stream()), "tb_gemm_mx")
+
+
 def check(device=None) -> None:
     device = torch.device("cuda") if device is None else torch.device(device)
     torch.cuda.synchronize(device)
