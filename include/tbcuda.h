@@ -156,7 +156,16 @@ typedef struct tb_model {
   const void* lstm0_hh;     /* [2560, 640]: the h columns of lstm_w[0] (its last 640), contiguous */
   const float* lstm0_emb;   /* [8193, 2560] fp32: embedding . (the x columns of lstm_w[0])^T,
                                the input term of layer 0's gates for every token */
+  /* block-scaled FFN (bf16 models only; NULL: the bf16 FFN): 4 per layer, ff1_w1, ff1_w2,
+     ff2_w1, ff2_w2, each in tb_mx_quantize's form */
+  const struct tb_mx_weight* ffn_mx;
 } tb_model;
+
+/* One weight matrix [n, k] in MXFP8 (tb_mx_quantize): E4M3 codes and tiled E8M0 scales. */
+typedef struct tb_mx_weight {
+  const void* codes;
+  const void* scales;
+} tb_mx_weight;
 
 /* A batch of clips, packed end to end at every stage (no padding between clips).
  * Offsets are cumulative row counts, [clips + 1], on the device; *_total are the
@@ -266,8 +275,13 @@ int tb_subsample(const tb_model* m, const tb_batch* batch, const float* feats, f
 
 /* ---- whole encoder: tinybark/tinygrad/model.py:140-158 (_encode),
  * tinybark/mojo/bark/gpu.mojo:399-426 (GpuEncoder.encode) ----
- * feats -> enc [t3_total, 640] fp32 (encoder frames projected for the joint). */
+ * feats -> enc [t3_total, 640] fp32 (encoder frames projected for the joint). With
+ * tb_model.ffn_mx set, each FFN's input and hidden activations are quantized to MXFP8
+ * (tb_mx_quantize) and both FFN GEMMs run block-scaled (tb_gemm_mx). */
 size_t tb_encoder_workspace_bytes(int dtype, int t2_total, int t3_total);
+/* The workspace of a bf16 model with block-scaled FFN weights (tb_model.ffn_mx set): the
+ * bf16 one plus the MXFP8 activations of the FFN GEMMs. */
+size_t tb_encoder_workspace_bytes_mx(int t2_total, int t3_total);
 int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* feats, float* enc, void* ws,
                        size_t ws_bytes, int* err, void* stream);
 

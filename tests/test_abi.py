@@ -55,6 +55,12 @@ def test_bad_arguments_are_rejected_without_touching_the_device():
     assert _lib.lib.tb_text_offsets(None, 8, None, -1, None, 10, 8, None, None) == 1
     assert _lib.lib.tb_text_offsets(8, 8, 8, 4, None, 10, 8, None, None) == 1
     assert _lib.lib.tb_text_bytes(8, 8, 8, 4, 8, None, 5, 10, 8, 8, 100, None) == 1
+    # block-scaled: K not a multiple of 512, N not a multiple of 128, a bad source dtype
+    assert _lib.lib.tb_gemm_mx(16, 16, 16, 16, 4, 128, 1000, ctypes.byref(ep), None, None) == 1
+    assert _lib.lib.tb_gemm_mx(16, 16, 16, 16, 4, 100, 1024, ctypes.byref(ep), None, None) == 1
+    assert _lib.lib.tb_mx_quantize(5, 16, 1024, 4, 1024, 16, 16, None) == 1
+    assert _lib.lib.tb_mx_scale_bytes(200, 1024) == 256 * 32
+    assert _lib.lib.tb_encoder_workspace_bytes_mx(100, 50) > _lib.lib.tb_encoder_workspace_bytes(_lib.BF16, 100, 50)
     with pytest.raises(RuntimeError, match="bad argument"):
         _lib.check(1, "tb_gemm")
 
@@ -64,7 +70,7 @@ def test_struct_layouts_match_the_header(tmp_path):
     from tinybark_b200 import _lib
 
     structs = {"tb_epilogue": _lib.Epilogue, "tb_layer": _lib.Layer, "tb_model": _lib.Model, "tb_batch": _lib.Batch,
-               "tb_repack_job": _lib.RepackJob}
+               "tb_repack_job": _lib.RepackJob, "tb_mx_weight": _lib.MXWeight}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')

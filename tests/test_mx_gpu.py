@@ -81,3 +81,40 @@ def test_mx_gemm_silu_and_residual_epilogues():
     assert np.abs(h.float().cpu().numpy() - silu).max() <= 1e-2 * np.abs(silu).max()
     want = res0.cpu().numpy() + 0.5 * ref
     assert np.abs(res.cpu().numpy() - want).max() <= 1e-5 * np.abs(want).max()
+
+
+def test_encoder_with_block_scaled_ffn():
+    """24 layers, bf16, the FFN GEMMs block-scaled (Engine ffn="mxfp8"), on 8 of the 30 s
+    clips of the batched workload: encoder output against the float32 oracle within
+    max-rel 0.1 (E4M3 keeps 3 mantissa bits: each FFN input and weight carries up to 2^-4
+    relative rounding, against 2^-8 in bf16), and the decoded tokens against the bf16
+    encoder's on all 8 clips, the agreement printed."""
+    from conftest import max_rel, state_dict
+    from oracle import encoder, frontend
+    from tinybark_b200 import synthetic, weights
+    from tinybark_b200.engine import Engine
+
+    clips = [synthetic.to_float(synthetic.clip(30.0, seed)) for seed in range(1, 9)]
+    sd = state_dict(24)
+    conv, cfg = weights.convert(sd, synthetic.config(24)), synthetic.config(24)
+    toks, encs = {}, {}
+    for ffn in ("bf16", "mxfp8"):
+        eng = Engine(conv, cfg, dtype="bf16", ffn=ffn)
+        plan = eng.plan([len(c) // 160 for c in clips])
+        s, o = eng.upload(clips)
+        enc = eng.encode(eng.features(s, o, plan), plan)
+        tokens, counts = eng.decode(enc, plan)
+        eng.check()
+        e, off = enc.cpu().numpy(), plan.t3_off.cpu().numpy()
+        encs[ffn] = [e[off[i] : off[i + 1]] for i in range(len(clips))]
+        t, c = tokens.cpu().numpy(), counts.cpu().numpy()
+        toks[ffn] = [t[i, : c[i]].tolist() for i in range(len(clips))]
+        del eng
+    errs = []
+    for i in (0, 5):
+        ref = encoder.encode(sd, frontend.features(clips[i]))
+        errs.append((max_rel(encs["bf16"][i], ref), max_rel(encs["mxfp8"][i], ref)))
+    same = sum(a == b for a, b in zip(toks["bf16"], toks["mxfp8"]))
+    print(f"mxfp8 FFN: encoder max-rel vs fp32 oracle {[round(e[1], 4) for e in errs]} "
+          f"(bf16 {[round(e[0], 4) for e in errs]}); tokens identical to bf16 on {same}/{len(clips)} clips")
+    assert max(e[1] for e in errs) < 0.1

@@ -128,5 +128,6 @@ class Bark:
 def load(device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None) -> Bark:
     """The cuda backend on this process's current GPU, bf16 by default ("fp32" for the
     fp32 parity path). `weights` is (tensors, config): tensors the path of a converted
-    fp16 cache file or a dict of the converted arrays; by default tinybark's own cache."""
-    return Bark(device, dtype=dtype, weights=weights, tokenizer=tokenizer)
+    fp16 cache file or a dict of the converted arrays; by default tinybark's own cache.
+    `ffn="mxfp8"` runs the FFN GEMMs on block-scaled FP8 weights (bf16 only)."""
+    return Bark(device, dtype=dtype, weights=weights, tokenizer=tokenizer, ffn=ffn)

@@ -51,8 +51,14 @@ class Model(C.Structure):
         ("embedding", vp), ("lstm_w", vp * 2), ("lstm_b", vp * 2), ("dec_proj_w", vp), ("dec_proj_b", vp),
         ("joint_w", vp), ("joint_b", vp),
         ("window", vp), ("mel_w", vp), ("mel_start", vp), ("mel_off", vp),
-        ("lstm0_hh", vp), ("lstm0_emb", vp),
+        ("lstm0_hh", vp), ("lstm0_emb", vp), ("ffn_mx", vp),
     ]
+
+
+class MXWeight(C.Structure):
+    """tb_mx_weight: one MXFP8 weight matrix (codes, tiled scales)."""
+
+    _fields_ = [("codes", vp), ("scales", vp)]
 
 
 class Batch(C.Structure):
@@ -105,6 +111,7 @@ def _load() -> C.CDLL:
         "tb_selftest_math": (i32, [i32, vp, vp, ll, vp]),
         "tb_decode_lane_iterations": (i32, [vp, i32, i32, i32, vp, vp]),
         "tb_mx_scale_bytes": (sz, [i32, i32]),
+        "tb_encoder_workspace_bytes_mx": (sz, [i32, i32]),
         "tb_mx_quantize": (i32, [i32, vp, ll, i32, i32, vp, vp, vp]),
         "tb_gemm_mx": (i32, [vp, vp, vp, vp, i32, i32, i32, P(Epilogue), vp, vp]),
         "tb_tdt_decode": (i32, [P(Model), vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp, vp, vp]),
@@ -126,7 +133,7 @@ EXPORTS = (
     "tb_frontend_static", "tb_frontend_pcm16",
     "tb_layernorm", "tb_gemm", "tb_set_gemm_pairs", "tb_relpos_attention", "tb_conv_depthwise", "tb_subsample_workspace_bytes",
     "tb_subsample", "tb_encoder_workspace_bytes", "tb_encoder_forward", "tb_decode_workspace_bytes", "tb_tdt_decode",
-    "tb_selftest_wait", "tb_selftest_math", "tb_decode_lane_iterations", "tb_mx_scale_bytes", "tb_mx_quantize",
+    "tb_selftest_wait", "tb_selftest_math", "tb_decode_lane_iterations", "tb_mx_scale_bytes", "tb_mx_quantize", "tb_encoder_workspace_bytes_mx",
     "tb_gemm_mx", "tb_repack", "tb_text_offsets", "tb_text_bytes",
 )
 

@@ -18,6 +18,11 @@ int frontend_pcm16(const tb_model& m, const int16_t* pcm, const long long* sampl
                    int clips, int frames_total, float* feats, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t decode_ws_groups(int dtype, int lanes, int groups);
 int selftest_wait(int kind, unsigned* scratch, int* err, cudaStream_t stream);
+size_t mx_scale_bytes(int rows, int k);
+int mx_quantize(int src_dtype, const void* src, long long ld, int rows, int k, uint8_t* codes, uint8_t* sf,
+                cudaStream_t stream);
+int gemm_mx(const uint8_t* a, const uint8_t* sfa, const uint8_t* w, const uint8_t* sfw, int m, int n, int k,
+            const tb_epilogue& e, int* err, cudaStream_t stream);
 int tdt_decode(const tb_model& m, const float* enc, const int* enc_off, const int* cap, int lanes, int max_cap,
                int groups, int* tokens, int* counts, void* ws, size_t ws_bytes, int* host_flag, int* err,
                cudaStream_t stream);
@@ -85,11 +90,12 @@ int sm_count() {
 struct EncWs {
   float* x;
   void *xn, *hid, *qu, *qv, *k, *v, *att, *glu, *dwo;
+  uint8_t *xq, *xs, *hq, *hs;  // block-scaled FFN: MXFP8 codes and scales of its two inputs
   void* sub;
   size_t sub_bytes;
 };
 
-static EncWs carve_encoder(void* ws, int dtype, int t2_total, int t3_total) {
+static EncWs carve_encoder(void* ws, int dtype, int t2_total, int t3_total, bool mx = false) {
   const size_t e = dsize(dtype), R = t3_total;
   uint8_t* p = reinterpret_cast<uint8_t*>(ws);
   auto take = [&](size_t bytes) {
@@ -108,14 +114,22 @@ static EncWs carve_encoder(void* ws, int dtype, int t2_total, int t3_total) {
   w.att = take(R * TB_HIDDEN * e);
   w.glu = take(R * TB_HIDDEN * e);
   w.dwo = take(R * TB_HIDDEN * e);
+  w.xq = w.xs = w.hq = w.hs = nullptr;
+  if (mx) {
+    const size_t pad = (R + 127) / 128 * 128;
+    w.xq = (uint8_t*)take(pad * TB_HIDDEN);
+    w.xs = (uint8_t*)take(mx_scale_bytes(t3_total, TB_HIDDEN));
+    w.hq = (uint8_t*)take(pad * TB_FFN);
+    w.hs = (uint8_t*)take(mx_scale_bytes(t3_total, TB_FFN));
+  }
   w.sub_bytes = subsample_ws(dtype, t2_total, t3_total);
   w.sub = take(w.sub_bytes);
   return w;
 }
 
-static size_t encoder_ws(int dtype, int t2_total, int t3_total) {
+static size_t encoder_ws(int dtype, int t2_total, int t3_total, bool mx = false) {
   uint8_t* base = nullptr;
-  EncWs w = carve_encoder(base, dtype, t2_total, t3_total);
+  EncWs w = carve_encoder(base, dtype, t2_total, t3_total, mx);
   return (size_t)(reinterpret_cast<uint8_t*>(w.sub) - base) + align256(w.sub_bytes);
 }
 
@@ -123,10 +137,12 @@ static int encoder_forward(const tb_model& m, const tb_batch& b, const float* fe
                            size_t ws_bytes, int* err, cudaStream_t s) {
   if (b.t3_total <= 0) return TB_OK;
   if (!m.layer || m.layers <= 0 || !feats || !enc || !ws) return TB_ERR_ARG;
-  if (ws_bytes < encoder_ws(m.dtype, b.t2_total, b.t3_total)) return TB_ERR_WORKSPACE;
+  const bool mx = m.ffn_mx != nullptr;
+  if (mx && m.dtype != TB_BF16) return TB_ERR_ARG;
+  if (ws_bytes < encoder_ws(m.dtype, b.t2_total, b.t3_total, mx)) return TB_ERR_WORKSPACE;
   if (b.max_t3 > m.max_len) return TB_ERR_ARG;
   const int dt = m.dtype, R = b.t3_total;
-  EncWs w = carve_encoder(ws, dt, b.t2_total, b.t3_total);
+  EncWs w = carve_encoder(ws, dt, b.t2_total, b.t3_total, mx);
 
   if (int rc = subsample(m, b, feats, w.x, w.sub, w.sub_bytes, err, s)) return rc;
 
@@ -156,13 +172,31 @@ static int encoder_forward(const tb_model& m, const tb_batch& b, const float* fe
   qkv.out4 = w.v;
   qkv.ldo = TB_HIDDEN;
 
+  // One macaron FFN: x += 0.5 * W2 silu(W1 xn), xn the normalised input in w.xn; block
+  // scaled when the model has MXFP8 FFN weights (j: 0 for the first FFN, 1 the second).
+  auto ffn = [&](int i, int j) -> int {
+    const tb_layer& L = m.layer[i];
+    if (!mx) {
+      if (int rc = gemm(dt, w.xn, TB_HIDDEN, j ? L.ff2_w1 : L.ff1_w1, R, TB_FFN, TB_HIDDEN, silu, err, s)) return rc;
+      return gemm(dt, w.hid, TB_FFN, j ? L.ff2_w2 : L.ff1_w2, R, TB_HIDDEN, TB_FFN, half, err, s);
+    }
+    const tb_mx_weight& w1 = m.ffn_mx[4 * i + 2 * j];
+    const tb_mx_weight& w2 = m.ffn_mx[4 * i + 2 * j + 1];
+    if (int rc = mx_quantize(TB_BF16, w.xn, TB_HIDDEN, R, TB_HIDDEN, w.xq, w.xs, s)) return rc;
+    if (int rc = gemm_mx(w.xq, w.xs, static_cast<const uint8_t*>(w1.codes), static_cast<const uint8_t*>(w1.scales),
+                         R, TB_FFN, TB_HIDDEN, silu, err, s))
+      return rc;
+    if (int rc = mx_quantize(TB_BF16, w.hid, TB_FFN, R, TB_FFN, w.hq, w.hs, s)) return rc;
+    return gemm_mx(w.hq, w.hs, static_cast<const uint8_t*>(w2.codes), static_cast<const uint8_t*>(w2.scales), R,
+                   TB_HIDDEN, TB_FFN, half, err, s);
+  };
+
   const tb_layer& first = m.layer[0];
   if (int rc = layernorm(w.x, first.norm_w[0], first.norm_b[0], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
   for (int i = 0; i < m.layers; ++i) {
     const tb_layer& L = m.layer[i];
     // x += 0.5 * FF1(LN(x))  (the LN was applied at the end of the previous layer)
-    if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.ff1_w1, R, TB_FFN, TB_HIDDEN, silu, err, s)) return rc;
-    if (int rc = gemm(dt, w.hid, TB_FFN, L.ff1_w2, R, TB_HIDDEN, TB_FFN, half, err, s)) return rc;
+    if (int rc = ffn(i, 0)) return rc;
     // x += MHSA(LN(x))
     if (int rc = layernorm(w.x, L.norm_w[1], L.norm_b[1], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
     qkv.bias_u = L.bias_u;
@@ -177,8 +211,7 @@ static int encoder_forward(const tb_model& m, const tb_batch& b, const float* fe
     if (int rc = gemm(dt, w.dwo, TB_HIDDEN, L.pw2, R, TB_HIDDEN, TB_HIDDEN, full, err, s)) return rc;
     // x += 0.5 * FF2(LN(x))
     if (int rc = layernorm(w.x, L.norm_w[3], L.norm_b[3], nullptr, nullptr, nullptr, w.xn, dt, R, s)) return rc;
-    if (int rc = gemm(dt, w.xn, TB_HIDDEN, L.ff2_w1, R, TB_FFN, TB_HIDDEN, silu, err, s)) return rc;
-    if (int rc = gemm(dt, w.hid, TB_FFN, L.ff2_w2, R, TB_HIDDEN, TB_FFN, half, err, s)) return rc;
+    if (int rc = ffn(i, 1)) return rc;
     // x = LN_out(x), fused with the next layer's first LN (or, after the last layer, the
     // projector's input cast).
     if (i + 1 < m.layers) {
@@ -304,6 +337,10 @@ int tb_subsample(const tb_model* m, const tb_batch* batch, const float* feats, f
 
 size_t tb_encoder_workspace_bytes(int dtype, int t2_total, int t3_total) {
   return encoder_ws(dtype, t2_total, t3_total);
+}
+
+size_t tb_encoder_workspace_bytes_mx(int t2_total, int t3_total) {
+  return encoder_ws(TB_BF16, t2_total, t3_total, true);
 }
 
 int tb_encoder_forward(const tb_model* m, const tb_batch* batch, const float* feats, float* enc, void* ws,

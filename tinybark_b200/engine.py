@@ -100,10 +100,14 @@ class Engine:
     """The model on one GPU. `tensors` is the converted layout (tinybark/weights.py:62-89):
     the path of tinybark's fp16 cache file of it (tinybark/weights.py:92-120), read
     straight into GPU memory, or a dict of float32 arrays; `dtype` is "fp32" (parity) or
-    "bf16" (throughput)."""
+    "bf16" (throughput). `ffn` "mxfp8" (bf16 only) runs the FFN GEMMs block-scaled: their
+    weights quantized to MXFP8 at load, their inputs at run time (a lower-precision option,
+    tinybark/docs/2026-10-24-learnings.md:133-146; "bf16", the default, keeps them bf16)."""
 
     def __init__(self, tensors: dict[str, np.ndarray], config: dict, dtype: str = "bf16", device="cuda",
-                 max_len: int = 512):
+                 max_len: int = 512, ffn: str = "bf16"):
+        if ffn not in ("bf16", "mxfp8") or (ffn == "mxfp8" and dtype != "bf16"):
+            raise ValueError(f"ffn must be 'bf16', or 'mxfp8' with dtype 'bf16' (got {ffn!r}, {dtype!r})")
         if not torch.cuda.is_available():
             raise RuntimeError("the cuda backend needs a CUDA GPU")
         self.device = torch.device(device)
@@ -124,6 +128,9 @@ class Engine:
             self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.host_flag = torch.zeros(2 * MAX_DECODE_GROUPS, dtype=torch.int32).pin_memory()
             self._pack(tensors)
+            self.ffn = ffn
+            if ffn == "mxfp8":
+                self._quantize_ffn()
             self.max_len = 0
             self.ensure_len(max_len)
 
@@ -208,6 +215,22 @@ class Engine:
         m.mel_off = _ptr(self._vec(mel_off, torch.int32))
         self.model = m
         self.load_seconds = {"upload": t1 - t0, "repack": t2 - t1}
+
+    def _quantize_ffn(self) -> None:
+        """The FFN weights of every layer to MXFP8 on the GPU (tb_mx_quantize of the packed
+        bf16 matrices), pointed at by tb_model.ffn_mx."""
+        from . import kernels
+
+        self._mx = []
+        arr = (L.MXWeight * (4 * self.layers))()
+        for i in range(self.layers):
+            for j, key in enumerate(("ff1_w1", "ff1_w2", "ff2_w1", "ff2_w2")):
+                q = kernels.MX(self.layout.tensor_of(self._blob, f"{i}.{key}"))
+                self._mx.append(q)
+                arr[4 * i + j].codes, arr[4 * i + j].scales = q.codes.data_ptr(), q.scales.data_ptr()
+        self._mx_arr = arr
+        self.model.ffn_mx = C.cast(arr, C.c_void_p)
+        torch.cuda.synchronize(self.device)
 
     def ensure_len(self, t3: int) -> None:
         """Projected position tables (pos @ relative_k_proj^T, one per layer) covering
@@ -294,7 +317,10 @@ class Engine:
         enc = torch.empty(b.t3_total, L.PRED, device=self.device, dtype=torch.float32) if out is None else out
         if enc.shape != (b.t3_total, L.PRED) or not enc.is_contiguous() or enc.dtype != torch.float32:
             raise ValueError("encode: out must be a contiguous float32 [t3_total, 640] tensor")
-        nbytes = L.lib.tb_encoder_workspace_bytes(self.dtype, b.t2_total, b.t3_total)
+        if self.ffn == "mxfp8":
+            nbytes = L.lib.tb_encoder_workspace_bytes_mx(b.t2_total, b.t3_total)
+        else:
+            nbytes = L.lib.tb_encoder_workspace_bytes(self.dtype, b.t2_total, b.t3_total)
         ws = torch.empty(nbytes, device=self.device, dtype=torch.uint8)
         L.check(L.lib.tb_encoder_forward(C.byref(self.model), C.byref(b), feats.data_ptr(), enc.data_ptr(),
                                          ws.data_ptr(), nbytes, self.err.data_ptr(), _stream(self.device)),
