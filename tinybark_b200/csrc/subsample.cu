@@ -120,30 +120,54 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
   }
 }
 
-// depthwise 2: s2 [T2][32][256] -> d2 [T3][16][256]; one block per (row, frequency).
+// depthwise 2: s2 [T2][32][256] -> d2 [T3][16][256]; one block of 256 threads per output
+// row t3: thread t takes channels 2 (t % 128) and 2 (t % 128) + 1 (one 4-byte access of
+// two bf16 or two-wide fp32 halves) and the 8 frequencies f3 of half t / 128, sweeping f3
+// upwards so each step reads two new input columns (f2 = 2 f3, 2 f3 + 1) and reuses the
+// last one (2 f3 - 1).
 template <typename T>
 __global__ void __launch_bounds__(256) dw2_kernel(const T* __restrict__ s2, const int* __restrict__ t2_off,
                                                   const int* __restrict__ t3_off, const int* __restrict__ t3_clip,
                                                   const float* __restrict__ w, const float* __restrict__ b,
                                                   T* __restrict__ d2) {
-  const int row = blockIdx.x / S_F3, f3 = blockIdx.x % S_F3, c = threadIdx.x;
+  const int row = blockIdx.x, c = 2 * (threadIdx.x & 127), half = threadIdx.x >> 7;
   const int clip = t3_clip[row];
   const int t3 = row - t3_off[clip];
   const int T2 = t2_off[clip + 1] - t2_off[clip];
   const long long base2 = t2_off[clip];
-  float acc = b[c];
+  float wa[9], wb[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) wa[i] = w[c * 9 + i], wb[i] = w[(c + 1) * 9 + i];
+  const float ba = b[c], bb = b[c + 1];
+  bool ok[3];
+  const T* in[3];
 #pragma unroll
   for (int dt = 0; dt < 3; ++dt) {
     const int t2 = 2 * t3 + dt - 1;
-    if (t2 < 0 || t2 >= T2) continue;
-#pragma unroll
-    for (int df = 0; df < 3; ++df) {
-      const int f2 = 2 * f3 + df - 1;
-      if (f2 < 0 || f2 >= S_F2) continue;
-      acc = fmaf(w[c * 9 + dt * 3 + df], to_f(s2[((base2 + t2) * S_F2 + f2) * TB_CHANNELS + c]), acc);
-    }
+    ok[dt] = t2 >= 0 && t2 < T2;
+    in[dt] = s2 + ((base2 + (ok[dt] ? t2 : 0)) * S_F2) * TB_CHANNELS + c;
   }
-  d2[((long long)row * S_F3 + f3) * TB_CHANNELS + c] = from_f<T>(acc);
+  auto load2 = [&](int dt, int f2) -> float2 {
+    if (!ok[dt] || f2 < 0) return make_float2(0.f, 0.f);
+    return load2f(in[dt] + f2 * TB_CHANNELS);
+  };
+  const int f3a = half * (S_F3 / 2);
+  float2 prev[3];  // column 2 f3 - 1
+#pragma unroll
+  for (int dt = 0; dt < 3; ++dt) prev[dt] = load2(dt, 2 * f3a - 1);
+#pragma unroll
+  for (int k = 0; k < S_F3 / 2; ++k) {
+    const int f3 = f3a + k;
+    float acc_a = ba, acc_b = bb;
+#pragma unroll
+    for (int dt = 0; dt < 3; ++dt) {
+      const float2 m = load2(dt, 2 * f3), r = load2(dt, 2 * f3 + 1);
+      acc_a = fmaf(wa[dt * 3], prev[dt].x, fmaf(wa[dt * 3 + 1], m.x, fmaf(wa[dt * 3 + 2], r.x, acc_a)));
+      acc_b = fmaf(wb[dt * 3], prev[dt].y, fmaf(wb[dt * 3 + 1], m.y, fmaf(wb[dt * 3 + 2], r.y, acc_b)));
+      prev[dt] = r;
+    }
+    store2(d2 + ((long long)row * S_F3 + f3) * TB_CHANNELS + c, acc_a, acc_b);
+  }
 }
 
 int subsample_tile_rows() { return S_T2; }
@@ -189,11 +213,11 @@ int subsample(const tb_model& m, const tb_batch& bt, const float* feats, float* 
     return rc;
 
   if (m.dtype == TB_BF16)
-    dw2_kernel<__nv_bfloat16><<<bt.t3_total * S_F3, 256, 0, stream>>>(
+    dw2_kernel<__nv_bfloat16><<<bt.t3_total, 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(s2), bt.t2_off, bt.t3_off, bt.t3_clip, m.sub_dw_w[1], m.sub_dw_b[1],
         reinterpret_cast<__nv_bfloat16*>(d2));
   else
-    dw2_kernel<float><<<bt.t3_total * S_F3, 256, 0, stream>>>(reinterpret_cast<const float*>(s2), bt.t2_off, bt.t3_off,
+    dw2_kernel<float><<<bt.t3_total, 256, 0, stream>>>(reinterpret_cast<const float*>(s2), bt.t2_off, bt.t3_off,
                                                               bt.t3_clip, m.sub_dw_w[1], m.sub_dw_b[1],
                                                               reinterpret_cast<float*>(d2));
   if (int rc = check_launch()) return rc;
