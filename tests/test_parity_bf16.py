@@ -10,9 +10,10 @@
   different token only where two logits are nearly tied, so each clip's tokens must
   equal the oracle's up to the oracle's first iteration whose top-2 token or duration
   margin is below MARGIN (all of them if none is), and most clips must match whole.
-  Run on the synthetic weights (every clip repeats one token until the cap) and on the
-  same weights with the joint biases of the 'mixed' decode case (blanks and durations
-  1-4, so the frame moves).
+  Run on the synthetic weights with the GPU encoder's frames (with random-init weights
+  the encoder's frames of a clip are nearly alike, and each clip repeats one token at one
+  duration), and, so that blanks, durations 1-4 and several tokens occur, with the joint
+  biases of the 'mixed' decode case on seeded N(0, 4) frames of the same lengths.
 """
 
 import numpy as np
@@ -80,6 +81,8 @@ def test_persistent_decoder_matches_oracle(workload, weights_case):
         bias = sd["joint.head.bias"].copy()
         bias[synthetic.BLANK] += case["blank"]
         sd["joint.head.bias"] = bias
+        rng = np.random.default_rng(case["seed"])
+        enc = [(rng.standard_normal(e.shape) * case["scale"]).astype(np.float32) for e in enc]
     eng = Engine(weights.convert(sd, synthetic.config(2)), synthetic.config(2), dtype="bf16")
     plan = eng.plan(frames)
     tokens, counts = eng.decode(torch.from_numpy(np.concatenate(enc)).cuda(), plan)

@@ -366,6 +366,9 @@ int gemm_mx(const uint8_t* a, const uint8_t* sfa, const uint8_t* w, const uint8_
       (reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfw) & 15))
     return TB_ERR_ARG;
   if (e.rows) return TB_ERR_UNSUPPORTED;
+  // The scale-factor copy into tensor memory is being replaced (tcgen05.cp with this
+  // descriptor raised a misaligned-address fault); nothing launches until then.
+  if (k > 0) return TB_ERR_UNSUPPORTED;
   switch (e.kind) {
     case TB_EPI_STORE: return launch_mx<TB_EPI_STORE>(a, sfa, w, sfw, m, n, k, e, err, stream);
     case TB_EPI_SILU: return launch_mx<TB_EPI_SILU>(a, sfa, w, sfw, m, n, k, e, err, stream);

@@ -3,12 +3,16 @@ the clips end to end (front-end, encoder, TDT decode), with no collective on the
 path. Clips are independent units: nothing in the greedy loop
 (tinybark/tinygrad/model.py:196-233) reads another clip.
 
-`deal` splits a clip list into balanced shards: clips by predicted cost, longest first,
-each to the shard with the least predicted cost so far (longest processing time first;
-tinybark sorts clips into 256-frame length buckets, tinybark/tinygrad/model.py:15-20,
-and this build packs clips without padding, so the deal works on exact lengths). Taking
-the longest clips first also gives every shard one of the longest clips, so the shards'
-greedy loops, whose length is set by their longest clip, end together.
+`deal` splits a clip list into shards of equal predicted time: the clips sorted by length
+(tinybark sorts clips into 256-frame length buckets, tinybark/tinygrad/model.py:15-20;
+this build packs clips without padding, so the deal works on exact lengths) and cut into
+contiguous ranges, the cuts placed so that the largest predicted shard time is as small
+as it can be. A shard's time is not a sum over its clips: the encoder's is (FLOPs), but
+the greedy loop runs all of a shard's lanes together for as many iterations as its
+longest clip needs, each iteration costing a fixed latency plus a little per lane. So a
+shard of only short clips ends its loop early and can take more clips, and contiguous
+length ranges beat dealing every shard the same mix of lengths (`deal_lpt`, longest
+processing time first on additive costs), which gives every shard a full-length loop.
 
 `MultiGPU` runs the shards: one spawned process per GPU (pinned with
 CUDA_VISIBLE_DEVICES, as tinybark's benchmark isolates each backend in a process of its
@@ -36,6 +40,39 @@ ATTN_FLOP_PER_FRAME2 = 6 * 1024 * 24
 DEC_FLOP_PER_ITER = 24.6e6
 
 
+# Predicted seconds on one B200, bf16: the encoder (and front-end) per FLOP of
+# clip_encoder_flop, and one greedy-loop iteration of the persistent decoder per running
+# lane count (a latency floor plus a per-lane term).
+ENC_S_PER_FLOP = 1.0 / 1.0e15
+ITER_S = 31e-6
+ITER_S_PER_LANE = 4e-9
+
+
+def clip_encoder_flop(frames: int) -> float:
+    t = lengths.subsampled(frames, 3)
+    return ENC_FLOP_PER_FRAME * t + ATTN_FLOP_PER_FRAME2 * t * t
+
+
+def predicted_seconds(frames: Sequence[int]) -> float:
+    """Predicted time of one GPU transcribing these clips as one batch: encoder work, then
+    the greedy loop, iteration by iteration at the latency of the lanes still running."""
+    f = np.asarray(frames, np.int64)
+    if f.size == 0:
+        return 0.0
+    t = f
+    for _ in range(3):
+        t = (t - 1) // 2 + 1  # encoder frames (lengths.subsampled)
+    enc = float(np.sum(ENC_FLOP_PER_FRAME * t + ATTN_FLOP_PER_FRAME2 * t.astype(np.float64) ** 2)) * ENC_S_PER_FLOP
+    u = f + 1
+    for _ in range(3):
+        u = (u - 1) // 2 + 1
+    caps = np.sort(lengths.MAX_SYMBOLS * u - 1)[::-1]  # lengths.decode_cap, longest first
+    # The k longest lanes run for iterations caps[k] .. caps[k - 1].
+    lanes = np.arange(1, len(caps) + 1)
+    steps = caps - np.append(caps[1:], 0)
+    return enc + float(np.sum(steps * (ITER_S + ITER_S_PER_LANE * lanes)))
+
+
 def clip_cost(frames: int) -> float:
     """Predicted FLOPs of one clip of `frames` feature frames through the whole path."""
     t = lengths.subsampled(frames, 3)
@@ -43,10 +80,56 @@ def clip_cost(frames: int) -> float:
 
 
 def deal(frames: Sequence[int], parts: int) -> list[list[int]]:
-    """Indices of the clips (feature-frame counts `frames`) in each of `parts` shards,
-    longest processing time first: clips in decreasing predicted cost (ties by index),
-    each to the shard of least cost so far (ties to the lowest shard). Deterministic, so
-    every rank computes the same deal; each shard lists its clips in dealing order."""
+    """Indices of the clips (feature-frame counts `frames`) in each of `parts` shards:
+    contiguous ranges of the clips in decreasing length (ties by index), the first shard
+    the longest clips, cut so that the largest `predicted_seconds` of a shard is the
+    smallest the cuts allow (a bisection on that time; each shard takes as many clips as
+    fit under it). Deterministic, so every rank computes the same deal."""
+    if parts < 1:
+        raise ValueError("parts must be at least 1")
+    order = sorted(range(len(frames)), key=lambda i: (-int(frames[i]), i))
+    f = [int(frames[i]) for i in order]
+    if not f:
+        return [[] for _ in range(parts)]
+
+    def cuts(limit: float) -> list[int] | None:
+        """Shard ends filling each shard up to `limit`, or None if `parts` do not suffice."""
+        ends, start = [], 0
+        for _ in range(parts):
+            if start == len(f):
+                break
+            lo, hi = start + 1, len(f)  # the largest end with the shard's time <= limit
+            if predicted_seconds(f[start:lo]) > limit:
+                return None
+            while lo < hi:
+                mid = (lo + hi + 1) // 2
+                if predicted_seconds(f[start:mid]) <= limit:
+                    lo = mid
+                else:
+                    hi = mid - 1
+            ends.append(lo)
+            start = lo
+        return ends if start == len(f) else None
+
+    lo, hi = max(predicted_seconds([x]) for x in f), predicted_seconds(f)
+    for _ in range(40):
+        mid = (lo + hi) / 2
+        if cuts(mid) is None:
+            lo = mid
+        else:
+            hi = mid
+    ends = cuts(hi)
+    shards, start = [], 0
+    for e in ends:
+        shards.append(order[start:e])
+        start = e
+    return shards + [[] for _ in range(parts - len(shards))]
+
+
+def deal_lpt(frames: Sequence[int], parts: int) -> list[list[int]]:
+    """Longest processing time first on additive costs (clip_cost): clips in decreasing
+    cost (ties by index), each to the shard of least cost so far (ties to the lowest
+    shard). Every shard gets the same mix of lengths; kept to compare with `deal`."""
     if parts < 1:
         raise ValueError("parts must be at least 1")
     order = sorted(range(len(frames)), key=lambda i: (-clip_cost(int(frames[i])), i))
