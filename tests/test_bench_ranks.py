@@ -66,9 +66,14 @@ def test_two_gloo_ranks_shard_and_reduce():
         assert p.exitcode == 0
     assert [g["rank"] for g in got] == [0, 1] and all(g["world"] == 2 for g in got)
     # Every clip of the set on exactly one rank; shards longest first, 2-30 s of 16 kHz
-    # audio, balanced in length.
+    # audio, balanced in predicted time to within one clip (the longest clips on rank 0).
+    from tinybark_b200 import dp, lengths
+
     assert all(h == 1 for h in got[0]["holders"]) and got[0]["holders"] == got[1]["holders"]
-    assert abs(sum(got[0]["durs"]) - sum(got[1]["durs"])) < 0.1 * sum(got[0]["durs"])
+    frames = [[lengths.frames(n) for n in g["lens"]] for g in got]
+    times = [dp.predicted_seconds(f) for f in frames]
+    assert abs(times[0] - times[1]) <= max(dp.predicted_seconds([x]) for f in frames for x in f)
+    assert min(frames[0]) >= max(frames[1])
     for g in got:
         assert g["durs"] == sorted(g["durs"], reverse=True)
         assert all(2.0 <= d < 30.0 for d in g["durs"])
