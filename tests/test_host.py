@@ -148,6 +148,16 @@ def test_registry_has_cuda_backend():
     assert "gpu" in b.descriptions and b.env("gpu") == {}
 
 
+def test_public_entry_points_take_the_ffn_option():
+    import inspect
+
+    import tinybark_b200
+    from tinybark_b200.engine import Engine
+
+    for fn in (tinybark_b200.load, tinybark_b200.Bark.__init__, Engine.__init__):
+        assert inspect.signature(fn).parameters["ffn"].default == "bf16"
+
+
 def test_cpu_device_is_refused():
     import tinybark_b200
 

@@ -50,7 +50,7 @@ def converted_weights(path: str | Path | None = None) -> tuple[dict[str, np.ndar
 
 class Bark:
     def __init__(self, device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None,
-                 max_seconds: float = 30.0):
+                 max_seconds: float = 30.0, ffn: str = "bf16"):
         if device != "gpu":
             raise RuntimeError(f"the cuda backend runs on the gpu, not {device!r}")
         import torch
@@ -61,7 +61,7 @@ class Bark:
         # The cache file goes to the GPU as it is and is repacked there.
         tensors, config = weights if weights is not None else converted()
         max_len = lengths.subsampled(int(max_seconds * 100), 3)
-        self.engine = Engine(tensors, config, dtype=dtype, device="cuda", max_len=max_len)
+        self.engine = Engine(tensors, config, dtype=dtype, device="cuda", max_len=max_len, ffn=ffn)
         self.device = torch.cuda.get_device_name(self.engine.device)
         self._tokenizer_path = tokenizer
         self._tokenizer = None
@@ -125,7 +125,8 @@ class Bark:
         self.engine = None
 
 
-def load(device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None) -> Bark:
+def load(device: str = "gpu", dtype: str = "bf16", weights=None, tokenizer: str | None = None,
+         ffn: str = "bf16") -> Bark:
     """The cuda backend on this process's current GPU, bf16 by default ("fp32" for the
     fp32 parity path). `weights` is (tensors, config): tensors the path of a converted
     fp16 cache file or a dict of the converted arrays; by default tinybark's own cache.

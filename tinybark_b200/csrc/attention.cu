@@ -146,19 +146,17 @@ __global__ void __launch_bounds__(256) relpos_attention_simt(const T* __restrict
 // ---------------------------------------------------------------------------
 // tcgen05 form (bf16): one CTA per (clip, head, 128 queries), key tiles of 64.
 //
-// Warp 0 loads tiles with TMA, warp 1 issues the MMAs, warps 2-9 run the softmax: two
-// warps per tensor-memory lane quarter (32 query rows, one row per thread), each taking
-// half of a key tile's 64 columns and half of O's, with the row maximum and, at the end of
-// an item, the row sum exchanged through shared memory. Per key tile, into tensor memory:
+// Warp 0 loads tiles with TMA, warp 1 issues the MMAs, warps 2-5 (one query row per
+// thread) run the softmax. Per key tile, into tensor memory:
 //   S  = Qu K^T          (128 x 64)
 //   BD = Qu R_band^T     (128 x 192), R_band the 192 table rows the tile's relative
 //                        positions span (191 used)
 // The positional term of the reference, (q + bias_v) . r, is computed as
 // (q + bias_u) . r + (bias_v - bias_u) . r: the second product depends only on the
 // head and the relative position and comes precomputed per layer (rel_c), so Qu is the
-// only query operand. Each softmax warp copies the 64 BD columns its 32 rows and 32 keys
-// need into shared memory and reads its row's window shifted by its row index (the
-// relative shift). P (bf16) is written back into the tensor memory of S and the PV MMA reads
+// only query operand. Each softmax warp copies the 96 BD columns its 32 rows need into
+// shared memory and reads its row's window shifted by its row index (the relative
+// shift). P (bf16) is written back into the tensor memory of S and the PV MMA reads
 // it from there; V is an MN-major operand straight from the [frames, 1024] V tensor.
 // O accumulates in tensor memory, rescaled by the softmax threads when the row max
 // grows.
@@ -167,12 +165,10 @@ namespace att {
 constexpr int TQ = 128, TK = 64, D = 128, BAND = 192;
 constexpr int Q_BYTES = TQ * D * 2, K_BYTES = TK * D * 2, R_BYTES = BAND * D * 2, V_BYTES = TK * D * 2;
 constexpr int Q_SUB = TQ * 128, K_SUB = TK * 128, R_SUB = BAND * 128, V_SUB = TK * 128;  // 64-column halves
-constexpr int SOFT_WARPS = 8, THREADS = 32 * (2 + SOFT_WARPS);
-constexpr int ST_STRIDE = 68, WIN = 64;  // a softmax warp's BD window: 64 columns (+4 pad) per row
-constexpr int ST_BYTES = SOFT_WARPS * 32 * ST_STRIDE * 4, C_BYTES = SOFT_WARPS * WIN * 4;
-constexpr int X_BYTES = 3 * SOFT_WARPS * 32 * 4;  // row maxima (two buffers by tile parity), row sums
+constexpr int ST_STRIDE = 100, WIN = 96;
+constexpr int ST_BYTES = 4 * 32 * ST_STRIDE * 4, C_BYTES = 4 * WIN * 4;
 constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_R = OFF_K + K_BYTES, OFF_V = OFF_R + R_BYTES,
-              OFF_ST = OFF_V + V_BYTES, OFF_C = OFF_ST + ST_BYTES, OFF_X = OFF_C + C_BYTES, OFF_BAR = OFF_X + X_BYTES;
+              OFF_ST = OFF_V + V_BYTES, OFF_C = OFF_ST + ST_BYTES, OFF_BAR = OFF_C + C_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
 constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, COL_P = 384, TMEM_COLS = 512;
 // log2(e) / sqrt(128): scores are kept in the base-2 exponent domain.
@@ -180,7 +176,6 @@ constexpr float SCALE_LOG2 = 0.12751743074f;
 
 struct Bars {
   uint64_t q_full, q_empty, kr_full, kr_empty, v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, o_empty, done;
-  uint64_t pair[4];  // the two softmax warps of lane quarter q exchange through pair[q]
   uint32_t tmem;
   int abort;
 };
@@ -205,7 +200,7 @@ __device__ __forceinline__ bool att_warp_wait(uint64_t* bar, uint32_t parity, in
 // current item's last softmax and its output; q_empty (the item's last S and BD products
 // have read Q) and o_empty (the softmax warps have read the finished O) hand Q's buffer
 // and O's columns to the next item.
-__global__ void __launch_bounds__(att::THREADS, 1)
+__global__ void __launch_bounds__(192, 1)
     relpos_attention_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tr,
                         const float* __restrict__ rel_c, int max_len, const int* __restrict__ t3_off,
@@ -241,12 +236,11 @@ __global__ void __launch_bounds__(att::THREADS, 1)
     mbar_init(&bars->v_full, 1);
     mbar_init(&bars->v_empty, 1);
     mbar_init(&bars->sbd_full, 1);
-    mbar_init(&bars->sbd_empty, SOFT_WARPS);
-    mbar_init(&bars->p_full, SOFT_WARPS);
+    mbar_init(&bars->sbd_empty, 4);
+    mbar_init(&bars->p_full, 4);
     mbar_init(&bars->o_done, 1);
-    mbar_init(&bars->o_empty, SOFT_WARPS);
+    mbar_init(&bars->o_empty, 4);
     mbar_init(&bars->done, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&bars->pair[i], 2);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -376,29 +370,13 @@ __global__ void __launch_bounds__(att::THREADS, 1)
       att_drain(&bars->done, 0);
     }
   } else {
-    const int q = warp & 3;         // tensor-memory lane quarter: query rows 32q .. 32q+31
-    const int h = (warp - 2) >> 2;  // which half of the key tile (and of O's columns)
-    const int sw = q * 2 + h;       // this warp's index among the softmax warps
+    const int q = warp & 3;  // tensor-memory lane quarter: query rows 32q .. 32q+31
     const int il = q * 32 + lane;
-    float* stage = reinterpret_cast<float*>(smem + OFF_ST) + sw * 32 * ST_STRIDE;
-    float* cband = reinterpret_cast<float*>(smem + OFF_C) + sw * WIN;
-    float* xmax = reinterpret_cast<float*>(smem + OFF_X);  // [2][SOFT_WARPS][32]
-    float* xsum = xmax + 2 * SOFT_WARPS * 32;               // [SOFT_WARPS][32]
-    const int partner = q * 2 + (h ^ 1);
+    float* stage = reinterpret_cast<float*>(smem + OFF_ST) + q * 32 * ST_STRIDE;
+    float* cband = reinterpret_cast<float*>(smem + OFF_C) + q * WIN;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
-    // First BD column of this warp's window: its rows' windows over the whole tile start
-    // at 96 - 32q; its 32 keys are the half h of them.
-    const int wcol = 96 - 32 * q + 32 * h;
+    const int wcol = 96 - 32 * q;  // first BD column this warp's rows need
     const int rel_rows = 2 * max_len - 1;
-    // The two warps of a quarter meet on mbarrier pair[q] (one arrival each, after the
-    // warp's shared-memory writes; a bounded wait, so a partner that gave up cannot hang
-    // this warp). False if the wait gave up.
-    uint32_t pair_uses = 0;
-    auto pair_sync = [&]() -> bool {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->pair[q]);
-      return att_warp_wait(&bars->pair[q], pair_uses++ & 1, err, abort);
-    };
     bool ok = true;
     uint32_t r[32];
     int g = 0;  // key tiles this CTA has done
@@ -418,7 +396,7 @@ __global__ void __launch_bounds__(att::THREADS, 1)
       };
       load_cband(0);
       for (int j = 0; j < it.nk; ++j, ++g) {
-        const int k0 = j * TK + 32 * h;  // this warp's first key
+        const int k0 = j * TK;
         __syncwarp();  // every lane is done with the previous tile's cband
 #pragma unroll
         for (int u = 0; u < WIN / 32; ++u) cband[u * 32 + lane] = cnext[u];
@@ -429,13 +407,17 @@ __global__ void __launch_bounds__(att::THREADS, 1)
           break;
         }
         tc_fence_after();
-        float sc[32];
-        tmem_ld32(tl + COL_S + 32 * h, r);
+        float sc[TK];
+        tmem_ld32(tl + COL_S, r);
         tmem_wait_ld();
 #pragma unroll
         for (int k = 0; k < 32; ++k) sc[k] = __uint_as_float(r[k]);
+        tmem_ld32(tl + COL_S + 32, r);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(r[k]);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
           tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
           tmem_wait_ld();
           float4* dst = reinterpret_cast<float4*>(stage + lane * ST_STRIDE + 32 * c);
@@ -452,23 +434,14 @@ __global__ void __launch_bounds__(att::THREADS, 1)
         const float* crow = cband + (31 - lane);
         float mx = -INFINITY;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
+        for (int jj = 0; jj < TK; ++jj) {
           const float v = (sc[jj] + srow[jj] + crow[jj]) * SCALE_LOG2;
           sc[jj] = k0 + jj < it.T ? v : -INFINITY;
           mx = fmaxf(mx, sc[jj]);
         }
-        // The row's maximum over the whole tile: this half's and the partner warp's.
-        float* xm = xmax + ((g & 1) * SOFT_WARPS) * 32;
-        xm[sw * 32 + lane] = mx;
-        if (!pair_sync()) {
-          ok = false;
-          break;
-        }
-        mx = fmaxf(mx, xm[partner * 32 + lane]);
         // The running max moves only when the row max grows by more than 8 (a factor 256 in
         // the exponentials, which bf16 P and the fp32 sums hold exactly): O is rescaled far
-        // less often, and the final O / l is the same for any reference max. Both warps of
-        // the quarter see the same maxima, so they move it alike.
+        // less often, and the final O / l is the same for any reference max.
         float corr = 1.0f;
         if (mx > m_run + 8.0f) {
           corr = exp2f(m_run - mx);
@@ -477,13 +450,13 @@ __global__ void __launch_bounds__(att::THREADS, 1)
         const float m_new = m_run;
         float sum = 0.f;
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
+        for (int jj = 0; jj < TK; jj += 2) {
           const float p0 = exp2f(sc[jj] - m_new), p1 = exp2f(sc[jj + 1] - m_new);
           sum += p0 + p1;
           __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
           r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
         }
-        l_run = l_run * corr + sum;  // this half's share of the row sum
+        l_run = l_run * corr + sum;
         if (j > 0) {
           if (!att_warp_wait(&bars->o_done, (g - 1) & 1, err, abort)) {
             ok = false;
@@ -493,17 +466,16 @@ __global__ void __launch_bounds__(att::THREADS, 1)
           if (__any_sync(0xffffffffu, corr != 1.0f)) {
             uint32_t o[32];
 #pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-              const uint32_t col = tl + COL_O + 64 * h + 32 * c;
-              tmem_ld32(col, o);
+            for (int c = 0; c < 4; ++c) {
+              tmem_ld32(tl + COL_O + 32 * c, o);
               tmem_wait_ld();
 #pragma unroll
               for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * corr);
-              tmem_st32(col, o);
+              tmem_st32(tl + COL_O + 32 * c, o);
             }
           }
         }
-        tmem_st16(tl + COL_P + 16 * h, r);
+        tmem_st32(tl + COL_P, r);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -514,18 +486,12 @@ __global__ void __launch_bounds__(att::THREADS, 1)
         break;
       }
       tc_fence_after();
-      // The row sum: both halves' shares.
-      xsum[sw * 32 + lane] = l_run;
-      if (!pair_sync()) {
-        ok = false;
-        break;
-      }
-      const float inv = 1.0f / (l_run + xsum[partner * 32 + lane]);
+      const float inv = 1.0f / l_run;
       const bool valid = it.q0 + il < it.T;
-      __nv_bfloat16* dst = out + (long long)(it.base + it.q0 + il) * TB_HIDDEN + it.col0 + 64 * h;
+      __nv_bfloat16* dst = out + (long long)(it.base + it.q0 + il) * TB_HIDDEN + it.col0;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        tmem_ld32(tl + COL_O + 64 * h + 32 * c, r);
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(tl + COL_O + 32 * c, r);
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
@@ -537,8 +503,6 @@ __global__ void __launch_bounds__(att::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->o_empty);  // O's columns are free for the next item
-      // The partner reads this item's row sums before its next pair_sync, which comes
-      // before this warp writes them again (every item has at least one key tile).
     }
   }
 
@@ -570,7 +534,7 @@ static int launch_attn_tc(const void* qu, const void* k, const void* v, const vo
     return TB_ERR_CUDA;
   const int items = b.n_attn_tiles * TB_HEADS;
   const int grid = items < sm_budget() ? items : sm_budget();
-  return launch_pdl(relpos_attention_tc, grid, att::THREADS, att::SMEM, stream, mq, mk, mv, mr, rel_c, max_len, b.t3_off,
+  return launch_pdl(relpos_attention_tc, grid, 192, att::SMEM, stream, mq, mk, mv, mr, rel_c, max_len, b.t3_off,
                     b.attn_tiles, items, reinterpret_cast<__nv_bfloat16*>(out), err);
 }
 

@@ -9,18 +9,19 @@
 // binade is 2^8), clamped to [-127, 127], -127 for an all-zero block; codes = E4M3 of
 // x * 2^-e, rounded to nearest even and saturated to +-448.
 //
-// Scales are kept in the layout the MMA reads them from after one tcgen05.cp per 512
-// values of K: [rows / 128][K / 512][128 rows][16 bytes], byte j of a row's 16 the scale of
-// its 32-value block j of that 512. In tensor memory that is 4 columns per 128 rows:
-// column c holds k-block c (128 values: four MMAs of K = 32), byte b of it the scale of
-// the MMA b of that k-block, selected by the instruction descriptor's scale-factor ids.
+// Scales are stored tiled, one chunk per 128 rows and 512 values of K:
+// [rows / 128][K / 512][128 rows][16 bytes], byte j of a row's 16 the scale of its 32-value
+// block j of that 512 (k-block j / 4, MMA j % 4). In tensor memory a chunk takes 4 columns
+// for A and 4 for W per k-block (the layout at sf_store), byte b of a cell the scale of MMA
+// b, selected by the instruction descriptor's scale-factor ids.
 //
 // mx_gemm_kernel: the persistent warp-specialized layout of the bf16 GEMM (gemm.cu) with
 // 128 x 128 tiles and k-blocks of 128 E4M3 values (one 128-byte swizzled row per tile
 // row): warp 0 loads A and W tiles with TMA and, once per 512 values of K, both tiles'
-// 2 KB scale chunks with bulk copies; warp 1 copies each scale chunk into tensor memory
-// (tcgen05.cp, two buffers) and issues kind::mxf8f6f4 block-scaled MMAs into one of two
-// accumulators; warps 2-5 drain the other accumulator through the epilogue.
+// 2 KB scale chunks with bulk copies; warps 6-9 write each chunk into one of two
+// tensor-memory scale buffers (tcgen05.st, each warp its lane quarter); warp 1 issues
+// kind::mxf8f6f4 block-scaled MMAs into one of two accumulators; warps 2-5 drain the
+// other accumulator through the epilogue.
 #include <cuda_fp8.h>
 
 #include "host.h"
@@ -32,6 +33,8 @@ namespace {
 
 struct MxCfg {
   static constexpr int BM = 128, BN = 128, BK = 128, STAGES = 6;
+  static constexpr int THREADS = 32 * 10;  // producer, MMA, 4 epilogue warps, 4 SF warps
+  static constexpr uint32_t SF_COLS = 32;  // a scale buffer: 16 columns for A, then 16 for W
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SF_BYTES = 128 * 16;  // one 128-row x 512-value scale chunk
   static constexpr int SF_SLOTS = 2;
@@ -44,16 +47,10 @@ struct MxCfg {
 
 struct MxBars {
   TcBars tc;
-  uint64_t sf_full[2], sf_empty[2];
+  uint64_t sf_full[2], sf_empty[2];  // a group's scale chunks in shared memory
+  uint64_t st_full[2], st_empty[2];  // a group's scales in a tensor-memory buffer
 };
 static_assert(sizeof(MxBars) <= 256, "mx barriers");
-
-// Shared-memory descriptor of a 128-row x 16-byte matrix with no swizzling (rows 16
-// bytes apart: 8-row core matrices of 128 bytes, one core matrix wide).
-__device__ __forceinline__ uint64_t sdesc_rows16(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) |
-         ((uint64_t)1 << 46);
-}
 
 // Instruction descriptor of kind::mxf8f6f4 with block scaling: E4M3 A and B (K-major),
 // E8M0 scales, f32 accumulator of 128 x n; the scale-factor ids (which byte of the scale
@@ -70,10 +67,6 @@ __device__ __forceinline__ void umma_mx(uint32_t d, uint64_t a, uint64_t b, uint
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}\n" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(sfa), "r"(sfb), "r"(acc)
       : "memory");
-}
-
-__device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // One-dimensional bulk copy global -> shared (16-byte aligned, size a multiple of 16),
@@ -138,8 +131,53 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const T* __restrict__ 
   sf[(((long long)(r >> 7) * groups + (j >> 4)) * 128 + (r & 127)) * 16 + (j & 15)] = (uint8_t)(e + 127);
 }
 
+// Where a block-scaled MMA (M = 128, N = 128) reads its E8M0 scales in tensor memory, as
+// measured on the B200 with one-MMA experiments (each scale cell holding a distinct value,
+// in-bounds addresses only): for scale-buffer column `col` and scale-factor id k (the
+// byte of a cell), row m of A reads (lane m, column col + m / 32, byte k), and column n of
+// W reads (lane n % 32 + 32 * (m / 32), column col + n / 32, byte k) for output row m: every
+// lane quarter needs its own copy of W's scales. So a k-block of 128 values (four MMAs,
+// k = 0..3) takes 4 columns for A and 4 for W, lane r + 32 q of column col + g holding the
+// 4 scales of row r + 32 g (the copies in other quarters are read only for W).
+//
+// sf_store: SF warp q writes its lanes' cells for one 512-value group (4 k-blocks: 16
+// columns for A at col_a, 16 for W at col_w) from the group's shared-memory chunks
+// ([128 rows][16 bytes], bytes 4 kb .. 4 kb + 3 of a row the scales of k-block kb).
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void sf_store(const uint8_t* chunk_a, const uint8_t* chunk_w, uint32_t tmem_quarter,
+                                         uint32_t col_a, uint32_t col_w, int q, int lane) {
+  uint32_t v[16];
+  // A: lane 32 q + r's own row; column col_a + 4 kb + q is the one read, the others of
+  // the k-block's four get the same word.
+  const uint4 a = *reinterpret_cast<const uint4*>(chunk_a + (q * 32 + lane) * 16);
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = aw[i / 4];
+  tmem_st_x16(tmem_quarter + col_a, v);
+  // W: column col_w + 4 kb + g holds row r + 32 g, in every quarter.
+  uint4 w[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) w[g] = *reinterpret_cast<const uint4*>(chunk_w + (lane + 32 * g) * 16);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    v[0 + g] = w[g].x;
+    v[4 + g] = w[g].y;
+    v[8 + g] = w[g].z;
+    v[12 + g] = w[g].w;
+  }
+  tmem_st_x16(tmem_quarter + col_w, v);
+}
+
 template <int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(MxCfg::THREADS, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
                    const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfw, int M, int N, int K,
                    const tb_epilogue e, int* err) {
@@ -161,7 +199,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&bars->tfull[a], 1);
       mbar_init(&bars->tempty[a], 4);
       mbar_init(&mb->sf_full[a], 1);
-      mbar_init(&mb->sf_empty[a], 1);
+      mbar_init(&mb->sf_empty[a], 4);
+      mbar_init(&mb->st_full[a], 4);
+      mbar_init(&mb->st_empty[a], 1);
     }
     mbar_init(&bars->done, 1);
     bars->abort = 0;
@@ -230,8 +270,8 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int s = 0, acc = 0, f = 0;
-      uint32_t ph = 0, acc_ph = 0, fph = 0;
+      int s = 0, acc = 0, b = 0;
+      uint32_t ph = 0, acc_ph = 0, bph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         if (!mbar_wait(&bars->tempty[acc], acc_ph ^ 1, err, TB_DEV_GEMM_TIMEOUT, abort)) break;
@@ -240,20 +280,13 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t sf_col = 0;
         for (int kb = 0; kb < kb_count; ++kb) {
           if ((kb & 3) == 0) {
-            // This group's scales into tensor-memory buffer f (A: 4 columns, W: the next
-            // 4); tcgen05 copies and MMAs issued by one thread run in issue order, so the
-            // MMAs below read them, and the group two back has finished with the buffer.
-            if (!mbar_wait(&mb->sf_full[f], fph, err, TB_DEV_GEMM_TIMEOUT, abort)) {
+            // This group's scales, written into tensor-memory buffer b by the SF warps.
+            if (!mbar_wait(&mb->st_full[b], bph, err, TB_DEV_GEMM_TIMEOUT, abort)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t src = smem_u32(smem + C::OFF_SF + f * 2 * C::SF_BYTES);
-            sf_col = tmem + C::COL_SF + 8 * f;
-            tmem_cp_128x128b(sf_col, sdesc_rows16(src));
-            tmem_cp_128x128b(sf_col + 4, sdesc_rows16(src + C::SF_BYTES));
-            umma_commit(&mb->sf_empty[f]);  // the shared-memory chunk is free once copied
-            if (++f == C::SF_SLOTS) f = 0, fph ^= 1;
+            sf_col = tmem + C::COL_SF + C::SF_COLS * b;
           }
           if (!mbar_wait(&bars->full[s], ph, err, TB_DEV_GEMM_TIMEOUT, abort)) {
             ok = false;
@@ -262,12 +295,16 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
           const uint64_t ad = sdesc_sw128(sa), bd = sdesc_sw128(sa + C::A_BYTES);
-          const uint32_t col = sf_col + (kb & 3);
+          const uint32_t col = sf_col + 4 * (kb & 3);  // this k-block's 4 columns of A, then of W
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_mx(d, ad + 2 * k, bd + 2 * k, idesc_mx(C::BN, k), col, col + 4, (kb | k) != 0);
+            umma_mx(d, ad + 2 * k, bd + 2 * k, idesc_mx(C::BN, k), col, col + C::SF_COLS / 2, (kb | k) != 0);
           umma_commit(&bars->empty[s]);
           if (++s == C::STAGES) s = 0, ph ^= 1;
+          if ((kb & 3) == 3 || kb + 1 == kb_count) {
+            umma_commit(&mb->st_empty[b]);  // the buffer is free once these MMAs are done
+            if (++b == 2) b = 0, bph ^= 1;
+          }
         }
         if (!ok) break;
         umma_commit(&bars->tfull[acc]);
@@ -276,7 +313,7 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(&bars->done);
       drain_wait(&bars->done, 0);
     }
-  } else {
+  } else if (warp < 6) {
     const int q = warp & 3;
     float* stage = out_stage + q * 32 * TC_OUT_STRIDE;
     int acc = 0;
@@ -292,6 +329,36 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive_relaxed(&bars->tempty[acc]);
       if (++acc == 2) acc = 0, acc_ph ^= 1;
     }
+  } else {
+    // SF warps (6-9): each group's scale chunks from shared memory into a tensor-memory
+    // scale buffer, for the 32 lanes of this warp's quarter.
+    const int q = warp & 3;
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    int f = 0, b = 0;
+    uint32_t fph = 0, bph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int g = 0; g < groups; ++g) {
+        if (!warp_wait(&mb->sf_full[f], fph, err, abort) || !warp_wait(&mb->st_empty[b], bph ^ 1, err, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* chunk = smem + C::OFF_SF + f * 2 * C::SF_BYTES;
+        const uint32_t col = C::COL_SF + C::SF_COLS * b;
+        sf_store(chunk, chunk + C::SF_BYTES, tq, col, col + C::SF_COLS / 2, q, lane);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&mb->st_full[b]);
+          mbar_arrive(&mb->sf_empty[f]);
+        }
+        if (++f == C::SF_SLOTS) f = 0, fph ^= 1;
+        if (++b == 2) b = 0, bph ^= 1;
+      }
+    }
+    if (!ok) *abort = 1;
   }
 
   tc_fence_before();
@@ -332,7 +399,7 @@ int launch_mx(const uint8_t* a, const uint8_t* sfa, const uint8_t* w, const uint
   if (!encode_tmap_fp8(&ta, a, m, k, k) || !encode_tmap_fp8(&tw, w, n, k, k)) return TB_ERR_CUDA;
   const int tiles = ((m + C::BM - 1) / C::BM) * (n / C::BN);
   const int grid = tiles < sm_budget() ? tiles : sm_budget();
-  return launch_pdl(mx_gemm_kernel<EPI>, grid, 192, C::SMEM, stream, ta, tw, sfa, sfw, m, n, k, e, err);
+  return launch_pdl(mx_gemm_kernel<EPI>, grid, C::THREADS, C::SMEM, stream, ta, tw, sfa, sfw, m, n, k, e, err);
 }
 
 }  // namespace
@@ -366,9 +433,6 @@ int gemm_mx(const uint8_t* a, const uint8_t* sfa, const uint8_t* w, const uint8_
       (reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfw) & 15))
     return TB_ERR_ARG;
   if (e.rows) return TB_ERR_UNSUPPORTED;
-  // The scale-factor copy into tensor memory is being replaced (tcgen05.cp with this
-  // descriptor raised a misaligned-address fault); nothing launches until then.
-  if (k > 0) return TB_ERR_UNSUPPORTED;
   switch (e.kind) {
     case TB_EPI_STORE: return launch_mx<TB_EPI_STORE>(a, sfa, w, sfw, m, n, k, e, err, stream);
     case TB_EPI_SILU: return launch_mx<TB_EPI_SILU>(a, sfa, w, sfw, m, n, k, e, err, stream);
