@@ -12,7 +12,7 @@
 // BN is 256, 128 or 64: small-M GEMMs (the decoder's) take narrow tiles to spread
 // over more SMs.
 // fp32: a CUDA-core kernel, 128 x 128 tiles, 8 x 8 outputs per thread, for the fp32
-// parity path.
+// parity path; at most 8 rows (the fp32 decoder at small batch), a matrix-vector kernel.
 #include <algorithm>
 
 #include "host.h"
@@ -421,6 +421,67 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 }
 
 // ---------------------------------------------------------------------------
+// fp32 matrix-vector kernel for a few rows (the fp32 decoder's GEMMs at batch 1-8): each
+// warp takes 4 consecutive output columns (one epilogue group) for every row, reading its
+// 4 weight rows once with 16-byte loads; the rows of A are staged in shared memory. A
+// 128 x 128 tile of the GEMM kernel would compute up to 127 rows of nothing here.
+
+constexpr int GV_MAX_ROWS = 8, GV_WARPS = 8, GV_MAX_K = 1280;
+
+__global__ void __launch_bounds__(GV_WARPS * 32) gemv_f32_kernel(const float* __restrict__ A, long long lda,
+                                                                 const float* __restrict__ W, int M, int N, int K,
+                                                                 const tb_epilogue e) {
+  __shared__ __align__(16) float As[GV_MAX_ROWS * GV_MAX_K];
+  grid_dep_wait();
+  grid_dep_launch();
+  if (e.rows) M = min(M, *e.rows);
+  if (M <= 0) return;
+  for (int i = threadIdx.x * 4; i < M * K; i += blockDim.x * 4) {
+    const int m = i / K, k = i - m * K;
+    *reinterpret_cast<float4*>(As + i) = *reinterpret_cast<const float4*>(A + (long long)m * lda + k);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = (blockIdx.x * GV_WARPS + warp) * 4;
+  if (n >= N) return;
+  float acc[GV_MAX_ROWS][4];
+#pragma unroll
+  for (int m = 0; m < GV_MAX_ROWS; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
+  for (int k = lane * 4; k < K; k += 128) {
+    float4 w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const float4*>(W + (long long)(n + j) * K + k);
+#pragma unroll
+    for (int m = 0; m < GV_MAX_ROWS; ++m) {
+      if (m >= M) break;
+      const float4 a = *reinterpret_cast<const float4*>(As + m * K + k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        acc[m][j] = fmaf(a.w, w[j].w, fmaf(a.z, w[j].z, fmaf(a.y, w[j].y, fmaf(a.x, w[j].x, acc[m][j]))));
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < GV_MAX_ROWS; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], o);
+  if (lane != 0) return;
+  for (int m = 0; m < M; ++m) {
+    if (e.kind == TB_EPI_ARGMAX) {
+      ArgmaxAcc am;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) am.add(e, n + j, acc[m][j]);
+      am.flush(e, m);
+    } else {
+      epi_group(e, m, n, acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 
 bool encode_tmap_2d(CUtensorMap* map, const void* ptr, long long rows, long long cols, long long ld_elems,
@@ -572,6 +633,12 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
     }
   }
   if (dtype != TB_F32) return TB_ERR_ARG;
+  if (m <= GV_MAX_ROWS && k <= GV_MAX_K && k % 128 == 0 && n % 4 == 0 && lda % 4 == 0 &&
+      !(reinterpret_cast<uintptr_t>(a) & 15) && !(reinterpret_cast<uintptr_t>(w) & 15)) {
+    const int cols = GV_WARPS * 4;
+    return launch_pdl(gemv_f32_kernel, dim3((n + cols - 1) / cols), GV_WARPS * 32, 0, stream,
+                      reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(w), m, n, k, e);
+  }
   if (k % SG_BK || n % SG_BN || lda % 4) return TB_ERR_UNSUPPORTED;
   dim3 grid(n / SG_BN, (m + SG_BM - 1) / SG_BM);
   return launch_pdl(gemm_f32_kernel, grid, 256, 0, stream, reinterpret_cast<const float*>(a), lda,
