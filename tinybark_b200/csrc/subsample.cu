@@ -19,11 +19,7 @@ constexpr int S_T2 = 8;          // depthwise-1 output rows per block: one warp 
 constexpr int S_C = 64;          // channels per block: two per lane
 constexpr int S_F1 = 64, S_F2 = 32, S_F3 = 16;
 constexpr int S_FEAT_ROWS = 4 * S_T2 + 3;  // feature rows behind S_T2 depthwise-1 rows
-// Feature f of a shared-memory row at column f + 4 (zero columns 0-3 and 132-135): the four
-// features a sweep step reads, 4 f2 .. 4 f2 + 3, are then one aligned 16-byte load, and
-// the row stride (544 bytes) keeps every row 16-byte aligned.
-constexpr int S_FEAT_PAD = 4;
-constexpr int S_FEAT_COLS = TB_MELS + 2 * S_FEAT_PAD;
+constexpr int S_FEAT_COLS = TB_MELS + 2;   // frequency padded by one each side
 
 // conv 0 (3x3/2, 1 -> 256, + ReLU) fused into depthwise 1 (3x3/2 + bias). Warp w of a
 // block makes depthwise-1 row t2 = t2a + w for channels c0 + lane and c0 + 32 + lane,
@@ -32,8 +28,8 @@ constexpr int S_FEAT_COLS = TB_MELS + 2 * S_FEAT_PAD;
 // first of those columns is the previous step's last, so each step computes 2 x 3
 // conv-0 values per channel from a 7 x 5 window of features (the window's first
 // column also carried over), all features read from shared memory (the same address
-// for every lane: one broadcast per read, four features per read). Conv-0 values
-// outside the clip's rows or the frequency range are the zero padding of depthwise 1.
+// for every lane: one broadcast per read). Conv-0 values outside the clip's rows or
+// the frequency range are the zero padding of depthwise 1.
 template <typename T>
 __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict__ feats,
                                                         const int* __restrict__ frame_off,
@@ -41,7 +37,7 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
                                                         const int* __restrict__ tiles, const float* __restrict__ w0,
                                                         const float* __restrict__ b0, const float* __restrict__ w1,
                                                         const float* __restrict__ b1, T* __restrict__ d1) {
-  __shared__ __align__(16) float sf[S_FEAT_ROWS][S_FEAT_COLS];
+  __shared__ float sf[S_FEAT_ROWS][S_FEAT_COLS];
   const int clip = tiles[2 * blockIdx.x], t2a = tiles[2 * blockIdx.x + 1];
   const int F = frame_off[clip + 1] - frame_off[clip], T1 = t1_off[clip + 1] - t1_off[clip],
             T2 = t2_off[clip + 1] - t2_off[clip];
@@ -49,9 +45,9 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
   const int fa = 4 * t2a - 3;  // feature row of the tile's first shared-memory row
 
   for (int i = threadIdx.x; i < S_FEAT_ROWS * S_FEAT_COLS; i += 256) {
-    const int r = i / S_FEAT_COLS, f = i % S_FEAT_COLS - S_FEAT_PAD;
+    const int r = i / S_FEAT_COLS, f = i % S_FEAT_COLS - 1;
     const int t = fa + r;
-    sf[r][f + S_FEAT_PAD] = (t >= 0 && t < F && f >= 0 && f < TB_MELS) ? fbase[(long long)t * TB_MELS + f] : 0.f;
+    sf[r][f + 1] = (t >= 0 && t < F && f >= 0 && f < TB_MELS) ? fbase[(long long)t * TB_MELS + f] : 0.f;
   }
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ca = blockIdx.y * S_C + lane, cb = ca + 32;
@@ -74,9 +70,9 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
     rowok[dt] = t1 >= 0 && t1 < T1;
   }
   const float* srow = &sf[4 * w][0];  // conv-0 row dt reads feature rows 2 dt .. 2 dt + 2 of these 7
-  float xc[7];  // feature 4 f2 - 1 (zero at f2 = 0), carried from the previous step
+  float xc[7];                        // feature column 4 f2 (padded), carried from the previous step
 #pragma unroll
-  for (int r = 0; r < 7; ++r) xc[r] = srow[r * S_FEAT_COLS + S_FEAT_PAD - 1];
+  for (int r = 0; r < 7; ++r) xc[r] = srow[r * S_FEAT_COLS];
   float pa[3] = {0.f, 0.f, 0.f}, pb[3] = {0.f, 0.f, 0.f};  // conv-0 column 2 f2 - 1 (zero at f2 = 0)
   T* out = d1 + (long long)(t2_off[clip] + t2) * S_F2 * TB_CHANNELS;
 #pragma unroll 1
@@ -84,11 +80,11 @@ __global__ void __launch_bounds__(256) conv0_dw1_kernel(const float* __restrict_
     float x1[7], x2[7], x3[7], x4[7];
 #pragma unroll
     for (int r = 0; r < 7; ++r) {
-      const float4 q = *reinterpret_cast<const float4*>(srow + r * S_FEAT_COLS + S_FEAT_PAD + 4 * f2);
-      x1[r] = q.x;
-      x2[r] = q.y;
-      x3[r] = q.z;
-      x4[r] = q.w;
+      const float* q = srow + r * S_FEAT_COLS + 4 * f2;
+      x1[r] = q[1];
+      x2[r] = q[2];
+      x3[r] = q[3];
+      x4[r] = q[4];
     }
     float acc_a = b1a, acc_b = b1b;
 #pragma unroll
