@@ -64,7 +64,7 @@ def args_parser():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-config0", action="store_true", help="skip the batch-1 fp32 end-to-end line")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,longform,load,text)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,decode_loop,longform,load,text)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -664,12 +664,46 @@ def run_micro(args):
                     emit(kernel="relpos_attention", dtype=dt_name, rows=rows, T=t, clips=clips, us=s * 1e6,
                          tflops=fl / s / 1e12, frac=fl / s / 1e12 / tflops)
     K.check(dev)
+    if want("decode_loop"):
+        run_decode_loop(args, dev)
     if want("longform"):
         run_longform(args, dev, tflops)
     if want("load"):
         run_load(args, dev, hbm)
     if want("text"):
         run_text(args, dev)
+
+
+def run_decode_loop(args, dev):
+    """The whole persistent greedy loop (2-layer model, bf16) for `--lanes` lanes whose
+    lengths are those of 2-30 s clips, on seeded N(0, 1) encoder frames (every lane then
+    runs to its cap): milliseconds per loop, per iteration and per lane-iteration."""
+    import torch
+
+    from tinybark_b200 import lengths, synthetic
+    from tinybark_b200 import weights as w
+    from tinybark_b200.engine import Engine
+
+    cfg = synthetic.config(2)
+    eng = Engine(w.convert(synthetic.state_dict(0, layers=2), cfg), cfg, dtype="bf16", device=dev)
+    for lanes in map(int, args.lanes.split(",")):
+        durs = np.sort(synthetic.durations(lanes, 4000 + lanes))[::-1]
+        plan = eng.plan([lengths.frames(int(round(d * 16000))) for d in durs])
+        enc = torch.randn(plan.batch.t3_total, 640, device=dev, generator=torch.Generator(device=dev).manual_seed(0))
+        eng.decode(enc, plan)
+        eng.check()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(2):
+            eng.decode(enc, plan, early_exit=False)
+        b.record()
+        torch.cuda.synchronize()
+        eng.check()
+        ms = a.elapsed_time(b) / 2
+        caps = plan.caps.cpu().numpy()
+        print(json.dumps({"kernel": "decode_loop", "lanes": lanes, "ms": ms, "max_cap": int(caps.max()),
+                          "lane_iterations": int(caps.sum()), "us_per_iteration": 1000 * ms / int(caps.max()),
+                          "ns_per_lane_iteration": 1e6 * ms / int(caps.sum())}), flush=True)
 
 
 def run_text(args, dev):
