@@ -155,8 +155,9 @@ __global__ void __launch_bounds__(256) relpos_attention_simt(const T* __restrict
 // (q + bias_u) . r + (bias_v - bias_u) . r: the second product depends only on the
 // head and the relative position and comes precomputed per layer (rel_c), so Qu is the
 // only query operand. Each softmax warp copies the 96 BD columns its 32 rows need into
-// shared memory and reads its row's window shifted by its row index (the relative
-// shift). P (bf16) is written back into the tensor memory of S and the PV MMA reads
+// shared memory (a 64-column ring per row) and reads its row's window shifted by its row
+// index (the relative shift). K and the band are double-buffered: tile g + 1's copies land
+// while tile g's S and BD are computed. P (bf16) is written back into the tensor memory of S and the PV MMA reads
 // it from there; V is an MN-major operand straight from the [frames, 1024] V tensor.
 // O accumulates in tensor memory, rescaled by the softmax threads when the row max
 // grows.
@@ -165,9 +166,11 @@ namespace att {
 constexpr int TQ = 128, TK = 64, D = 128, BAND = 192;
 constexpr int Q_BYTES = TQ * D * 2, K_BYTES = TK * D * 2, R_BYTES = BAND * D * 2, V_BYTES = TK * D * 2;
 constexpr int Q_SUB = TQ * 128, K_SUB = TK * 128, R_SUB = BAND * 128, V_SUB = TK * 128;  // 64-column halves
-constexpr int ST_STRIDE = 100, WIN = 96;
+// A softmax warp stages its rows' 96 BD columns in a 64-column ring per row (columns 64-95
+// land on 0-31 once the first 32 keys no longer need them), so K and the band fit twice.
+constexpr int ST_STRIDE = 68, WIN = 96;
 constexpr int ST_BYTES = 4 * 32 * ST_STRIDE * 4, C_BYTES = 4 * WIN * 4;
-constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_R = OFF_K + K_BYTES, OFF_V = OFF_R + R_BYTES,
+constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_R = OFF_K + 2 * K_BYTES, OFF_V = OFF_R + 2 * R_BYTES,
               OFF_ST = OFF_V + V_BYTES, OFF_C = OFF_ST + ST_BYTES, OFF_BAR = OFF_C + C_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
 constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, COL_P = 384, TMEM_COLS = 512;
@@ -175,7 +178,8 @@ constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, COL_P = 384, TMEM_COLS =
 constexpr float SCALE_LOG2 = 0.12751743074f;
 
 struct Bars {
-  uint64_t q_full, q_empty, kr_full, kr_empty, v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, o_empty, done;
+  uint64_t q_full, q_empty, kr_full[2], kr_empty[2], v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, o_empty,
+      done;
   uint32_t tmem;
   int abort;
 };
@@ -231,8 +235,10 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->q_empty, 1);
-    mbar_init(&bars->kr_full, 1);
-    mbar_init(&bars->kr_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->kr_full[i], 1);
+      mbar_init(&bars->kr_empty[i], 1);
+    }
     mbar_init(&bars->v_full, 1);
     mbar_init(&bars->v_empty, 1);
     mbar_init(&bars->sbd_full, 1);
@@ -269,15 +275,19 @@ __global__ void __launch_bounds__(192, 1)
         for (int j = 0; j < it.nk; ++j) {
           const int k0 = j * TK;
           const int band0 = max_len - TQ - it.q0 + k0;  // may be negative: TMA fills zeros
-          if (!mbar_wait(&bars->kr_empty, (kr_issued & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+          // K and the band in one of two stages (tile kr_issued uses stage kr_issued % 2).
+          const int ks = kr_issued & 1;
+          if (!mbar_wait(&bars->kr_empty[ks], ((kr_issued >> 1) & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&bars->kr_full, K_BYTES + R_BYTES);
-          tma_load_2d(smem + OFF_K, &tk, &bars->kr_full, it.col0, it.base + k0);
-          tma_load_2d(smem + OFF_K + K_SUB, &tk, &bars->kr_full, it.col0 + 64, it.base + k0);
-          tma_load_2d(smem + OFF_R, &tr, &bars->kr_full, it.col0, band0);
-          tma_load_2d(smem + OFF_R + R_SUB, &tr, &bars->kr_full, it.col0 + 64, band0);
+          uint8_t* sk = smem + OFF_K + ks * K_BYTES;
+          uint8_t* sr = smem + OFF_R + ks * R_BYTES;
+          mbar_expect_tx(&bars->kr_full[ks], K_BYTES + R_BYTES);
+          tma_load_2d(sk, &tk, &bars->kr_full[ks], it.col0, it.base + k0);
+          tma_load_2d(sk + K_SUB, &tk, &bars->kr_full[ks], it.col0 + 64, it.base + k0);
+          tma_load_2d(sr, &tr, &bars->kr_full[ks], it.col0, band0);
+          tma_load_2d(sr + R_SUB, &tr, &bars->kr_full[ks], it.col0 + 64, band0);
           ++kr_issued;
           if (!mbar_wait(&bars->v_empty, (v_issued & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
             ok = false;
@@ -292,17 +302,19 @@ __global__ void __launch_bounds__(192, 1)
       // Let the copies in flight land before the CTA exits (all have, unless the loop was
       // abandoned).
       if (q_issued) att_drain(&bars->q_full, (q_issued - 1) & 1);
-      if (kr_issued) att_drain(&bars->kr_full, (kr_issued - 1) & 1);
+      for (int i = kr_issued - 1; i >= 0 && i >= kr_issued - 2; --i) att_drain(&bars->kr_full[i & 1], (i >> 1) & 1);
       if (v_issued) att_drain(&bars->v_full, (v_issued - 1) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_bf16(TQ, TK), id_bd = idesc_bf16(TQ, BAND), id_pv = idesc_bf16_bmn(TQ, D);
-      const uint32_t qa = smem_u32(smem + OFF_Q), ka = smem_u32(smem + OFF_K), ra = smem_u32(smem + OFF_R),
+      const uint32_t qa = smem_u32(smem + OFF_Q), ka0 = smem_u32(smem + OFF_K), ra0 = smem_u32(smem + OFF_R),
                      va = smem_u32(smem + OFF_V);
       // S and BD of tile g + 1 are issued as soon as the softmax has read tile g's (before
-      // tile g's PV), so they overlap the softmax of tile g; P has its own columns.
-      auto sbd = [&]() {
+      // tile g's PV), so they overlap the softmax of tile g; P has its own columns. Tile gg's
+      // K and band are in stage gg % 2.
+      auto sbd = [&](int gg) {
+        const uint32_t ka = ka0 + (gg & 1) * K_BYTES, ra = ra0 + (gg & 1) * R_BYTES;
         tc_fence_after();
 #pragma unroll
         for (int s = 0; s < 2; ++s)
@@ -317,7 +329,7 @@ __global__ void __launch_bounds__(192, 1)
             umma_f16(tmem + COL_BD, sdesc_sw128(qa + s * Q_SUB) + 2 * k, sdesc_sw128(ra + s * R_SUB) + 2 * k, id_bd,
                      (s | k) != 0);
         umma_commit(&bars->sbd_full);
-        umma_commit(&bars->kr_empty);
+        umma_commit(&bars->kr_empty[gg & 1]);
       };
       bool ok = true;
       int g = 0, n = 0;  // key tiles and items this CTA has done
@@ -325,9 +337,9 @@ __global__ void __launch_bounds__(192, 1)
       // loaded, the tile's K and band loaded, the softmax done reading the S and BD before.
       auto first_sbd = [&](int items, int gg) {
         if (!mbar_wait(&bars->q_full, items & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
-        if (!mbar_wait(&bars->kr_full, gg & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
+        if (!mbar_wait(&bars->kr_full[gg & 1], (gg >> 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
         if (gg > 0 && !mbar_wait(&bars->sbd_empty, (gg - 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) return false;
-        sbd();
+        sbd(gg);
         return true;
       };
       int t = blockIdx.x;
@@ -336,12 +348,12 @@ __global__ void __launch_bounds__(192, 1)
         const int nk = item(t).nk;
         for (int j = 0; j < nk && ok; ++j, ++g) {
           if (j + 1 < nk) {
-            if (!mbar_wait(&bars->kr_full, (g + 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort) ||
+            if (!mbar_wait(&bars->kr_full[(g + 1) & 1], ((g + 1) >> 1) & 1, err, TB_DEV_ATTN_TIMEOUT, abort) ||
                 !mbar_wait(&bars->sbd_empty, g & 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {  // tile g read
               ok = false;
               break;
             }
-            sbd();
+            sbd(g + 1);
           } else {
             umma_commit(&bars->q_empty);  // this item's S and BD products are issued: Q is free after them
           }
@@ -416,26 +428,45 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(r[k]);
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-          tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
-          tmem_wait_ld();
-          float4* dst = reinterpret_cast<float4*>(stage + lane * ST_STRIDE + 32 * c);
+        // BD columns 0-63 of this warp's window into the row's ring.
+        float* ring = stage + lane * ST_STRIDE;
+        auto to_ring = [&](int slot) {
+          float4* dst = reinterpret_cast<float4*>(ring + slot);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
             dst[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
                                  __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
+        };
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
+          tmem_wait_ld();
+          to_ring(32 * c);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->sbd_empty);
-        // Scores: content + shifted position term, scaled into the base-2 domain.
-        const float* srow = stage + lane * ST_STRIDE + (31 - lane);
+        // Scores: content + shifted position term, scaled into the base-2 domain. Key jj
+        // reads window column 31 - lane + jj: columns 0-62 for the first 32 keys; then
+        // columns 64-95 take ring slots 0-31 (each lane's ring is its own row), and the
+        // last 32 keys read column x at slot x % 64.
         const float* crow = cband + (31 - lane);
         float mx = -INFINITY;
 #pragma unroll
-        for (int jj = 0; jj < TK; ++jj) {
-          const float v = (sc[jj] + srow[jj] + crow[jj]) * SCALE_LOG2;
+        for (int jj = 0; jj < TK / 2; ++jj) {
+          const float v = (sc[jj] + ring[31 - lane + jj] + crow[jj]) * SCALE_LOG2;
+          sc[jj] = k0 + jj < it.T ? v : -INFINITY;
+          mx = fmaxf(mx, sc[jj]);
+        }
+        tmem_ld32(tl + COL_BD + wcol + 64, r);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->sbd_empty);  // S and BD read: the next tile's may go
+        to_ring(0);
+        const float* lo = ring + (31 - lane);  // window column x = 31 - lane + jj below 64: slot x
+        const float* hi = lo - 64;              // x of 64 and above: slot x - 64
+#pragma unroll
+        for (int jj = TK / 2; jj < TK; ++jj) {
+          const float b = jj >= 33 + lane ? hi[jj] : lo[jj];
+          const float v = (sc[jj] + b + crow[jj]) * SCALE_LOG2;
           sc[jj] = k0 + jj < it.T ? v : -INFINITY;
           mx = fmaxf(mx, sc[jj]);
         }
