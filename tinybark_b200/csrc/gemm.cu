@@ -40,7 +40,7 @@ struct TcCfg {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
-                   const tb_epilogue e, int* err) {
+                   const tb_epilogue e, int* err, int splits) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -71,7 +71,10 @@ __global__ void __launch_bounds__(192, 1)
   grid_dep_launch();
 
   if (e.rows) M = min(M, *e.rows);
-  const int m_tiles = (M + C::BM - 1) / C::BM, n_tiles = N / BN, tiles = m_tiles * n_tiles, kb_count = K / C::BK;
+  // Work item t: output tile t / splits, K range t % splits of `splits` equal ranges (split
+  // K only with the EPI_RESIDUAL_SPLIT epilogue, whose atomic adds sum the ranges).
+  const int m_tiles = (M + C::BM - 1) / C::BM, n_tiles = N / BN, tiles = m_tiles * n_tiles * splits,
+            kb_count = K / C::BK / splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -82,7 +85,7 @@ __global__ void __launch_bounds__(192, 1)
       long long issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int mt = t / n_tiles, nt = t % n_tiles;
+        const int tile = t / splits, mt = tile / n_tiles, nt = tile % n_tiles, kb0 = (t % splits) * kb_count;
         for (int kb = 0; kb < kb_count; ++kb) {
           if (!mbar_wait(&bars->empty[s], ph ^ 1, err, TB_DEV_GEMM_TIMEOUT, abort)) {
             ok = false;
@@ -90,8 +93,8 @@ __global__ void __launch_bounds__(192, 1)
           }
           uint8_t* sa = smem + s * C::STAGE_BYTES;
           mbar_expect_tx(&bars->full[s], C::STAGE_BYTES);
-          tma_load_2d(sa, &ta, &bars->full[s], kb * C::BK, mt * C::BM);
-          tma_load_2d(sa + C::A_BYTES, &tw, &bars->full[s], kb * C::BK, nt * BN);
+          tma_load_2d(sa, &ta, &bars->full[s], (kb0 + kb) * C::BK, mt * C::BM);
+          tma_load_2d(sa + C::A_BYTES, &tw, &bars->full[s], (kb0 + kb) * C::BK, nt * BN);
           ++issued;
           if (++s == C::STAGES) s = 0, ph ^= 1;
         }
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      const int mt = t / n_tiles, nt = t % n_tiles;
+      const int tile = t / splits, mt = tile / n_tiles, nt = tile % n_tiles;
       const int row0 = mt * C::BM + q * 32, n0 = nt * BN;
       if (!epilogue_tile<BN, EPI>(e, stage, tmem + ((uint32_t)(q * 32) << 16) + acc * BN, row0, n0, lane, M,
                                   &bars->tfull[acc], acc_ph, err, abort))
@@ -505,7 +508,7 @@ static bool encode_tmap(CUtensorMap* map, const void* ptr, long long rows, long 
 
 template <int BN, int EPI>
 static int launch_tc(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e, int* err,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int splits = 1) {
   using C = TcCfg<BN>;
   static bool configured = false;
   if (!configured) {
@@ -516,9 +519,9 @@ static int launch_tc(const void* a, long long lda, const void* w, int m, int n, 
   }
   CUtensorMap ta, tw;
   if (!encode_tmap(&ta, a, m, k, lda, C::BM) || !encode_tmap(&tw, w, n, k, k, BN)) return TB_ERR_CUDA;
-  const int tiles = ((m + C::BM - 1) / C::BM) * (n / BN);
+  const int tiles = ((m + C::BM - 1) / C::BM) * (n / BN) * splits;
   const int grid = tiles < sm_budget() ? tiles : sm_budget();
-  return launch_pdl(gemm_tc_kernel<BN, EPI>, grid, 192, C::SMEM, stream, ta, tw, m, n, k, e, err);
+  return launch_pdl(gemm_tc_kernel<BN, EPI>, grid, 192, C::SMEM, stream, ta, tw, m, n, k, e, err, splits);
 }
 
 // The pair kernel: clusters of two CTAs, as many pairs as can be resident at once (at
@@ -561,9 +564,25 @@ static int launch_tc2(const void* a, long long lda, const void* w, int m, int n,
   return check_launch();
 }
 
+// K splits for a residual GEMM of at most 256 rows (a clip or two) whose tiles leave most
+// SMs idle (three quarters of them or more): the largest power of two up to 8 that keeps at least
+// 4 k-blocks per split and at most one work item per SM. Split sums land in an order the
+// atomic adds choose, so such a GEMM is not bit-reproducible; larger ones never split.
+static int residual_splits(int m, int n, int k, int bn) {
+  const int tiles = ((m + 127) / 128) * (n / bn), kb = k / 64, sms = sm_budget();
+  if (m > 256 || 4 * tiles > sms) return 1;
+  int s = 1;
+  while (s < 8 && kb % (2 * s) == 0 && kb / (2 * s) >= 4 && tiles * 2 * s <= sms) s *= 2;
+  return s;
+}
+
 template <int BN>
 static int launch_tc_kind(const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue& e,
                           int* err, cudaStream_t s) {
+  if (e.kind == TB_EPI_RESIDUAL && !e.rows) {
+    const int splits = residual_splits(m, n, k, BN);
+    if (splits > 1) return launch_tc<BN, EPI_RESIDUAL_SPLIT>(a, lda, w, m, n, k, e, err, s, splits);
+  }
   switch (e.kind) {
     case TB_EPI_STORE: return launch_tc<BN, TB_EPI_STORE>(a, lda, w, m, n, k, e, err, s);
     case TB_EPI_SILU: return launch_tc<BN, TB_EPI_SILU>(a, lda, w, m, n, k, e, err, s);

@@ -7,6 +7,9 @@
 namespace tb {
 
 constexpr int TC_OUT_STRIDE = 36;  // floats per staged row: 16-byte aligned, conflict-free
+// Epilogue of a split-K residual GEMM (an internal kind beside tb_epilogue_kind): each
+// K-split's partial product, times alpha, added to the fp32 residual with atomic adds.
+constexpr int EPI_RESIDUAL_SPLIT = 64;
 
 struct TcBars {
   uint64_t full[8], empty[8], tfull[2], tempty[2], done;
@@ -148,7 +151,20 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
   float4 v[8];
 #pragma unroll
   for (int it = 0; it < 8; ++it) v[it] = *reinterpret_cast<const float4*>(stage + (it * 4 + sub) * S + col);
-  if constexpr (EPI == TB_EPI_RESIDUAL) {
+  if constexpr (EPI == EPI_RESIDUAL_SPLIT) {
+    float* out = reinterpret_cast<float*>(e.out);
+    const float alpha = e.alpha;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int m = row0 + it * 4 + sub;
+      if (m >= M) continue;
+      float* p = out + (long long)m * e.ldo + n;
+      atomicAdd(p, alpha * v[it].x);
+      atomicAdd(p + 1, alpha * v[it].y);
+      atomicAdd(p + 2, alpha * v[it].z);
+      atomicAdd(p + 3, alpha * v[it].w);
+    }
+  } else if constexpr (EPI == TB_EPI_RESIDUAL) {
     float* out = reinterpret_cast<float*>(e.out);
     const float4* x = ops.x;
     const float alpha = e.alpha;
