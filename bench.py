@@ -64,7 +64,7 @@ def args_parser():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-config0", action="store_true", help="skip the batch-1 fp32 end-to-end line")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,decode_loop,longform,load,text)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,decode_loop,batch1,longform,load,text)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -666,12 +666,43 @@ def run_micro(args):
     K.check(dev)
     if want("decode_loop"):
         run_decode_loop(args, dev)
+    if want("batch1"):
+        run_batch1(args, dev)
     if want("longform"):
         run_longform(args, dev, tflops)
     if want("load"):
         run_load(args, dev, hbm)
     if want("text"):
         run_text(args, dev)
+
+
+def run_batch1(args, dev):
+    """Batch 1: the bf16 encoder of one 10 s clip (the metric's "encoder ms per 10 s clip"),
+    and config 0 (fp32, Bark.tokens of the 10 s seed-0 clip, cold and warm)."""
+    import torch
+
+    import tinybark_b200
+    from tinybark_b200 import synthetic
+
+    tensors, cfg = weights(args.layers)
+    eng = tinybark_b200.load("gpu", dtype="bf16", weights=(tensors, cfg)).engine
+    plan = eng.plan([1000])
+    s1, o1 = eng.upload([synthetic.clip(10.0, 0)])
+    f1 = eng.features(s1, o1, plan)
+    for _ in range(3):
+        eng.encode(f1, plan)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(20):
+        eng.encode(f1, plan)
+    b.record()
+    torch.cuda.synchronize()
+    eng.check()
+    ms = a.elapsed_time(b) / 20
+    print(json.dumps({"kernel": "encoder_batch1_bf16", "layers": args.layers, "T": 125, "ms": ms,
+                      "weights_gbs": eng.layout.size / ms / 1e6}), flush=True)
+    del eng
+    print(json.dumps({"kernel": "config0_fp32", **run_config0(args, tensors, cfg)}), flush=True)
 
 
 def run_decode_loop(args, dev):
