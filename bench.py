@@ -69,6 +69,7 @@ def args_parser():
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
     p.add_argument("--lanes", default="64,512", help="--micro: decoder lanes")
+    p.add_argument("--lane-seconds", default="2,30", help="--micro decode_loop: the lanes' clip lengths, lo,hi seconds")
     p.add_argument("--profile", action="store_true", help="one step of the pipeline, for a profiler")
     p.add_argument("--decode-groups", type=int, default=0, help="concurrent decoder groups (0: by batch size)")
     return p
@@ -707,8 +708,9 @@ def run_batch1(args, dev):
 
 def run_decode_loop(args, dev):
     """The whole persistent greedy loop (2-layer model, bf16) for `--lanes` lanes whose
-    lengths are those of 2-30 s clips, on seeded N(0, 1) encoder frames (every lane then
-    runs to its cap): milliseconds per loop, per iteration and per lane-iteration."""
+    lengths are those of clips of `--lane-seconds` (uniform; 2-30 s by default), on seeded
+    N(0, 1) encoder frames (every lane then runs to its cap): milliseconds per loop, per
+    iteration and per lane-iteration."""
     import torch
 
     from tinybark_b200 import lengths, synthetic
@@ -718,7 +720,8 @@ def run_decode_loop(args, dev):
     cfg = synthetic.config(2)
     eng = Engine(w.convert(synthetic.state_dict(0, layers=2), cfg), cfg, dtype="bf16", device=dev)
     for lanes in map(int, args.lanes.split(",")):
-        durs = np.sort(synthetic.durations(lanes, 4000 + lanes))[::-1]
+        lo, hi = map(float, args.lane_seconds.split(","))
+        durs = np.sort(synthetic.durations(lanes, 4000 + lanes, lo, hi))[::-1]
         plan = eng.plan([lengths.frames(int(round(d * 16000))) for d in durs])
         enc = torch.randn(plan.batch.t3_total, 640, device=dev, generator=torch.Generator(device=dev).manual_seed(0))
         eng.decode(enc, plan)

@@ -146,8 +146,8 @@ __global__ void __launch_bounds__(256) relpos_attention_simt(const T* __restrict
 // ---------------------------------------------------------------------------
 // tcgen05 form (bf16): one CTA per (clip, head, 128 queries), key tiles of 64.
 //
-// Warp 0 loads tiles with TMA, warp 1 issues the MMAs, warps 2-5 (one query row per
-// thread) run the softmax. Per key tile, into tensor memory:
+// Warp 0 loads Q, K and band tiles with TMA, warp 6 the V tiles, warp 1 issues the MMAs,
+// warps 2-5 (one query row per thread) run the softmax. Per key tile, into tensor memory:
 //   S  = Qu K^T          (128 x 64)
 //   BD = Qu R_band^T     (128 x 192), R_band the 192 table rows the tile's relative
 //                        positions span (191 used)
@@ -176,6 +176,7 @@ constexpr int SMEM = 1024 + OFF_BAR + 256;
 constexpr uint32_t COL_S = 0, COL_BD = 64, COL_O = 256, COL_P = 384, TMEM_COLS = 512;
 // log2(e) / sqrt(128): scores are kept in the base-2 exponent domain.
 constexpr float SCALE_LOG2 = 0.12751743074f;
+constexpr int V_WARP = 6, THREADS = 32 * (V_WARP + 1);  // TMA, MMA, 4 softmax warps, the V loader
 
 struct Bars {
   uint64_t q_full, q_empty, kr_full[2], kr_empty[2], v_full, v_empty, sbd_full, sbd_empty, p_full, o_done, o_empty,
@@ -204,7 +205,7 @@ __device__ __forceinline__ bool att_warp_wait(uint64_t* bar, uint32_t parity, in
 // current item's last softmax and its output; q_empty (the item's last S and BD products
 // have read Q) and o_empty (the softmax warps have read the finished O) hand Q's buffer
 // and O's columns to the next item.
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(att::THREADS, 1)
     relpos_attention_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tr,
                         const float* __restrict__ rel_c, int max_len, const int* __restrict__ t3_off,
@@ -262,7 +263,7 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tr);
-      int kr_issued = 0, v_issued = 0, q_issued = 0;
+      int kr_issued = 0, q_issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < n_items && ok; t += gridDim.x) {
         const Item it = item(t);
@@ -289,20 +290,33 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d(sr, &tr, &bars->kr_full[ks], it.col0, band0);
           tma_load_2d(sr + R_SUB, &tr, &bars->kr_full[ks], it.col0 + 64, band0);
           ++kr_issued;
-          if (!mbar_wait(&bars->v_empty, (v_issued & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&bars->v_full, V_BYTES);
-          tma_load_2d(smem + OFF_V, &tv, &bars->v_full, it.col0, it.base + k0);
-          tma_load_2d(smem + OFF_V + V_SUB, &tv, &bars->v_full, it.col0 + 64, it.base + k0);
-          ++v_issued;
         }
       }
       // Let the copies in flight land before the CTA exits (all have, unless the loop was
       // abandoned).
       if (q_issued) att_drain(&bars->q_full, (q_issued - 1) & 1);
       for (int i = kr_issued - 1; i >= 0 && i >= kr_issued - 2; --i) att_drain(&bars->kr_full[i & 1], (i >> 1) & 1);
+    }
+  } else if (warp == V_WARP) {
+    // V has a producer of its own: its single buffer frees only when a tile's PV is done,
+    // and waiting for that in the K / band producer would hold back the next tiles'
+    // K and band copies.
+    if (lane == 0) {
+      int v_issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_items && ok; t += gridDim.x) {
+        const Item it = item(t);
+        for (int j = 0; j < it.nk; ++j) {
+          if (!mbar_wait(&bars->v_empty, (v_issued & 1) ^ 1, err, TB_DEV_ATTN_TIMEOUT, abort)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars->v_full, V_BYTES);
+          tma_load_2d(smem + OFF_V, &tv, &bars->v_full, it.col0, it.base + j * TK);
+          tma_load_2d(smem + OFF_V + V_SUB, &tv, &bars->v_full, it.col0 + 64, it.base + j * TK);
+          ++v_issued;
+        }
+      }
       if (v_issued) att_drain(&bars->v_full, (v_issued - 1) & 1);
     }
   } else if (warp == 1) {
@@ -382,6 +396,7 @@ __global__ void __launch_bounds__(192, 1)
       att_drain(&bars->done, 0);
     }
   } else {
+    // Warps 2-5 (V_WARP is 6).
     const int q = warp & 3;  // tensor-memory lane quarter: query rows 32q .. 32q+31
     const int il = q * 32 + lane;
     float* stage = reinterpret_cast<float*>(smem + OFF_ST) + q * 32 * ST_STRIDE;
@@ -565,7 +580,7 @@ static int launch_attn_tc(const void* qu, const void* k, const void* v, const vo
     return TB_ERR_CUDA;
   const int items = b.n_attn_tiles * TB_HEADS;
   const int grid = items < sm_budget() ? items : sm_budget();
-  return launch_pdl(relpos_attention_tc, grid, 192, att::SMEM, stream, mq, mk, mv, mr, rel_c, max_len, b.t3_off,
+  return launch_pdl(relpos_attention_tc, grid, att::THREADS, att::SMEM, stream, mq, mk, mv, mr, rel_c, max_len, b.t3_off,
                     b.attn_tiles, items, reinterpret_cast<__nv_bfloat16*>(out), err);
 }
 
