@@ -64,7 +64,7 @@ def args_parser():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-config0", action="store_true", help="skip the batch-1 fp32 end-to-end line")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,conv,mhsa,decode,decode_loop,batch1,longform,load,text)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,mx,conv,mhsa,decode,decode_loop,batch1,longform,load,text)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -597,6 +597,24 @@ def run_micro(args):
                 for name, s in (("ffn_up_silu", s1), ("ffn_down_residual", s2)):
                     emit(kernel=name, dtype=dt_name, rows=bt, us=s * 1e6, tflops=fl / s / 1e12,
                          frac=fl / s / 1e12 / tflops, bound="tensor" if code == L.BF16 else "fma")
+            if want("mx") and code == L.BF16:
+                # The FFN-up GEMM on block-scaled FP8 (the ffn="mxfp8" option): activations
+                # quantized (tb_mx_quantize), then the kind::mxf8f6f4 GEMM with SiLU.
+                x = rnd(bt, 1024, dt=dt)
+                xa, wa = K.MX(x), K.MX(rnd(4096, 1024, dt=dt) / 32)
+                h = torch.empty(bt, 4096, device=dev, dtype=dt)
+                e1 = L.Epilogue(kind=L.EPI_SILU, out_dtype=code, out=h.data_ptr(), ldo=4096)
+                quant = lambda: L.check(L.lib.tb_mx_quantize(code, x.data_ptr(), x.stride(0), bt, 1024,
+                                                             xa.codes.data_ptr(), xa.scales.data_ptr(),
+                                                             torch.cuda.current_stream().cuda_stream), "tb_mx_quantize")
+                sq = timed(quant, flush=flush)
+                sg = timed(lambda: K.gemm_mx(xa, wa, e1), flush=flush)
+                nbytes = bt * 1024 * (2 + 1) + bt * 1024 // 32
+                emit(kernel="mx_quantize", dtype="bf16->mxfp8", rows=bt, us=sq * 1e6, gbs=nbytes / sq / 1e9,
+                     frac=nbytes / sq / 1e9 / hbm, bound="hbm")
+                fl = 2 * bt * 1024 * 4096
+                emit(kernel="ffn_up_silu_mxfp8", dtype="mxfp8", rows=bt, us=sg * 1e6, tflops=fl / sg / 1e12,
+                     frac_of_2x_bf16=fl / sg / 1e12 / (2 * tflops), bound="tensor")
             if want("conv"):
                 x = rnd(bt, 1024, dt=dt)
                 pw1, pw2 = rnd(2048, 1024, dt=dt) / 32, rnd(1024, 1024, dt=dt) / 32

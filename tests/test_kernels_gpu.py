@@ -376,6 +376,25 @@ def test_depthwise_conv_silu(L, dtype, t3, err):
         assert max_rel(y[s].float().cpu(), F.silu(ref).cpu()) < TOL[dtype], c
 
 
+def test_depthwise_small_batch_matches_streaming_kernel(L, err):
+    """bf16: a few rows run the small-batch kernel, many rows the streaming kernel; the
+    clips they share come out bit for bit the same."""
+    small, big = [1, 5, 9, 40, 3, 125], [1, 5, 9, 40, 3, 125, 5000]
+    outs = []
+    x = torch.randn(sum(big), 1024, device="cuda").to(torch.bfloat16)
+    w = torch.randn(1024, 9, device="cuda")
+    bias = torch.randn(1024, device="cuda")
+    for t3 in (small, big):
+        b, keep, off = batch_for(L, t3, 32)
+        y = torch.full((off[-1], 1024), float("nan"), device="cuda", dtype=torch.bfloat16)
+        L.check(L.lib.tb_conv_depthwise(1, x.data_ptr(), w.data_ptr(), bias.data_ptr(), ctypes.byref(b), y.data_ptr(),
+                                        err.data_ptr(), stream()), "tb_conv_depthwise")
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs.append(y[: sum(small)])
+    assert torch.equal(outs[0], outs[1])
+
+
 @pytest.fixture(scope="module")
 def engine2():
     from conftest import state_dict

@@ -1,7 +1,7 @@
 """The backend registry of tinybark (tinybark/backends.py:1-142) with the `cuda` backend
 this package adds. `Model`, `Backend` and `DEVICES` mirror the reference's definitions
-(tinybark/backends.py:18-39) so the entry reads as it will in tinybark's own registry;
-INTEGRATION.md shows the one entry a maintainer adds there.
+(tinybark/backends.py:18-39) so the entry reads as it will in tinybark's own registry, where
+a maintainer adds that one entry.
 
     bark = BACKENDS["cuda"].load("gpu")
     text = bark.transcribe(samples)  # 16 kHz mono float32 NumPy array

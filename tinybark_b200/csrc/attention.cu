@@ -434,16 +434,16 @@ __global__ void __launch_bounds__(att::THREADS, 1)
           break;
         }
         tc_fence_after();
-        float sc[TK];
-        tmem_ld32(tl + COL_S, r);
+        // S (64 columns) and this warp's 96 BD columns out of tensor memory before any
+        // arithmetic, so the next tile's S and BD products can start right away. BD columns
+        // 0-63 of the window go to the row's ring; columns 64-95 stay in registers until
+        // the first 32 keys are scored. (Adding the (bias_v - bias_u) . r term into the
+        // ring here, from broadcast reads, measured slower than adding it per score.)
+        uint32_t s0[32], s1[32];
+        tmem_ld32(tl + COL_S, s0);
+        tmem_ld32(tl + COL_S + 32, s1);
+        tmem_ld32(tl + COL_BD + wcol, r);
         tmem_wait_ld();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) sc[k] = __uint_as_float(r[k]);
-        tmem_ld32(tl + COL_S + 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) sc[32 + k] = __uint_as_float(r[k]);
-        // BD columns 0-63 of this warp's window into the row's ring.
         float* ring = stage + lane * ST_STRIDE;
         auto to_ring = [&](int slot) {
           float4* dst = reinterpret_cast<float4*>(ring + slot);
@@ -452,56 +452,71 @@ __global__ void __launch_bounds__(att::THREADS, 1)
             dst[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
                                  __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
         };
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(tl + COL_BD + wcol + 32 * c, r);
-          tmem_wait_ld();
-          to_ring(32 * c);
-        }
-        // Scores: content + shifted position term, scaled into the base-2 domain. Key jj
-        // reads window column 31 - lane + jj: columns 0-62 for the first 32 keys; then
-        // columns 64-95 take ring slots 0-31 (each lane's ring is its own row), and the
-        // last 32 keys read column x at slot x % 64.
-        const float* crow = cband + (31 - lane);
-        float mx = -INFINITY;
-#pragma unroll
-        for (int jj = 0; jj < TK / 2; ++jj) {
-          const float v = (sc[jj] + ring[31 - lane + jj] + crow[jj]) * SCALE_LOG2;
-          sc[jj] = k0 + jj < it.T ? v : -INFINITY;
-          mx = fmaxf(mx, sc[jj]);
-        }
+        to_ring(0);
+        tmem_ld32(tl + COL_BD + wcol + 32, r);
+        tmem_wait_ld();
+        to_ring(32);
         tmem_ld32(tl + COL_BD + wcol + 64, r);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->sbd_empty);  // S and BD read: the next tile's may go
-        to_ring(0);
-        const float* lo = ring + (31 - lane);  // window column x = 31 - lane + jj below 64: slot x
-        const float* hi = lo - 64;              // x of 64 and above: slot x - 64
+        // Scores: content + shifted position terms. Key jj reads window column
+        // 31 - lane + jj: columns 0-62 for the first 32 keys; then columns 64-95 take ring
+        // slots 0-31 (each lane's ring is its own row), and the last 32 keys read column x
+        // at slot x % 64. Keys at or past the clip's end (last tile only) score -inf. The
+        // maxima run in four independent chains.
+        const int lim = it.T - k0;  // keys of this tile inside the clip
+        const bool partial = lim < TK;
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        const float* row_lo = ring + (31 - lane);
+        const float* crow = cband + (31 - lane);
 #pragma unroll
-        for (int jj = TK / 2; jj < TK; ++jj) {
-          const float b = jj >= 33 + lane ? hi[jj] : lo[jj];
-          const float v = (sc[jj] + b + crow[jj]) * SCALE_LOG2;
-          sc[jj] = k0 + jj < it.T ? v : -INFINITY;
-          mx = fmaxf(mx, sc[jj]);
+        for (int jj = 0; jj < TK / 2; ++jj) {
+          float v = __uint_as_float(s0[jj]) + row_lo[jj] + crow[jj];
+          if (partial && jj >= lim) v = -INFINITY;
+          s0[jj] = __float_as_uint(v);
+          mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
         }
-        // The running max moves only when the row max grows by more than 8 (a factor 256 in
-        // the exponentials, which bf16 P and the fp32 sums hold exactly): O is rescaled far
-        // less often, and the final O / l is the same for any reference max.
+        to_ring(0);  // slots 0-31 are only this lane's row: its reads above are done
+        const float* hi = row_lo - 64;  // x of 64 and above: slot x - 64
+#pragma unroll
+        for (int jj = 0; jj < TK / 2; ++jj) {
+          const int kk = TK / 2 + jj;
+          float v = __uint_as_float(s1[jj]) + (kk >= 33 + lane ? hi[kk] : row_lo[kk]) + crow[kk];
+          if (partial && kk >= lim) v = -INFINITY;
+          s1[jj] = __float_as_uint(v);
+          mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+        }
+        // In the base-2 exponent domain (scores times log2(e) / sqrt(128)). The running
+        // max moves only when the row max grows by more than 8 (a factor 256 in the
+        // exponentials, which bf16 P and the fp32 sums hold exactly): O is rescaled far less
+        // often, and the final O / l is the same for any reference max.
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * SCALE_LOG2;
         float corr = 1.0f;
         if (mx > m_run + 8.0f) {
-          corr = exp2f(m_run - mx);
+          corr = ex2_approx(m_run - mx);
           m_run = mx;
         }
         const float m_new = m_run;
-        float sum = 0.f;
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int jj = 0; jj < TK; jj += 2) {
-          const float p0 = exp2f(sc[jj] - m_new), p1 = exp2f(sc[jj + 1] - m_new);
-          sum += p0 + p1;
+        for (int jj = 0; jj < TK / 2; jj += 2) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(s0[jj]), SCALE_LOG2, -m_new));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(s0[jj + 1]), SCALE_LOG2, -m_new));
+          sum4[(jj >> 1) & 1] += p0 + p1;
           __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
           r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
         }
+#pragma unroll
+        for (int jj = 0; jj < TK / 2; jj += 2) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(s1[jj]), SCALE_LOG2, -m_new));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(s1[jj + 1]), SCALE_LOG2, -m_new));
+          sum4[2 + ((jj >> 1) & 1)] += p0 + p1;
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+          r[16 + (jj >> 1)] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
         l_run = l_run * corr + sum;
         if (j > 0) {
           if (!att_warp_wait(&bars->o_done, (g - 1) & 1, err, abort)) {

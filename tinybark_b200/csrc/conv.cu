@@ -40,14 +40,14 @@ __global__ void __launch_bounds__(256, 2) depthwise_silu_kernel(const T* __restr
                                                              const float* __restrict__ b,
                                                              const int* __restrict__ row_clip,
                                                              const int* __restrict__ off, int rows, T* __restrict__ y) {
-  grid_dep_wait();
-  grid_dep_launch();
   const int c = (blockIdx.y * 256 + threadIdx.x) * 2;
   const int r0 = blockIdx.x * DW_ROWS;
   float ta[TB_KERNEL], tb[TB_KERNEL];
 #pragma unroll
   for (int k = 0; k < TB_KERNEL; ++k) ta[k] = w[c * TB_KERNEL + k], tb[k] = w[(c + 1) * TB_KERNEL + k];
   const float ba = b[c], bb = b[c + 1];
+  grid_dep_wait();  // the taps above are weights: read before the predecessor ends
+  grid_dep_launch();
   float ia[DW_ROWS + 2 * DW_HALO], ib[DW_ROWS + 2 * DW_HALO];
 #pragma unroll
   for (int i = 0; i < DW_ROWS + 2 * DW_HALO; ++i) {
@@ -204,6 +204,59 @@ __global__ void __launch_bounds__(DWS_THREADS, 1)
   }
 }
 
+// bf16 for few rows (a batch of one or two clips, where the streaming kernel would run
+// a handful of CTAs): a CTA per 8 output frames and 256 channels, the frames read
+// straight from global memory, the taps and bias loaded before waiting on the
+// predecessor. The arithmetic is the streaming kernel's, operation for operation, so a
+// clip's output does not depend on the batch it runs in.
+constexpr int DWQ_R = 8, DWQ_THREADS = 128;
+
+__global__ void __launch_bounds__(DWQ_THREADS) depthwise_small_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                      const float* __restrict__ w,
+                                                                      const float* __restrict__ b,
+                                                                      const int* __restrict__ row_clip,
+                                                                      const int* __restrict__ off, int rows,
+                                                                      __nv_bfloat16* __restrict__ y) {
+  const int c0 = (blockIdx.y * DWQ_THREADS + threadIdx.x) * 2;
+  float2 wk[TB_KERNEL];
+#pragma unroll
+  for (int k = 0; k < TB_KERNEL; ++k) wk[k] = make_float2(w[c0 * TB_KERNEL + k], w[(c0 + 1) * TB_KERNEL + k]);
+  const float2 bias0 = make_float2(b[c0], b[c0 + 1]);
+  grid_dep_wait();
+  grid_dep_launch();
+  const int r0 = blockIdx.x * DWQ_R;
+  float2 win[DWQ_R + 2 * DW_HALO];  // frames r0-4 .. r0+R+3, zero outside [0, rows)
+#pragma unroll
+  for (int i = 0; i < DWQ_R + 2 * DW_HALO; ++i) {
+    const int r = r0 - DW_HALO + i;
+    win[i] = (r >= 0 && r < rows)
+                 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + (long long)r * TB_HIDDEN + c0))
+                 : make_float2(0.f, 0.f);
+  }
+  const bool interior = r0 >= DW_HALO && r0 + DWQ_R + DW_HALO <= rows &&
+                        row_clip[r0 - DW_HALO] == row_clip[r0 + DWQ_R + DW_HALO - 1];
+#pragma unroll
+  for (int o = 0; o < DWQ_R; ++o) {
+    const int r = r0 + o;
+    if (!interior && r >= rows) break;
+    float2 a0 = bias0;
+    if (interior) {
+#pragma unroll
+      for (int q = 0; q < TB_KERNEL; ++q) a0 = fma2(wk[q], win[o + q], a0);
+    } else {
+      const int clip = row_clip[r];
+      const int lo = off[clip] - r, hi = off[clip + 1] - r;  // valid tap offsets: lo <= q-4 < hi
+#pragma unroll
+      for (int q = 0; q < TB_KERNEL; ++q) {
+        const int d = q - DW_HALO;
+        if (d >= lo && d < hi) a0 = fma2(wk[q], win[o + q], a0);
+      }
+    }
+    a0 = fast_silu2(a0);
+    *reinterpret_cast<uint32_t*>(y + (long long)r * TB_HIDDEN + c0) = pack_bf16x2(a0.x, a0.y);
+  }
+}
+
 int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, const tb_batch& bt, void* out, int* err,
                    cudaStream_t stream) {
   const int rows = bt.t3_total;
@@ -221,6 +274,12 @@ int conv_depthwise(int dtype, const void* glu, const float* w, const float* b, c
       configured[dev] = true;
     }
     const int tiles = (rows + DWS_R - 1) / DWS_R;
+    if (tiles < sm_budget()) {
+      dim3 grid((rows + DWQ_R - 1) / DWQ_R, TB_HIDDEN / 2 / DWQ_THREADS);
+      return launch_pdl(depthwise_small_kernel, grid, DWQ_THREADS, 0, stream,
+                        reinterpret_cast<const __nv_bfloat16*>(glu), w, b, bt.t3_clip, bt.t3_off, rows,
+                        reinterpret_cast<__nv_bfloat16*>(out));
+    }
     const int grid = std::min(tiles, sm_budget());
     return launch_pdl(depthwise_stream_kernel, grid, DWS_THREADS, DWS_SMEM, stream, reinterpret_cast<const __nv_bfloat16*>(glu),
                       w, b, bt.t3_clip, bt.t3_off, rows, reinterpret_cast<__nv_bfloat16*>(out), err);

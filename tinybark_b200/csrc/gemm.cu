@@ -67,14 +67,30 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
+  const int n_tiles = N / BN, kb_count = K / C::BK / splits;
+  // W holds weights, never written by the predecessor kernel: for a few rows (a batch of
+  // one or two clips, where a launch is mostly latency) and a row count fixed at launch,
+  // the producer starts the weight copies of its first item's first stages before waiting
+  // on the predecessor (the A copies of those stages follow after the wait). Each such
+  // stage's `full` barrier expects the weight bytes now, and the A bytes with its arrival.
+  int pre = 0;
+  if (warp == 0 && lane == 0 && !e.rows && M <= 2 * C::BM &&
+      (int)blockIdx.x < (M + C::BM - 1) / C::BM * n_tiles * splits) {
+    prefetch_tmap(&tw);
+    const int t = blockIdx.x, nt = (t / splits) % n_tiles, kb0 = (t % splits) * kb_count;
+    pre = kb_count < C::STAGES ? kb_count : C::STAGES;
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_expect_tx_only(&bars->full[kb], C::B_BYTES);
+      tma_load_2d(smem + kb * C::STAGE_BYTES + C::A_BYTES, &tw, &bars->full[kb], (kb0 + kb) * C::BK, nt * BN);
+    }
+  }
   grid_dep_wait();
   grid_dep_launch();
 
   if (e.rows) M = min(M, *e.rows);
   // Work item t: output tile t / splits, K range t % splits of `splits` equal ranges (split
   // K only with the EPI_RESIDUAL_SPLIT epilogue, whose atomic adds sum the ranges).
-  const int m_tiles = (M + C::BM - 1) / C::BM, n_tiles = N / BN, tiles = m_tiles * n_tiles * splits,
-            kb_count = K / C::BK / splits;
+  const int m_tiles = (M + C::BM - 1) / C::BM, tiles = m_tiles * n_tiles * splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -92,13 +108,22 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           uint8_t* sa = smem + s * C::STAGE_BYTES;
-          mbar_expect_tx(&bars->full[s], C::STAGE_BYTES);
-          tma_load_2d(sa, &ta, &bars->full[s], (kb0 + kb) * C::BK, mt * C::BM);
-          tma_load_2d(sa + C::A_BYTES, &tw, &bars->full[s], (kb0 + kb) * C::BK, nt * BN);
+          if (issued < pre) {  // the weights of this stage are on their way already
+            mbar_expect_tx(&bars->full[s], C::A_BYTES);
+            tma_load_2d(sa, &ta, &bars->full[s], (kb0 + kb) * C::BK, mt * C::BM);
+          } else {
+            mbar_expect_tx(&bars->full[s], C::STAGE_BYTES);
+            tma_load_2d(sa, &ta, &bars->full[s], (kb0 + kb) * C::BK, mt * C::BM);
+            tma_load_2d(sa + C::A_BYTES, &tw, &bars->full[s], (kb0 + kb) * C::BK, nt * BN);
+          }
           ++issued;
           if (++s == C::STAGES) s = 0, ph ^= 1;
         }
       }
+      // Stages whose weights were prefetched but whose A copy was never issued (the loop
+      // was abandoned): their arrival completes them once the weights land.
+      for (long long i = issued; i < pre; ++i) mbar_arrive(&bars->full[i]);
+      if (issued < pre) issued = pre, ok = false;
       if (!ok) {
         // Let the copies already in flight land before the CTA exits.
         long long back = issued < C::STAGES ? issued : C::STAGES;

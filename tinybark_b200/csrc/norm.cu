@@ -14,7 +14,10 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ void ln_row(float4 (&v)[8], const float* w, const float* b, int lane) {
+// Normalizes the row held in v (this lane's 32 values); Affine gives the parameters of
+// column group i (from registers, or loaded on use).
+template <typename Affine>
+__device__ __forceinline__ void ln_row(float4 (&v)[8], Affine&& affine) {
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
@@ -28,8 +31,8 @@ __device__ __forceinline__ void ln_row(float4 (&v)[8], const float* w, const flo
   const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / TB_HIDDEN) + 1e-5f);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int c = (i * 32 + lane) * 4;
-    float4 g = load4(w + c), bb = load4(b + c);
+    float4 g, bb;
+    affine(i, g, bb);
     v[i].x = (v[i].x - mean) * inv * g.x + bb.x;
     v[i].y = (v[i].y - mean) * inv * g.y + bb.y;
     v[i].z = (v[i].z - mean) * inv * g.z + bb.z;
@@ -37,27 +40,48 @@ __device__ __forceinline__ void ln_row(float4 (&v)[8], const float* w, const flo
   }
 }
 
-template <typename OutT>
+// PRE (small row counts, where a launch is mostly latency): the first norm's parameters
+// (weights, never written by a predecessor) are loaded before waiting on the predecessor
+// kernel, at the cost of registers (and so of the blocks per SM the large launches need).
+template <typename OutT, bool PRE>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                         const float* __restrict__ b, float* x_out,
                                                         const float* __restrict__ w2, const float* __restrict__ b2,
                                                         OutT* y, int rows) {
-  grid_dep_wait();
-  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  float4 pg[PRE ? 8 : 1], pb[PRE ? 8 : 1];
+  if constexpr (PRE) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pg[i] = load4(w + (i * 32 + lane) * 4);
+      pb[i] = load4(b + (i * 32 + lane) * 4);
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
   if (row >= rows) return;
   const float* xr = x + (long long)row * TB_HIDDEN;
   float4 v[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = load4(xr + (i * 32 + lane) * 4);
-  ln_row(v, w, b, lane);
+  auto loaded = [&](const float* wp, const float* bp) {
+    return [=](int i, float4& g, float4& bb) {
+      g = load4(wp + (i * 32 + lane) * 4);
+      bb = load4(bp + (i * 32 + lane) * 4);
+    };
+  };
+  if constexpr (PRE) {
+    ln_row(v, [&](int i, float4& g, float4& bb) { g = pg[i], bb = pb[i]; });
+  } else {
+    ln_row(v, loaded(w, b));
+  }
   if (x_out) {
     float* xo = x_out + (long long)row * TB_HIDDEN;
 #pragma unroll
     for (int i = 0; i < 8; ++i) store4(xo + (i * 32 + lane) * 4, v[i].x, v[i].y, v[i].z, v[i].w);
   }
-  if (w2) ln_row(v, w2, b2, lane);
+  if (w2) ln_row(v, loaded(w2, b2));
   OutT* yr = y + (long long)row * TB_HIDDEN;
 #pragma unroll
   for (int i = 0; i < 8; ++i) store4(yr + (i * 32 + lane) * 4, v[i].x, v[i].y, v[i].z, v[i].w);
@@ -68,12 +92,18 @@ int layernorm(const float* x, const float* w, const float* b, float* x_out, cons
   if (rows <= 0) return TB_OK;
   if (!x || !w || !b || !y || (w2 && (!b2 || !x_out))) return TB_ERR_ARG;
   dim3 grid((rows + 7) / 8);
-  if (y_dtype == TB_BF16)
-    return launch_pdl(layernorm_kernel<__nv_bfloat16>, grid, 256, 0, stream, x, w, b, x_out, w2, b2,
-                      reinterpret_cast<__nv_bfloat16*>(y), rows);
-  if (y_dtype == TB_F32)
-    return launch_pdl(layernorm_kernel<float>, grid, 256, 0, stream, x, w, b, x_out, w2, b2,
-                      reinterpret_cast<float*>(y), rows);
+  const bool pre = (int)grid.x <= sm_count();
+  if (y_dtype == TB_BF16) {
+    auto* yo = reinterpret_cast<__nv_bfloat16*>(y);
+    return pre ? launch_pdl(layernorm_kernel<__nv_bfloat16, true>, grid, 256, 0, stream, x, w, b, x_out, w2, b2, yo, rows)
+               : launch_pdl(layernorm_kernel<__nv_bfloat16, false>, grid, 256, 0, stream, x, w, b, x_out, w2, b2, yo,
+                            rows);
+  }
+  if (y_dtype == TB_F32) {
+    auto* yo = reinterpret_cast<float*>(y);
+    return pre ? launch_pdl(layernorm_kernel<float, true>, grid, 256, 0, stream, x, w, b, x_out, w2, b2, yo, rows)
+               : launch_pdl(layernorm_kernel<float, false>, grid, 256, 0, stream, x, w, b, x_out, w2, b2, yo, rows);
+  }
   return TB_ERR_ARG;
 }
 
