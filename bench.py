@@ -64,7 +64,7 @@ def args_parser():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-config0", action="store_true", help="skip the batch-1 fp32 end-to-end line")
     p.add_argument("--micro", action="store_true", help="per-kernel microbenchmarks at encoder shapes")
-    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,mx,conv,mhsa,decode,decode_loop,batch1,longform,load,text)")
+    p.add_argument("--only", default="", help="--micro: comma-separated cases (layernorm,ffn,mx,conv,mhsa,decode,decode_loop,batch1,longform,load,text; config0 only by name)")
     p.add_argument("--rows", default="125,4000,32000", help="--micro: B*T values")
     p.add_argument("--lengths", default="125,375,1500", help="--micro: T values of the attention cases")
     p.add_argument("--micro-dtypes", default="bf16,fp32")
@@ -687,6 +687,8 @@ def run_micro(args):
         run_decode_loop(args, dev)
     if want("batch1"):
         run_batch1(args, dev)
+    if "config0" in only:
+        print(json.dumps({"kernel": "config0_fp32", **run_config0(args, *weights(args.layers))}), flush=True)
     if want("longform"):
         run_longform(args, dev, tflops)
     if want("load"):

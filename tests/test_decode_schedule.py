@@ -2,9 +2,10 @@
 runs (csrc/decode_tiles.cuh compiled into a host program): in every GEMM phase, for every
 row count and grid size, each tile of each GEMM runs exactly once; a CTA's tiles come
 without gaps (once it has none, it has no more); no tile is larger than the ring stage its
-CTA cuts for the phase; and with layer 1 split, its tile t runs on CTA t both in LSTM and
-in the PROJ phase before it (the accumulator stays on that SM), as that CTA's last tile of
-PROJ."""
+CTA cuts for the phase; with layer 1 split, its tile t runs on CTA t both in LSTM and in
+the PROJ phase before it (the accumulator stays on that SM), as that CTA's last tile of
+PROJ; and every next-P0 tile runs once, in LSTM or (the surplus beyond one per free CTA)
+in PROJ."""
 
 import shutil
 import subprocess
@@ -33,10 +34,11 @@ int main() {
           if (split && lstm1_tiles(mtiles * 128) >= G) continue;  // the host splits only below the grid
           const int rows = part ? mtiles * 128 - 77 : mtiles * 128;
           const int kinds[] = {P_JOINT, P_LSTM, P_PROJ};
+          std::map<std::tuple<int, int, int>, int> pre0_seen;  // next-P0 tiles, in LSTM or PROJ
           for (int kind : kinds) {
             std::map<std::tuple<int, int, int>, int> seen;
             for (int cta = 0; cta < G; ++cta) {
-              const int sg = phase_stage_gemm(kind, split, rows, cta);
+              const int sg = phase_stage_gemm(kind, split, rows, cta, G);
               bool ended = false;
               int last = -1;
               for (int k = 0; k < 64; ++k) {
@@ -52,7 +54,10 @@ int main() {
                   ++bad, printf("G %d rows %d kind %d: layer-1 tile (%d,%d) on cta %d\n", G, rows, kind, mt, nt, cta);
                 if (last == G_HH1) ++bad, printf("G %d rows %d cta %d: a tile after the W_hh1 product\n", G, rows, cta);
                 last = g;
-                ++seen[std::make_tuple(g, mt, nt)];
+                if (g == G_PRE0)
+                  ++pre0_seen[std::make_tuple(g, mt, nt)];
+                else
+                  ++seen[std::make_tuple(g, mt, nt)];
               }
             }
             std::map<std::tuple<int, int, int>, int> want;
@@ -61,7 +66,7 @@ int main() {
                 for (int nt = 0; nt < gemm_n(g) / gemm_bn(g); ++nt) want[std::make_tuple(g, mt, nt)] = 1;
             };
             if (kind == P_JOINT) add(G_JOINT);
-            if (kind == P_LSTM) add(G_LSTM1), add(G_PRE0);
+            if (kind == P_LSTM) add(G_LSTM1);
             if (kind == P_PROJ) {
               add(G_PROJ);
               if (split) add(G_HH1);
@@ -71,6 +76,20 @@ int main() {
                             rows, kind, seen.size(), want.size());
             ++checked;
           }
+          std::map<std::tuple<int, int, int>, int> pre0_want;
+          for (int mt = 0; mt < mtiles; ++mt)
+            for (int nt = 0; nt < gemm_n(G_PRE0) / gemm_bn(G_PRE0); ++nt) pre0_want[std::make_tuple(G_PRE0, mt, nt)] = 1;
+          if (pre0_seen != pre0_want)
+            ++bad, printf("G %d split %d rows %d: %zu next-P0 tiles run, %zu expected (or some twice)\n", G, split, rows,
+                          pre0_seen.size(), pre0_want.size());
+          // With the surplus P0 tiles moved into PROJ, no CTA runs two of them in LSTM.
+          if (split && p0_in_proj(mtiles, G))
+            for (int cta = 0; cta < G; ++cta) {
+              int n0 = 0, g, mt, nt;
+              for (int k = 0; k < 64; ++k)
+                if (phase_tile(P_LSTM, rows, cta, G, k, split, g, mt, nt) && g == G_PRE0) ++n0;
+              if (n0 > 1) ++bad, printf("G %d rows %d cta %d: %d next-P0 tiles in LSTM\n", G, rows, cta, n0);
+            }
         }
   printf("checked %d phases, %d problems\n", checked, bad);
   return bad ? 1 : 0;

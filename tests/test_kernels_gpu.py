@@ -80,16 +80,17 @@ def test_gemm_silu_residual_relu(L, dtype, err):
     assert max_rel(out.float().cpu(), torch.relu(ref + bias.double()).cpu()) < TOL[dtype]
 
 
-@pytest.mark.parametrize("m,n,k", [(125, 1024, 4096), (7, 1024, 1024), (250, 1024, 1024)])
-def test_gemm_residual_split_k_small_m(L, err, m, n, k):
-    """bf16 residual GEMMs of a few rows (one clip) split K over more SMs, the partial
-    products added to the fp32 residual atomically: within the residual tolerance of the
-    float64 reference."""
-    a, w, ref = operands(L.BF16, m, n, k, seed=5)
+@pytest.mark.parametrize("dtype", [0, 1])
+@pytest.mark.parametrize("m,n,k", [(125, 1024, 4096), (7, 1024, 1024), (250, 1024, 1024), (130, 1024, 1024)])
+def test_gemm_residual_split_k_small_m(L, err, dtype, m, n, k):
+    """Residual GEMMs of a few rows (one clip) split K over more SMs, the partial products
+    added to the fp32 residual atomically (bf16 tensor-core and fp32 CUDA-core kernels):
+    within the residual tolerance of the float64 reference."""
+    a, w, ref = operands(dtype, m, n, k, seed=5)
     res = torch.randn(m, n, device="cuda")
     expect = res.double() + 0.5 * ref
-    gemm(L, L.BF16, a, w, L.Epilogue(kind=L.EPI_RESIDUAL, out=res.data_ptr(), ldo=n, alpha=0.5), err)
-    assert max_rel(res.cpu(), expect.cpu()) < TOL[L.BF16] / 10
+    gemm(L, dtype, a, w, L.Epilogue(kind=L.EPI_RESIDUAL, out=res.data_ptr(), ldo=n, alpha=0.5), err)
+    assert max_rel(res.cpu(), expect.cpu()) < TOL[dtype] / 10
 
 
 @pytest.mark.parametrize("m", [2100, 2500])

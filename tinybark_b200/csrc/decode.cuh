@@ -95,58 +95,68 @@ __device__ __forceinline__ void lane_init(const DecodeWs& w, const T* __restrict
   }
 }
 
-// One iteration of the greedy loop for lane l (one warp, lane 0 does the work): reads
-// the joint's argmax keys (and clears them for the next joint), then blank ->
-// frame += max(d, 1); otherwise emit, stop on EOS, else frame += d and the LSTM steps on
-// the token; the lane stops when frame >= valid or after cap[l] iterations. On every
-// lane of the warp: returns whether lane l still runs, and sets `step` (the LSTM steps)
-// and `tok`. counts_out (if not NULL) receives the lane's token count when it stops.
+// One iteration of the greedy loop for lane l, run by one thread: reads the joint's argmax
+// keys (and clears them for the next joint), then blank -> frame += max(d, 1); otherwise
+// emit, stop on EOS, else frame += d and the LSTM steps on the token; the lane stops when
+// frame >= valid or after cap[l] iterations. Returns whether lane l still runs; sets
+// `step` (the LSTM steps) and `tok`. counts_out (if not NULL) receives the lane's token
+// count when it stops.
+__device__ __forceinline__ bool lane_scalar(const DecodeWs& w, const int* __restrict__ enc_off,
+                                            const int* __restrict__ cap, int l, int max_cap,
+                                            int* __restrict__ tokens, int& step, int& tok,
+                                            int* __restrict__ counts_out) {
+  step = 0;
+  tok = 0;
+  int running = 0;
+  // Every scalar the step needs, loaded at once (one memory round trip), then used.
+  const int was_done = w.done[l];
+  const unsigned long long k1 = w.keys[l], k2 = w.keys2[l];
+  const int frame0 = w.frame[l], it0 = w.it[l], n0 = w.count[l], cap_l = cap[l];
+  const int off0 = enc_off[l], off1 = enc_off[l + 1];
+  if (!was_done) {
+    tok = argmax_index(k1);
+    int d = argmax_index(k2);  // durations are 0, 1, 2, 3, 4
+    w.keys[l] = 0ull;  // cleared for the next joint
+    w.keys2[l] = 0ull;
+    // The joint always sets both keys; an index out of range can only come from a
+    // key the joint never wrote, and is read as a blank of duration 1.
+    if (tok < 0 || tok >= TB_VOCAB) tok = TB_BLANK;
+    if (d < 0 || d >= TB_DURATIONS) d = 1;
+    const int valid = off1 - off0;
+    int frame = frame0, it = it0 + 1, done = 0, n = n0;
+    if (tok == TB_BLANK) {
+      frame += d > 1 ? d : 1;
+    } else {
+      if (n0 < max_cap) tokens[(long long)l * max_cap + n0] = tok;
+      n = n0 + 1;
+      w.count[l] = n;
+      if (tok == TB_EOS) {
+        done = 1;
+      } else {
+        step = 1;
+        frame += d;
+      }
+    }
+    if (it >= cap_l || frame >= valid) done = 1;
+    if (done) step = 0;
+    if (done && counts_out) counts_out[l] = n;
+    w.frame[l] = frame;
+    w.it[l] = it;
+    w.done[l] = done;
+    w.erow[l] = done ? -1 : off0 + frame;
+    running = !done;
+  }
+  w.mask[l] = step;
+  return running != 0;
+}
+
+// lane_scalar for lane l on one warp (lane 0 does the work); the results on every lane.
 __device__ __forceinline__ bool lane_scalar_step(const DecodeWs& w, const int* __restrict__ enc_off,
                                                  const int* __restrict__ cap, int l, int max_cap,
                                                  int* __restrict__ tokens, int lane, int& step_out, int& tok_out,
                                                  int* __restrict__ counts_out = nullptr) {
   int step = 0, tok = 0, running = 0;
-  if (lane == 0) {
-    // Every scalar the step needs, loaded at once (one memory round trip), then used.
-    const int was_done = w.done[l];
-    const unsigned long long k1 = w.keys[l], k2 = w.keys2[l];
-    const int frame0 = w.frame[l], it0 = w.it[l], n0 = w.count[l], cap_l = cap[l];
-    const int off0 = enc_off[l], off1 = enc_off[l + 1];
-    if (!was_done) {
-      tok = argmax_index(k1);
-      int d = argmax_index(k2);  // durations are 0, 1, 2, 3, 4
-      w.keys[l] = 0ull;  // cleared for the next joint
-      w.keys2[l] = 0ull;
-      // The joint always sets both keys; an index out of range can only come from a
-      // key the joint never wrote, and is read as a blank of duration 1.
-      if (tok < 0 || tok >= TB_VOCAB) tok = TB_BLANK;
-      if (d < 0 || d >= TB_DURATIONS) d = 1;
-      const int valid = off1 - off0;
-      int frame = frame0, it = it0 + 1, done = 0, n = n0;
-      if (tok == TB_BLANK) {
-        frame += d > 1 ? d : 1;
-      } else {
-        if (n0 < max_cap) tokens[(long long)l * max_cap + n0] = tok;
-        n = n0 + 1;
-        w.count[l] = n;
-        if (tok == TB_EOS) {
-          done = 1;
-        } else {
-          step = 1;
-          frame += d;
-        }
-      }
-      if (it >= cap_l || frame >= valid) done = 1;
-      if (done) step = 0;
-      if (done && counts_out) counts_out[l] = n;
-      w.frame[l] = frame;
-      w.it[l] = it;
-      w.done[l] = done;
-      w.erow[l] = done ? -1 : off0 + frame;
-      running = !done;
-    }
-    w.mask[l] = step;
-  }
+  if (lane == 0) running = lane_scalar(w, enc_off, cap, l, max_cap, tokens, step, tok, counts_out) ? 1 : 0;
   step_out = __shfl_sync(0xffffffffu, step, 0);
   tok_out = __shfl_sync(0xffffffffu, tok, 0);
   return __shfl_sync(0xffffffffu, running, 0) != 0;

@@ -14,9 +14,10 @@
 //   q = 1, 2, 3       CELL, LSTM, PROJ of the first prediction step (token blank)
 //   q = 4 + 4i + r    iteration i: r = 0 JOINT, 1 CELL, 2 LSTM, 3 PROJ
 // JOINT  z [lanes x 640] . joint_w^T [8448 x 640] -> per-lane argmax keys (BN = 256)
-// CELL   per lane (one warp): the loop body (lane_scalar_step: token, duration, frame,
-//        stop) and, for a lane that emitted a token, the layer-0 cell from E[token] + P0:
-//        c0 and h0 (into x1[:, :640]), and h1 (hp) copied into x1[:, 640:]
+// CELL   the loop body of each lane (lane_scalar: token, duration, frame, stop; 32 lanes
+//        at a time per warp, one per thread) and, for a lane that emitted a token, the
+//        layer-0 cell from E[token] + P0 (a warp per lane): c0 and h0 (into x1[:, :640]),
+//        and h1 (hp) copied into x1[:, 640:]
 // LSTM   layer 1: x1 . W1^T [2560 x 1280] with the cell in the epilogue (BN = 128), and
 //        on the SMs it leaves idle, the next P0 = x1[:, :640] . W_hh0^T + b0
 // PROJ   hp . dec_proj^T [640 x 640] -> dec, and z = relu(enc[frame] + dec) (BN = 64)
@@ -162,7 +163,10 @@ __device__ __forceinline__ void prefetch_phase_maps(const DecodeTcArgs& args, in
   } else if (kind == P_PROJ) {
     prefetch_tmap(&args.a[G_PROJ]);
     prefetch_tmap(&args.w[G_PROJ]);
-    if (args.split) prefetch_tmap(&args.w[G_HH1]);
+    if (args.split) {
+      prefetch_tmap(&args.w[G_HH1]);
+      prefetch_tmap(&args.w[G_PRE0]);  // next-P0 tiles moved into this phase
+    }
   }
 }
 
@@ -218,22 +222,12 @@ __device__ __forceinline__ void lane_init_tc(const DecodeTcArgs& args, int l, in
   }
 }
 
-// The loop body for lane l (one warp) and, for a lane that emitted a token, layer 0's
-// cell from E[token] + P0 (the first prediction step, iter < 0, feeds the blank token to
-// every lane still running). Returns whether the lane still runs.
-__device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int iter, int lane) {
+// Layer 0's cell for lane l, which steps on token `tok` (one warp): gates E[tok] + P0,
+// c0 and h0 (into x1[:, :640]), and h1 (hp) copied into x1[:, 640:] unless layer 1 is
+// split (it then reads h1 from hp itself) or this is the first prediction step (h1 = 0,
+// as INIT wrote it).
+__device__ __forceinline__ void lane_cell(const DecodeTcArgs& args, int l, int tok, int iter, int lane) {
   const DecodeWs& w = args.ws;
-  int step, tok;
-  bool running;
-  if (iter < 0) {
-    running = !w.done[l];
-    step = running;
-    tok = TB_BLANK;
-  } else {
-    running = lane_scalar_step(w, args.enc_off, args.cap, l, args.max_cap, args.tokens, lane, step, tok, args.counts);
-  }
-  if (!step) return running;
-  const long long L = args.lanes;
   const float4* __restrict__ eg = reinterpret_cast<const float4*>(args.emb_gates + (long long)tok * 4 * TB_PRED);
   const float4* __restrict__ p0 = reinterpret_cast<const float4*>(w.pre0 + (long long)l * 4 * TB_PRED);
   float* __restrict__ c0 = w.c + (long long)l * TB_PRED;
@@ -248,10 +242,8 @@ __device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int i
     gp[k] = p0[u];
     cv[k] = c0[u];
   }
-  // h1 (from the last layer-1 cell) into layer 1's next input; at the first step it is
-  // the zero that INIT wrote there.
   uint2 h1v[TB_PRED / 128];
-  const bool copy_h1 = iter >= 0 && !args.split;  // split layer 1 reads h1 from hp itself
+  const bool copy_h1 = iter >= 0 && !args.split;
   if (copy_h1) {
 #pragma unroll
     for (int k = 0; k < TB_PRED / 128; ++k) h1v[k] = reinterpret_cast<const uint2*>(hp)[k * 32 + lane];
@@ -269,8 +261,37 @@ __device__ __forceinline__ bool lane_cell(const DecodeTcArgs& args, int l, int i
 #pragma unroll
     for (int k = 0; k < TB_PRED / 128; ++k) reinterpret_cast<uint2*>(x1 + TB_PRED)[k * 32 + lane] = h1v[k];
   }
-  (void)L;
-  return running;
+}
+
+// The CELL phase for this warp's lanes l = first + t * stride (t = 0, 1, ...) below `rows`:
+// the loop body of 32 lanes at a time, one lane per thread (their scalars in one memory
+// round trip), then layer 0's cell of each lane that steps, the whole warp on one lane.
+// The first prediction step (iter < 0) feeds the blank token to every lane still running.
+// The row bound of iteration `iter` rises to 1 + the last lane still running.
+__device__ __forceinline__ void cell_phase(const DecodeTcArgs& args, int first, int stride, int rows, int iter,
+                                           int lane, int* bounds) {
+  const DecodeWs& w = args.ws;
+  for (int base = first; base < rows; base += 32 * stride) {
+    const int l = base + lane * stride;
+    int step = 0, tok = TB_BLANK;
+    bool running = false;
+    if (l < rows) {
+      if (iter < 0) {
+        running = !w.done[l];
+        step = running;
+      } else {
+        running = lane_scalar(w, args.enc_off, args.cap, l, args.max_cap, args.tokens, step, tok, args.counts);
+      }
+    }
+    const unsigned run_mask = __ballot_sync(0xffffffffu, running);
+    if (iter >= 0 && run_mask && lane == 31 - __clz(run_mask)) atomicMax(bounds + iter + 1, l + 1);
+    unsigned step_mask = __ballot_sync(0xffffffffu, step != 0);
+    while (step_mask) {
+      const int t = __ffs(step_mask) - 1;
+      step_mask &= step_mask - 1;
+      lane_cell(args, base + t * stride, __shfl_sync(0xffffffffu, tok, t), iter, lane);
+    }
+  }
 }
 
 }  // namespace
@@ -330,7 +351,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;  // no lane runs: the loop is over
         if (p.kind == P_CELL) continue;
-        const int sg = phase_stage_gemm(p.kind, args.split, rows, blockIdx.x), sb = stage_bytes(sg), slots = ring_slots(sg);
+        const int sg = phase_stage_gemm(p.kind, args.split, rows, blockIdx.x, G), sb = stage_bytes(sg), slots = ring_slots(sg);
         // The new cut may overlap stages of the old one: wait until the MMAs have
         // released every stage in use. They complete in issue order, so the release of
         // the stage filled last implies all the others.
@@ -370,7 +391,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         const int rows = phase_rows(p, bounds);
         if (rows <= 0) break;
         if (p.kind == P_CELL) continue;
-        const int sg = phase_stage_gemm(p.kind, args.split, rows, blockIdx.x), sb = stage_bytes(sg), slots = ring_slots(sg);
+        const int sg = phase_stage_gemm(p.kind, args.split, rows, blockIdx.x, G), sb = stage_bytes(sg), slots = ring_slots(sg);
         int s = 0, g, mt, nt;
         for (int k = 0; ok && phase_tile(p.kind, rows, blockIdx.x, G, k, args.split, g, mt, nt); ++k) {
           const int kb_count = gemm_k(g, args.split) / 64;
@@ -458,8 +479,7 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
       if (p.kind == P_INIT) {
         for (int l = blockIdx.x * 4 + ew; l < args.lanes; l += G * 4) lane_init_tc(args, l, lane);
       } else if (p.kind == P_CELL) {
-        for (int l = blockIdx.x * 4 + ew; l < rows; l += G * 4)
-          if (lane_cell(args, l, p.iter, lane) && p.iter >= 0 && lane == 0) atomicMax(bounds + p.iter + 1, l + 1);
+        cell_phase(args, blockIdx.x * 4 + ew, G * 4, rows, p.iter, lane, bounds);
       } else {
         int g, mt, nt;
         for (int k = 0; phase_tile(p.kind, rows, blockIdx.x, G, k, args.split, g, mt, nt); ++k) {

@@ -40,6 +40,14 @@ __host__ __device__ __forceinline__ Phase phase_of(int q) {
   return {r == 0 ? P_JOINT : (r == 1 ? P_CELL : (r == 2 ? P_LSTM : P_PROJ)), i};
 }
 
+// Split layer 1 with more next-P0 tiles than CTAs left over in LSTM: the P0 tiles beyond
+// one per free CTA run in PROJ instead, on the CTAs past the projector's tiles (P0 reads h0,
+// which CELL wrote, and is read in the next CELL), so no CTA runs two of them in LSTM.
+__host__ __device__ constexpr bool p0_in_proj(int mtiles, int G) {
+  return G - mtiles * 20 > 0 && mtiles * 20 > G - mtiles * 20 &&
+         mtiles * 20 - (G - mtiles * 20) <= (G - mtiles * 20) - mtiles * 10;
+}
+
 // The k-th GEMM tile of this CTA in a phase, as (gemm, m tile, n tile); false if none.
 // JOINT and PROJ: tile t = cta + k * gridDim. LSTM: layer 1's tiles (the critical path)
 // go one per CTA, and the next-P0 tiles (half the work each) to the CTAs left over, at
@@ -72,9 +80,15 @@ __host__ __device__ __forceinline__ bool phase_tile(int kind, int rows, int cta,
       nt = t % nc;
       return true;
     }
-    if (k > np || cta >= t1) return false;
-    g = G_HH1;
-    t = cta;
+    if (p0_in_proj(mtiles, G) && cta >= t1 + pt && cta < t1 + pt + (t1 - free)) {
+      if (k != np) return false;
+      g = G_PRE0;
+      t = free + (cta - t1 - pt);
+    } else {
+      if (k > np || cta >= t1) return false;
+      g = G_HH1;
+      t = cta;
+    }
   } else if (split) {
     if (cta < t1) {
       if (k > 0) return false;
@@ -82,7 +96,7 @@ __host__ __device__ __forceinline__ bool phase_tile(int kind, int rows, int cta,
       t = cta;
     } else {
       t = (cta - t1) + k * free;
-      if (t >= t1) return false;
+      if (t >= (p0_in_proj(mtiles, G) ? free : t1)) return false;
       g = G_PRE0;
     }
   } else if (free > 0 && (t1 + free - 1) / free <= 2) {
@@ -107,11 +121,16 @@ __host__ __device__ __forceinline__ bool phase_tile(int kind, int rows, int cta,
 }
 
 // The ring's stage size for this CTA in a GEMM phase (both LSTM-phase GEMMs have
-// BN = 128, and so has the W_hh1 product that joins the projector's phase, on CTAs below
-// layer 1's tile count, when layer 1 is split).
-__host__ __device__ __forceinline__ int phase_stage_gemm(int kind, int split, int rows, int cta) {
+// BN = 128, and so have the W_hh1 product that joins the projector's phase, on CTAs below
+// layer 1's tile count, when layer 1 is split, and next-P0 tiles moved into that phase).
+__host__ __device__ __forceinline__ int phase_stage_gemm(int kind, int split, int rows, int cta, int G) {
   if (kind == P_JOINT) return G_JOINT;
-  if (kind == P_PROJ) return split && cta < lstm1_tiles(rows) ? G_HH1 : G_PROJ;
+  if (kind == P_PROJ) {
+    const int mtiles = (rows + 127) / 128, t1 = lstm1_tiles(rows);
+    if (split && cta < t1) return G_HH1;
+    if (split && p0_in_proj(mtiles, G) && cta >= t1 + mtiles * 10) return G_PRE0;  // BN = 128 tiles
+    return G_PROJ;
+  }
   return G_LSTM1;
 }
 

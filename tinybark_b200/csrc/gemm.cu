@@ -353,6 +353,8 @@ __global__ void __launch_bounds__(Tc2Cfg::THREADS, 1)
 
 constexpr int SG_BM = 128, SG_BN = 128, SG_BK = 16, SG_PAD = 4;
 
+// K range blockIdx.z of gridDim.z equal ranges: with more than one (the residual epilogue
+// only), each range's product is added to the residual rows atomically.
 __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A, long long lda,
                                                        const float* __restrict__ W, int M, int N, int K,
                                                        const tb_epilogue e) {
@@ -364,6 +366,9 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   grid_dep_launch();
   if (e.rows) M = min(M, *e.rows);
   if (m0 >= M) return;
+  const int k_len = K / gridDim.z, k_base = blockIdx.z * k_len;
+  A += k_base;
+  W += k_base;
   // Loader mapping: rows lr and lr + 64, k offset lk.
   const int lr = tid >> 2, lk = (tid & 3) * 4;
 
@@ -398,8 +403,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   stash(0);
   __syncthreads();
   int buf = 0;
-  for (int k0 = 0; k0 < K; k0 += SG_BK) {
-    const bool more = k0 + SG_BK < K;
+  for (int k0 = 0; k0 < k_len; k0 += SG_BK) {
+    const bool more = k0 + SG_BK < k_len;
     if (more) load(k0 + SG_BK);
 #pragma unroll
     for (int k = 0; k < SG_BK; ++k) {
@@ -436,6 +441,17 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
         am.dur = t2 > am.dur ? t2 : am.dur;
       }
       if (tx == 0 && m < M) am.flush(e, m);
+    }
+    return;
+  }
+  if (gridDim.z > 1) {  // split K: residual rows += alpha * this range's product
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+      if (m >= M) continue;
+      float* r = reinterpret_cast<float*>(e.out) + (long long)m * e.ldo;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(r + n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4), e.alpha * acc[i][j]);
     }
     return;
   }
@@ -685,6 +701,15 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
   }
   if (k % SG_BK || n % SG_BN || lda % 4) return TB_ERR_UNSUPPORTED;
   dim3 grid(n / SG_BN, (m + SG_BM - 1) / SG_BM);
+  // A residual GEMM of a clip or two whose tiles leave most SMs idle splits K (a power of
+  // two up to 16, at least 64 of K per range, at most one CTA per SM). The ranges' sums
+  // land in the order the atomic adds take, so such a GEMM is not bit-reproducible.
+  if (e.kind == TB_EPI_RESIDUAL && !e.rows && m <= 256) {
+    const int sms = sm_budget();
+    while (grid.z < 16 && k % (2 * grid.z * SG_BK) == 0 && k / (2 * (int)grid.z) >= 64 &&
+           (int)(grid.x * grid.y * grid.z * 2) <= sms)
+      grid.z *= 2;
+  }
   return launch_pdl(gemm_f32_kernel, grid, 256, 0, stream, reinterpret_cast<const float*>(a), lda,
                     reinterpret_cast<const float*>(w), m, n, k, e);
 }
