@@ -241,9 +241,9 @@ int tb_layernorm(const float* x, const float* w, const float* b, float* x_out, c
  * A [M, K] (lda elements) times W [N, K] transposed, epilogue `epi`. dtype TB_BF16 runs
  * the tcgen05 tensor-core kernel (K % 64 == 0, N % 256 == 0 or N % 128 == 0); TB_F32 a
  * CUDA-core fp32 kernel (K % 16 == 0, N % 128 == 0). W is read as constant: for M <= 256
- * the bf16 kernel may start reading it before the kernel launched just before it on the
- * stream has finished, so W must not be the output of that kernel (the library's kernels
- * let their successor start early). */
+ * (bf16) or M <= 8 (fp32) the kernel may start reading it before the kernel launched just
+ * before it on the stream has finished, so W must not be the output of that kernel (the
+ * library's kernels let their successor start early). */
 int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue* epi,
             int* err, void* stream);
 /* Large bf16 GEMMs (at least 2048 rows, N % 256 == 0, no run-time row bound, epilogue

@@ -149,6 +149,36 @@ def test_gemm_pairs_match_single_cta(L, err, kind, m):
         assert max_rel(g, wnt.cpu()) < TOL[1]
 
 
+@pytest.mark.parametrize("kind", ["silu", "qkv", "store"])
+def test_gemm_f32_small_tiles_same_bits(L, err, kind):
+    """fp32: a GEMM of a clip or two (125 rows) runs on 64 x 64 tiles, a larger one (300
+    rows) on 128 x 128 tiles; every output sums over K in the same order, so the rows they
+    share come out bit for bit the same, and both match the float64 product."""
+    n = {"silu": 4096, "qkv": 3072, "store": 1024}[kind]
+    k = 1024
+    g = torch.Generator(device="cuda").manual_seed(31)
+    a = torch.randn(300, k, device="cuda", generator=g)
+    w = torch.randn(n, k, device="cuda", generator=g) / k**0.5
+    bias = torch.randn(n, device="cuda", generator=g)
+    u, v = torch.randn(1024, device="cuda"), torch.randn(1024, device="cuda")
+    results = []
+    for m in (125, 300):
+        outs = [torch.full((m, 1024 if kind == "qkv" else n), float("nan"), device="cuda") for _ in range(4)]
+        ep = {"silu": L.Epilogue(kind=L.EPI_SILU, out_dtype=0, out=outs[0].data_ptr(), ldo=n),
+              "store": L.Epilogue(kind=L.EPI_STORE, out_dtype=0, out=outs[0].data_ptr(), ldo=n, bias=bias.data_ptr()),
+              "qkv": L.Epilogue(kind=L.EPI_QKV, out_dtype=0, out=outs[0].data_ptr(), out2=outs[1].data_ptr(),
+                                out3=outs[2].data_ptr(), out4=outs[3].data_ptr(), ldo=1024, bias_u=u.data_ptr(),
+                                bias_v=v.data_ptr())}[kind]
+        gemm(L, 0, a[:m], w, ep, err)
+        results.append([o[:125].cpu() for o in outs[: (4 if kind == "qkv" else 1)]])
+    ref = a[:125].double() @ w.double().T
+    want = {"silu": [F.silu(ref)], "store": [ref + bias.double()],
+            "qkv": [ref[:, :1024] + u.double(), ref[:, :1024] + v.double(), ref[:, 1024:2048], ref[:, 2048:]]}[kind]
+    for x, y, wnt in zip(results[0], results[1], want):
+        assert torch.equal(x, y)
+        assert max_rel(x, wnt.cpu()) < TOL[0]
+
+
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_gemm_glu(L, dtype, err):
     m, n, k = 200, 2048, 256

@@ -464,64 +464,131 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   }
 }
 
+// The same product on 64 x 64 tiles (4 x 4 outputs per thread), for a clip or two, whose
+// 128 x 128 tiles would leave most SMs idle: each output sums over k in the same order
+// as in the kernel above, so the results are the same bits.
+constexpr int SS_BM = 64, SS_BN = 64, SS_BK = 16, SS_PAD = 4;
+
+__global__ void __launch_bounds__(256) gemm_f32_small_kernel(const float* __restrict__ A, long long lda,
+                                                             const float* __restrict__ W, int M, int N, int K,
+                                                             const tb_epilogue e) {
+  __shared__ __align__(16) float As[2][SS_BK][SS_BM + SS_PAD];
+  __shared__ __align__(16) float Ws[2][SS_BK][SS_BN + SS_PAD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * SS_BM, n0 = blockIdx.x * SS_BN;
+  const int lr = tid >> 2, lk = (tid & 3) * 4;  // loader: row lr, k offset lk
+  float4 rw = *reinterpret_cast<const float4*>(W + (long long)(n0 + lr) * K + lk);  // weights: before the wait
+  grid_dep_wait();
+  grid_dep_launch();
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  const int am = m0 + lr;
+  float4 ra = am < M ? *reinterpret_cast<const float4*>(A + (long long)am * lda + lk) : make_float4(0, 0, 0, 0);
+  auto stash = [&](int buf) {
+    As[buf][lk + 0][lr] = ra.x, As[buf][lk + 1][lr] = ra.y, As[buf][lk + 2][lr] = ra.z, As[buf][lk + 3][lr] = ra.w;
+    Ws[buf][lk + 0][lr] = rw.x, Ws[buf][lk + 1][lr] = rw.y, Ws[buf][lk + 2][lr] = rw.z, Ws[buf][lk + 3][lr] = rw.w;
+  };
+  stash(0);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = 0; k0 < K; k0 += SS_BK) {
+    const bool more = k0 + SS_BK < K;
+    if (more) {
+      ra = am < M ? *reinterpret_cast<const float4*>(A + (long long)am * lda + k0 + SS_BK + lk) : make_float4(0, 0, 0, 0);
+      rw = *reinterpret_cast<const float4*>(W + (long long)(n0 + lr) * K + k0 + SS_BK + lk);
+    }
+#pragma unroll
+    for (int k = 0; k < SS_BK; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      const float4 w = *reinterpret_cast<const float4*>(&Ws[buf][k][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+    }
+    if (more) {
+      stash(buf ^ 1);
+      __syncthreads();
+      buf ^= 1;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m < M) epi_group(e, m, n0 + tx * 4, acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// fp32 matrix-vector kernel for a few rows (the fp32 decoder's GEMMs at batch 1-8): each
-// warp takes 4 consecutive output columns (one epilogue group) for every row, reading its
-// 4 weight rows once with 16-byte loads; the rows of A are staged in shared memory. A
-// 128 x 128 tile of the GEMM kernel would compute up to 127 rows of nothing here.
+// fp32 matrix-vector kernel for a few rows (the fp32 decoder's GEMMs at batch 1-8): a CTA
+// of four warps per epilogue group of 4 output columns, warp j taking column n0 + j over
+// all of K for every row. Each lane holds its K / 128 16-byte pieces of the weight row in
+// registers, loaded before waiting on the predecessor kernel (W is weights), so one memory
+// round trip brings the whole row; the rows of A are staged in shared memory. Per column
+// the sum runs in the same order as one warp's (lane l takes k = 4l + 128i, i ascending;
+// a butterfly over the lanes). A 128 x 128 tile of the GEMM kernel would compute up to
+// 127 rows of nothing here.
 
-constexpr int GV_MAX_ROWS = 8, GV_WARPS = 8, GV_MAX_K = 1280;
+constexpr int GV_MAX_ROWS = 8, GV_MAX_K = 1280, GV_THREADS = 128;
 
-__global__ void __launch_bounds__(GV_WARPS * 32) gemv_f32_kernel(const float* __restrict__ A, long long lda,
-                                                                 const float* __restrict__ W, int M, int N, int K,
-                                                                 const tb_epilogue e) {
-  __shared__ __align__(16) float As[GV_MAX_ROWS * GV_MAX_K];
+__global__ void __launch_bounds__(GV_THREADS) gemv_f32_kernel(const float* __restrict__ A, long long lda,
+                                                             const float* __restrict__ W, int M, int N, int K,
+                                                             const tb_epilogue e) {
+  extern __shared__ __align__(16) float As[];  // [M, K], sized by the launch
+  __shared__ float red[GV_MAX_ROWS][4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * 4, n = n0 + warp;
+  float4 w[GV_MAX_K / 128];
+#pragma unroll
+  for (int i = 0; i < GV_MAX_K / 128; ++i) {
+    const int k = i * 128 + lane * 4;
+    w[i] = (n < N && k < K) ? *reinterpret_cast<const float4*>(W + (long long)n * K + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   grid_dep_wait();
   grid_dep_launch();
   if (e.rows) M = min(M, *e.rows);
   if (M <= 0) return;
-  for (int i = threadIdx.x * 4; i < M * K; i += blockDim.x * 4) {
+  for (int i = threadIdx.x * 4; i < M * K; i += GV_THREADS * 4) {
     const int m = i / K, k = i - m * K;
     *reinterpret_cast<float4*>(As + i) = *reinterpret_cast<const float4*>(A + (long long)m * lda + k);
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = (blockIdx.x * GV_WARPS + warp) * 4;
-  if (n >= N) return;
-  float acc[GV_MAX_ROWS][4];
+  float acc[GV_MAX_ROWS];
 #pragma unroll
-  for (int m = 0; m < GV_MAX_ROWS; ++m)
+  for (int m = 0; m < GV_MAX_ROWS; ++m) acc[m] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
-  for (int k = lane * 4; k < K; k += 128) {
-    float4 w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const float4*>(W + (long long)(n + j) * K + k);
+  for (int i = 0; i < GV_MAX_K / 128; ++i) {
+    const int k = i * 128 + lane * 4;
+    if (k >= K) break;
 #pragma unroll
     for (int m = 0; m < GV_MAX_ROWS; ++m) {
       if (m >= M) break;
       const float4 a = *reinterpret_cast<const float4*>(As + m * K + k);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        acc[m][j] = fmaf(a.w, w[j].w, fmaf(a.z, w[j].z, fmaf(a.y, w[j].y, fmaf(a.x, w[j].x, acc[m][j]))));
+      acc[m] = fmaf(a.w, w[i].w, fmaf(a.z, w[i].z, fmaf(a.y, w[i].y, fmaf(a.x, w[i].x, acc[m]))));
     }
   }
 #pragma unroll
   for (int m = 0; m < GV_MAX_ROWS; ++m)
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int o = 16; o; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+  if (lane == 0) {
 #pragma unroll
-      for (int o = 16; o; o >>= 1) acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], o);
-  if (lane != 0) return;
-  for (int m = 0; m < M; ++m) {
-    if (e.kind == TB_EPI_ARGMAX) {
-      ArgmaxAcc am;
+    for (int m = 0; m < GV_MAX_ROWS; ++m) red[m][warp] = acc[m];
+  }
+  __syncthreads();
+  const int m = threadIdx.x;
+  if (m >= M || n0 >= N) return;
+  if (e.kind == TB_EPI_ARGMAX) {
+    ArgmaxAcc am;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) am.add(e, n + j, acc[m][j]);
-      am.flush(e, m);
-    } else {
-      epi_group(e, m, n, acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
-    }
+    for (int j = 0; j < 4; ++j) am.add(e, n0 + j, red[m][j]);
+    am.flush(e, m);
+  } else {
+    epi_group(e, m, n0, red[m][0], red[m][1], red[m][2], red[m][3]);
   }
 }
 
@@ -695,12 +762,16 @@ int gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, i
   if (dtype != TB_F32) return TB_ERR_ARG;
   if (m <= GV_MAX_ROWS && k <= GV_MAX_K && k % 128 == 0 && n % 4 == 0 && lda % 4 == 0 &&
       !(reinterpret_cast<uintptr_t>(a) & 15) && !(reinterpret_cast<uintptr_t>(w) & 15)) {
-    const int cols = GV_WARPS * 4;
-    return launch_pdl(gemv_f32_kernel, dim3((n + cols - 1) / cols), GV_WARPS * 32, 0, stream,
+    // Shared memory for the launch's M rows only (at most 40 KB), so more CTAs share an SM.
+    return launch_pdl(gemv_f32_kernel, dim3(n / 4), GV_THREADS, (size_t)m * k * sizeof(float), stream,
                       reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(w), m, n, k, e);
   }
   if (k % SG_BK || n % SG_BN || lda % 4) return TB_ERR_UNSUPPORTED;
   dim3 grid(n / SG_BN, (m + SG_BM - 1) / SG_BM);
+  if (e.kind != TB_EPI_RESIDUAL && e.kind != TB_EPI_ARGMAX && !e.rows && m <= 256 &&
+      (int)(2 * grid.x * grid.y) <= sm_budget())
+    return launch_pdl(gemm_f32_small_kernel, dim3(n / SS_BN, (m + SS_BM - 1) / SS_BM), 256, 0, stream,
+                      reinterpret_cast<const float*>(a), lda, reinterpret_cast<const float*>(w), m, n, k, e);
   // A residual GEMM of a clip or two whose tiles leave most SMs idle splits K (a power of
   // two up to 16, at least 64 of K per range, at most one CTA per SM). The ranges' sums
   // land in the order the atomic adds take, so such a GEMM is not bit-reproducible.
