@@ -2,7 +2,8 @@
 (log-mel front-end, 24-layer encoder, TDT greedy decode) on the whole-box workload: 4096
 synthetic speech-like clips of 2-30 s (durations uniform, seeded), with seeded random-init
 weights of the Parakeet-TDT-0.6B-v3 architecture, bf16. One process per GPU: the clips are
-dealt to the GPUs longest processing time first (tinybark_b200.dp.deal) and each rank
+dealt to the GPUs in contiguous ranges of the length order, cut where the predicted shard
+times balance (tinybark_b200.dp.deal), and each rank
 transcribes its shard end to end with no collective on the data path (strong scaling: the
 same 4096 clips at every GPU count; one GPU runs them all as one batch).
 
@@ -41,8 +42,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "RTFx (audio-s per wall-s) per box at 1/2/4/8 B200; encoder ms per 10 s clip"
-WORKLOAD = ("whole-box: 4096 synthetic clips 2-30 s (uniform, seeded) dealt to the GPUs longest processing time "
-            "first, packed end to end, front-end + encoder + TDT decode")
+WORKLOAD = ("whole-box: 4096 synthetic clips 2-30 s (uniform, seeded) dealt to the GPUs in contiguous length ranges "
+            "balancing predicted time, packed end to end, front-end + encoder + TDT decode")
 SEED = 4
 CLIPS = 4096
 # Algorithmic work of the greedy loop (tinybark/tinygrad/model.py:162-233): the joint on
