@@ -252,6 +252,48 @@ def test_gemm_argmax(L, dtype, err):
         assert (tok == lt.argmax(1)).all() and (dur == ld.argmax(1)).all()
 
 
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_gemv_f32_few_rows(L, err, m):
+    """fp32 GEMMs of at most 8 rows (the fp32 decoder at batch 1-8) run the matrix-vector
+    kernel (a warp per weight row, the row in registers): STORE with bias, the LSTM cell
+    with a lane mask, and the joint's argmax, each against float64."""
+    a, w, ref = operands(0, m, 640, 640, seed=40 + m)
+    bias = torch.randn(640, device="cuda")
+    out = torch.full((m, 640), float("nan"), device="cuda")
+    gemm(L, 0, a, w, L.Epilogue(kind=L.EPI_STORE, out_dtype=0, out=out.data_ptr(), ldo=640, bias=bias.data_ptr()), err)
+    assert max_rel(out.cpu(), (ref + bias.double()).cpu()) < TOL[0]
+
+    a, w, ref = operands(0, m, 2560, 1280, seed=50 + m)
+    bias = torch.randn(2560, device="cuda")
+    c = torch.randn(m, 640, device="cuda")
+    h = torch.zeros(m, 640, device="cuda")
+    mask = (torch.arange(m, device="cuda") % 2 == 0).int()
+    c0 = c.clone()
+    gemm(L, 0, a, w, L.Epilogue(kind=L.EPI_LSTM, out_dtype=0, bias=bias.data_ptr(), c=c.data_ptr(), h=h.data_ptr(),
+                                mask=mask.data_ptr()), err)
+    g = (ref + bias.double()).view(m, 640, 4)
+    c_new = torch.sigmoid(g[..., 1]) * c0.double() + torch.sigmoid(g[..., 0]) * torch.tanh(g[..., 2])
+    h_new = torch.sigmoid(g[..., 3]) * torch.tanh(c_new)
+    keep = mask.bool()
+    assert max_rel(c[keep].cpu(), c_new[keep].cpu()) < TOL[0]
+    assert max_rel(h[keep].cpu(), h_new[keep].cpu()) < TOL[0]
+    assert torch.equal(c[~keep], c0[~keep])
+
+    split, n = 8256, 8448
+    a, w, ref = operands(0, m, n, 640, seed=60 + m)
+    bias = torch.randn(n, device="cuda")
+    bias[8193:split] = float("-inf")
+    bias[split + 5 :] = float("-inf")
+    keys = torch.zeros(m, dtype=torch.int64, device="cuda")
+    keys2 = torch.zeros(m, dtype=torch.int64, device="cuda")
+    gemm(L, 0, a, w, L.Epilogue(kind=L.EPI_ARGMAX, bias=bias.data_ptr(), keys=keys.data_ptr(), keys2=keys2.data_ptr(),
+                                split=split, split_end=split + 5), err)
+    logits = (ref + bias.double()).cpu().numpy()
+    tok = (0xFFFFFFFF - (keys & 0xFFFFFFFF)).cpu().numpy()
+    dur = (0xFFFFFFFF - (keys2 & 0xFFFFFFFF)).cpu().numpy()
+    assert (tok == logits[:, :split].argmax(1)).all() and (dur == logits[:, split : split + 5].argmax(1)).all()
+
+
 @pytest.mark.parametrize("lanes", [90, 300])
 def test_gemm_argmax_first_index_exact(L, err, lanes):
     """bf16 with small-integer operands and biases: every accumulator and logit is an
