@@ -318,7 +318,8 @@ int tb_selftest_wait(int kind, void* scratch, int* err, void* stream);
 /* Self-test of the epilogues' fast arithmetic (no reference counterpart): y[i] = f(x[i])
  * for n float32 values on the device, f by kind: 0 the Newton reciprocal (x >= 1),
  * 1 sigmoid and 2 SiLU with one special-function operation, 3 and 4 their two-wide forms,
- * 5 the tanh-based sigmoid and 6 the hardware tanh of the LSTM cells. */
+ * 5 the tanh-based sigmoid and 6 the hardware tanh of the LSTM cells, 7 the tanh-based
+ * two-wide SiLU of the FFN-up and depthwise-conv epilogues. */
 int tb_selftest_math(int kind, const float* x, float* y, long long n, void* stream);
 
 size_t tb_decode_workspace_bytes(int dtype, int lanes, int groups);

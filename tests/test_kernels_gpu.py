@@ -648,26 +648,28 @@ def test_fast_math_within_bounds(L):
     """The epilogues' fast arithmetic against float64 (tb_selftest_math): the Newton
     reciprocal over y in [1, 1e30] within 1e-5 relative, the one-MUFU sigmoid and SiLU (and
     their two-wide forms) over x in [-90, 90] within 2e-5 absolute (sigmoid) and relative
-    2e-5 + 1e-30 (SiLU), the tanh-based sigmoid within 5e-4 and the hardware tanh within
-    2^-10 relative plus 1e-6 absolute, each checked against the bound CUDA documents for
-    its approximate instructions."""
+    2e-5 + 1e-30 (SiLU), the tanh-based sigmoid within 5e-4, the tanh-based two-wide SiLU
+    within 2^-11.9 |x| (half the tanh's relative bound on |x / 2|) and the hardware tanh
+    within 2^-10 relative plus 1e-6 absolute, each checked against the bound CUDA documents
+    for its approximate instructions."""
     g = torch.Generator().manual_seed(5)
     n = 1 << 20
     cases = {
         0: torch.exp(torch.rand(n, generator=g, dtype=torch.float64) * 69.0).float(),  # 1 .. 1e30
-        **{k: (torch.rand(n, generator=g, dtype=torch.float64) * 180 - 90).float() for k in (1, 2, 3, 4, 5)},
+        **{k: (torch.rand(n, generator=g, dtype=torch.float64) * 180 - 90).float() for k in (1, 2, 3, 4, 5, 7)},
         6: (torch.rand(n, generator=g, dtype=torch.float64) * 20 - 10).float(),
     }
-    cases[3][-1] = cases[4][-1] = 0.0
+    cases[3][-1] = cases[4][-1] = cases[7][-1] = 0.0
     for kind, x in cases.items():
         xd = x.cuda()
         y = torch.full_like(xd, float("nan"))
-        L.check(L.lib.tb_selftest_math(kind, xd.data_ptr(), y.data_ptr(), n - (kind == 4), stream()), "tb_selftest_math")
+        L.check(L.lib.tb_selftest_math(kind, xd.data_ptr(), y.data_ptr(), n - (kind in (4, 7)), stream()),
+                "tb_selftest_math")
         torch.cuda.synchronize()
         got = y.cpu().double()
         xx = x.double()
         sig = torch.sigmoid(xx)
-        if kind == 4:
+        if kind in (4, 7):
             got, xx, sig = got[:-1], xx[:-1], sig[:-1]
             assert torch.isnan(y[-1].cpu())  # past n: untouched
         if kind == 0:
@@ -678,6 +680,9 @@ def test_fast_math_within_bounds(L):
             assert ((got - xx * sig).abs() <= 2e-5 * (xx * sig).abs() + 1e-30).all(), kind
         elif kind == 5:
             assert (got - sig).abs().max() < 5e-4, kind
+        elif kind == 7:  # h + h tanh(h), h = x / 2: the tanh's 2^-10.987 relative error on |h|
+            ref = xx * sig
+            assert ((got - ref).abs() <= 2.0**-11.9 * xx.abs() + 2.0**-23 * ref.abs() + 1e-30).all(), kind
         else:
             t = torch.tanh(xx)
             assert ((got - t).abs() <= 2.0 ** -10 * t.abs() + 1e-6).all(), kind

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(DWS_THREADS, 1)
         float2 a0 = bias0;
 #pragma unroll
         for (int q = 0; q < TB_KERNEL; ++q) a0 = fma2(wk[q], win[q], a0);
-        a0 = fast_silu2(a0);
+        a0 = silu2_tanh(a0);
         *reinterpret_cast<uint32_t*>(y + (long long)(r0 + o) * TB_HIDDEN + c0) = pack_bf16x2(a0.x, a0.y);
 #pragma unroll
         for (int q = 0; q < TB_KERNEL - 1; ++q) win[q] = win[q + 1];
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(DWS_THREADS, 1)
             const int d = q - DW_HALO;
             if (d >= lo && d < hi) a0 = fma2(wk[q], win[q], a0);
           }
-          a0 = fast_silu2(a0);
+          a0 = silu2_tanh(a0);
           *reinterpret_cast<uint32_t*>(y + (long long)r * TB_HIDDEN + c0) = pack_bf16x2(a0.x, a0.y);
         }
 #pragma unroll
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(DWQ_THREADS) depthwise_small_kernel(const __nv
         if (d >= lo && d < hi) a0 = fma2(wk[q], win[o + q], a0);
       }
     }
-    a0 = fast_silu2(a0);
+    a0 = silu2_tanh(a0);
     *reinterpret_cast<uint32_t*>(y + (long long)r * TB_HIDDEN + c0) = pack_bf16x2(a0.x, a0.y);
   }
 }

@@ -32,13 +32,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// The PTX tanh.approx.f32 instruction (one MUFU operation, about 2^-11 relative error).
-// Used in the bf16 decoder's LSTM cell, whose inputs and outputs are bf16 (2^-8).
-__device__ __forceinline__ float tanh_mufu(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+// sigmoid through tanh_mufu (common.cuh), for the bf16 decoder's LSTM cells, whose inputs
+// and outputs are bf16 (2^-8).
 __device__ __forceinline__ float sigmoid_mufu(float x) { return fmaf(0.5f, tanh_mufu(0.5f * x), 0.5f); }
 
 // Global values an epilogue reads, loaded by each epilogue warp for its 32 rows of a
@@ -191,7 +186,7 @@ __device__ __forceinline__ void epi_chunk(const tb_epilogue& e, const float* sta
     // the stores.
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
-      const float2 lo = fast_silu2(make_float2(v[it].x, v[it].y)), hi = fast_silu2(make_float2(v[it].z, v[it].w));
+      const float2 lo = silu2_tanh(make_float2(v[it].x, v[it].y)), hi = silu2_tanh(make_float2(v[it].z, v[it].w));
       v[it] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
     store_rows4(e, v, row0, sub, n, M);
