@@ -464,29 +464,49 @@ __global__ void __launch_bounds__(att::THREADS, 1)
         // Scores: content + shifted position terms. Key jj reads window column
         // 31 - lane + jj: columns 0-62 for the first 32 keys; then columns 64-95 take ring
         // slots 0-31 (each lane's ring is its own row), and the last 32 keys read column x
-        // at slot x % 64. Keys at or past the clip's end (last tile only) score -inf. The
-        // maxima run in four independent chains.
+        // at slot x & 63 (one load, conflict-free: lane L's slot lands in bank 3L + c).
+        // Keys at or past the clip's end score -inf; only a clip's last tile can have
+        // them, so whole tiles run loops without the test. The maxima run in four
+        // independent chains.
         const int lim = it.T - k0;  // keys of this tile inside the clip
         const bool partial = lim < TK;
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         const float* row_lo = ring + (31 - lane);
         const float* crow = cband + (31 - lane);
+        if (!partial) {
 #pragma unroll
-        for (int jj = 0; jj < TK / 2; ++jj) {
-          float v = __uint_as_float(s0[jj]) + row_lo[jj] + crow[jj];
-          if (partial && jj >= lim) v = -INFINITY;
-          s0[jj] = __float_as_uint(v);
-          mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          for (int jj = 0; jj < TK / 2; ++jj) {
+            const float v = __uint_as_float(s0[jj]) + row_lo[jj] + crow[jj];
+            s0[jj] = __float_as_uint(v);
+            mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < TK / 2; ++jj) {
+            float v = __uint_as_float(s0[jj]) + row_lo[jj] + crow[jj];
+            if (jj >= lim) v = -INFINITY;
+            s0[jj] = __float_as_uint(v);
+            mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          }
         }
         to_ring(0);  // slots 0-31 are only this lane's row: its reads above are done
-        const float* hi = row_lo - 64;  // x of 64 and above: slot x - 64
+        if (!partial) {
 #pragma unroll
-        for (int jj = 0; jj < TK / 2; ++jj) {
-          const int kk = TK / 2 + jj;
-          float v = __uint_as_float(s1[jj]) + (kk >= 33 + lane ? hi[kk] : row_lo[kk]) + crow[kk];
-          if (partial && kk >= lim) v = -INFINITY;
-          s1[jj] = __float_as_uint(v);
-          mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          for (int jj = 0; jj < TK / 2; ++jj) {
+            const int kk = TK / 2 + jj;
+            const float v = __uint_as_float(s1[jj]) + ring[(31 - lane + kk) & 63] + crow[kk];
+            s1[jj] = __float_as_uint(v);
+            mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < TK / 2; ++jj) {
+            const int kk = TK / 2 + jj;
+            float v = __uint_as_float(s1[jj]) + ring[(31 - lane + kk) & 63] + crow[kk];
+            if (kk >= lim) v = -INFINITY;
+            s1[jj] = __float_as_uint(v);
+            mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          }
         }
         // In the base-2 exponent domain (scores times log2(e) / sqrt(128)). The running
         // max moves only when the row max grows by more than 8 (a factor 256 in the
