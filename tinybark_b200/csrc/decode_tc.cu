@@ -520,9 +520,12 @@ __global__ void __launch_bounds__(192, 1) decode_tc_kernel(const __grid_constant
         }
       }
       // The phase's writes, visible to the other CTAs' loads and TMA reads, then one
-      // arrival for this CTA.
+      // arrival for this CTA: each writer orders its stores before later async-proxy
+      // reads, the named barrier orders every epilogue thread's stores before thread 0's
+      // GPU-scope fence, and that fence (cumulative over what the barrier ordered) before
+      // the arrival. A fence in every thread as well costs ~2 us per iteration and orders
+      // nothing more (the same pattern as a cooperative grid sync).
       fence_proxy_async_global();
-      __threadfence();
       if (epi_bar_or(!ok)) {
         *abort = 1;
         break;
