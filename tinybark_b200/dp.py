@@ -42,10 +42,10 @@ DEC_FLOP_PER_ITER = 24.6e6
 
 # Predicted seconds on one B200, bf16, measured: the front-end and encoder at 0.88 PFLOP/s
 # of clip_encoder_flop (154 ms for a 512-clip batch of 2-30 s clips), and one iteration of
-# the persistent decoder at 27.3 us plus 27.9 ns per running lane (a least-squares fit to
-# the whole greedy loop of 512, 1024, 2048 and 4096 lanes: 126, 165, 216, 327 ms).
+# the persistent decoder at 25.1 us plus 27.9 ns per running lane (a least-squares fit to
+# the whole greedy loop of 512, 1024, 2048 and 4096 lanes: 118, 157, 208, 319 ms).
 ENC_S_PER_FLOP = 1.0 / 0.88e15
-ITER_S = 27.3e-6
+ITER_S = 25.1e-6
 ITER_S_PER_LANE = 27.9e-9
 
 
