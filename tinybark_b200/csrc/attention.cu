@@ -475,10 +475,12 @@ __global__ void __launch_bounds__(att::THREADS, 1)
         const float* crow = cband + (31 - lane);
         if (!partial) {
 #pragma unroll
-          for (int jj = 0; jj < TK / 2; ++jj) {
-            const float v = __uint_as_float(s0[jj]) + row_lo[jj] + crow[jj];
-            s0[jj] = __float_as_uint(v);
-            mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+          for (int jj = 0; jj < TK / 2; jj += 2) {
+            const float v0 = __uint_as_float(s0[jj]) + row_lo[jj] + crow[jj];
+            const float v1 = __uint_as_float(s0[jj + 1]) + row_lo[jj + 1] + crow[jj + 1];
+            s0[jj] = __float_as_uint(v0);
+            s0[jj + 1] = __float_as_uint(v1);
+            mx4[(jj >> 1) & 3] = max3(mx4[(jj >> 1) & 3], v0, v1);
           }
         } else {
 #pragma unroll
@@ -492,11 +494,13 @@ __global__ void __launch_bounds__(att::THREADS, 1)
         to_ring(0);  // slots 0-31 are only this lane's row: its reads above are done
         if (!partial) {
 #pragma unroll
-          for (int jj = 0; jj < TK / 2; ++jj) {
+          for (int jj = 0; jj < TK / 2; jj += 2) {
             const int kk = TK / 2 + jj;
-            const float v = __uint_as_float(s1[jj]) + ring[(31 - lane + kk) & 63] + crow[kk];
-            s1[jj] = __float_as_uint(v);
-            mx4[jj & 3] = fmaxf(mx4[jj & 3], v);
+            const float v0 = __uint_as_float(s1[jj]) + ring[(31 - lane + kk) & 63] + crow[kk];
+            const float v1 = __uint_as_float(s1[jj + 1]) + ring[(32 - lane + kk) & 63] + crow[kk + 1];
+            s1[jj] = __float_as_uint(v0);
+            s1[jj + 1] = __float_as_uint(v1);
+            mx4[(jj >> 1) & 3] = max3(mx4[(jj >> 1) & 3], v0, v1);
           }
         } else {
 #pragma unroll
@@ -519,19 +523,21 @@ __global__ void __launch_bounds__(att::THREADS, 1)
           m_run = mx;
         }
         const float m_new = m_run;
+        // Two scores per packed FMA (each half rounds as fmaf would).
+        const float2 scale2 = make_float2(SCALE_LOG2, SCALE_LOG2), negm2 = make_float2(-m_new, -m_new);
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int jj = 0; jj < TK / 2; jj += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(s0[jj]), SCALE_LOG2, -m_new));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(s0[jj + 1]), SCALE_LOG2, -m_new));
+          const float2 e = fma2(make_float2(__uint_as_float(s0[jj]), __uint_as_float(s0[jj + 1])), scale2, negm2);
+          const float p0 = ex2_approx(e.x), p1 = ex2_approx(e.y);
           sum4[(jj >> 1) & 1] += p0 + p1;
           __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
           r[jj >> 1] = *reinterpret_cast<uint32_t*>(&b2);
         }
 #pragma unroll
         for (int jj = 0; jj < TK / 2; jj += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(s1[jj]), SCALE_LOG2, -m_new));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(s1[jj + 1]), SCALE_LOG2, -m_new));
+          const float2 e = fma2(make_float2(__uint_as_float(s1[jj]), __uint_as_float(s1[jj + 1])), scale2, negm2);
+          const float p0 = ex2_approx(e.x), p1 = ex2_approx(e.y);
           sum4[2 + ((jj >> 1) & 1)] += p0 + p1;
           __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
           r[16 + (jj >> 1)] = *reinterpret_cast<uint32_t*>(&b2);

@@ -102,6 +102,12 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
   return f2_from(r);
 }
+// Largest of three (sm_100 three-input max.f32: one instruction where two fmaxf would be).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   unsigned long long r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
