@@ -243,7 +243,9 @@ int tb_layernorm(const float* x, const float* w, const float* b, float* x_out, c
  * CUDA-core fp32 kernel (K % 16 == 0, N % 128 == 0). W is read as constant: for M <= 256
  * (bf16) or M <= 8 (fp32) the kernel may start reading it before the kernel launched just
  * before it on the stream has finished, so W must not be the output of that kernel (the
- * library's kernels let their successor start early). */
+ * library's kernels let their successor start early). A RESIDUAL GEMM of at most 256 rows
+ * whose tiles would leave most SMs idle splits K over several CTAs that add their sums
+ * into out atomically: its last bits depend on the order of those adds. */
 int tb_gemm(int dtype, const void* a, long long lda, const void* w, int m, int n, int k, const tb_epilogue* epi,
             int* err, void* stream);
 /* Large bf16 GEMMs (at least 2048 rows, N % 256 == 0, no run-time row bound, epilogue

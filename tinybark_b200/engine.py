@@ -23,6 +23,12 @@ from . import lengths, pack, tables
 
 DTYPES = {"fp32": L.F32, "bf16": L.BF16}
 MAX_DECODE_GROUPS = 8
+# Smallest part upload_parts makes (samples; 60 s of audio, about 750 encoder rows). The
+# residual GEMMs of at most 256 rows (about 20 s of audio) split K over several CTAs whose
+# sums land in the order their atomic adds take, so their last bits can differ from call
+# to call. A batch of more than 256 encoder rows is cut only into parts of more than 256
+# rows, so its encoder gives the same bits on every call.
+MIN_PART_SAMPLES = 60 * 16000
 
 
 def lane_order(idx: list[int], frames: list[int], groups: int | None = None) -> list[int]:
@@ -407,7 +413,8 @@ class Engine:
         part (at most about three times the one before, the ratio of encoder time to transfer
         time) is packed and copied while the previous one is computed. Within a part the
         clips are packed in slices of about `slice_bytes`, each copied as soon as it is
-        packed, so packing and copying overlap."""
+        packed, so packing and copying overlap. No part is shorter than MIN_PART_SAMPLES
+        (unless the whole batch is)."""
         pcm = len(clips) > 0 and all(c.dtype == np.int16 for c in clips)
         tdt = torch.int16 if pcm else torch.float32
         sizes = np.array([len(c) for c in clips], np.int64)
@@ -426,7 +433,13 @@ class Engine:
         cur = torch.cuda.current_stream(self.device)
         self._copy.wait_stream(cur)
         cuts = np.searchsorted(off, [f * total for f in fractions]).tolist()
-        edges = [0, *sorted(set(c for c in cuts if 0 < c < len(clips))), len(clips)]
+        edges = [0]
+        for c in sorted(set(c for c in cuts if 0 < c < len(clips))):
+            # No part shorter than MIN_PART_SAMPLES: such a cut is dropped, and its clips go
+            # with the next part.
+            if off[c] - off[edges[-1]] >= MIN_PART_SAMPLES and total - off[c] >= MIN_PART_SAMPLES:
+                edges.append(c)
+        edges.append(len(clips))
 
         def pack(i: int) -> None:
             hv[off[i] : off[i + 1]] = clips[i]
