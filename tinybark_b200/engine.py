@@ -404,7 +404,7 @@ class Engine:
         sample_off = torch.from_numpy(off).pin_memory().to(self.device, non_blocking=True)
         return samples, sample_off
 
-    def upload_parts(self, clips: list[np.ndarray], fractions=(1 / 16, 1 / 4, 1 / 2), slice_bytes=64 << 20):
+    def upload_parts(self, clips: list[np.ndarray], fractions=(1 / 64, 1 / 16, 1 / 4, 1 / 2), slice_bytes=64 << 20):
         """upload() in parts, for callers that start on each part while the next is still
         on its way: yields (first clip, end clip, samples, sample_off) per part, the copy
         of each part (on the engine's copy stream) ordered before the current stream's
