@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from tinybark_b200 import backends, lengths
-from tinybark_b200.engine import plan_arrays
+from tinybark_b200.engine import MIN_PART_SAMPLES, part_edges, plan_arrays
 from tinybark_b200.text import Tokenizer
 
 
@@ -29,6 +29,29 @@ def test_plan_offsets_and_tiles():
     sub = p["sub_tiles"].reshape(-1, 2)
     covered = {(c, r + k) for c, r in sub for k in range(2) if r + k < t2[c]}
     assert covered == {(c, r) for c in range(len(frames)) for r in range(t2[c])}
+
+
+def test_upload_parts_are_never_shorter_than_the_minimum():
+    """tokens_batch's upload parts: contiguous clip ranges covering the batch, cut near the
+    fractions, none shorter than MIN_PART_SAMPLES unless the batch itself is (so a batch of
+    more than 256 encoder rows never runs a part through the small-batch GEMMs whose K
+    split makes the last bits vary between calls)."""
+    rng = np.random.default_rng(3)
+    fractions = (1 / 64, 1 / 16, 1 / 4, 1 / 2)
+    for n, lo, hi in [(9, 0.5, 12.0), (40, 1.0, 30.0), (4096, 2.0, 30.0), (1, 5.0, 5.0), (3, 0.02, 60.0)]:
+        sizes = (rng.uniform(lo, hi, n) * 16000).astype(np.int64)
+        off = np.concatenate([[0], np.cumsum(sizes)])
+        edges = part_edges(off, fractions)
+        assert edges[0] == 0 and edges[-1] == n and all(a < b for a, b in zip(edges, edges[1:]))
+        lens = [int(off[b] - off[a]) for a, b in zip(edges, edges[1:])]
+        assert len(lens) == 1 or min(lens) >= MIN_PART_SAMPLES
+    # The bench's set keeps every cut, each at the first clip boundary past its fraction.
+    sizes = (rng.uniform(2.0, 30.0, 4096) * 16000).astype(np.int64)
+    off = np.concatenate([[0], np.cumsum(sizes)])
+    edges = part_edges(off, fractions)
+    assert edges[1:-1] == np.searchsorted(off, [f * off[-1] for f in fractions]).tolist()
+    # A batch of 56 s in all is one part.
+    assert part_edges(np.array([0, 56 * 16000]), fractions) == [0, 1]
 
 
 def test_plan_rejects_short_clips():

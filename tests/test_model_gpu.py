@@ -166,6 +166,24 @@ def test_end_to_end_bf16_batch_consistent():
         assert len(b) > 0
 
 
+def test_batch_encoder_gives_the_same_bits_on_every_call():
+    """A batch of 9 clips (0.5-12 s, about 700 encoder rows) is encoded as one part, never
+    as a first part of a few clips whose residual GEMMs would split K and add the ranges
+    atomically: two calls give the same encoder rows bit for bit, and the same tokens."""
+    import tinybark_b200
+    from tinybark_b200 import synthetic, weights
+
+    rng = np.random.default_rng(12)
+    clips = [synthetic.clip(float(s), 400 + i) for i, s in enumerate(rng.uniform(0.5, 12.0, 9))]
+    bark = tinybark_b200.load("gpu", weights=(weights.convert(state_dict(2), synthetic.config(2)), synthetic.config(2)))
+    runs = []
+    for _ in range(2):
+        keep, enc, plan = bark.engine._encode_batch(clips)
+        runs.append((enc.clone(), bark.tokens_batch(clips)))
+    assert plan.batch.t3_total > 256
+    assert torch.equal(runs[0][0], runs[1][0]) and runs[0][1] == runs[1][1]
+
+
 def test_tokens_batch_parts_match_whole_batch_path():
     """bf16, 40 clips of 1-30 s: tokens_batch uploads and encodes the batch in parts (the
     copy of each part overlapping the previous part's encoder) and turns finished lanes

@@ -31,6 +31,21 @@ MAX_DECODE_GROUPS = 8
 MIN_PART_SAMPLES = 60 * 16000
 
 
+def part_edges(off: np.ndarray, fractions, min_samples: int = MIN_PART_SAMPLES) -> list[int]:
+    """Clip indices where upload_parts cuts a batch whose clips start at sample offsets
+    `off` [clips + 1]: [0, ..., clips], each cut at the first clip boundary at or past a
+    fraction of the samples, except that no part is shorter than `min_samples` (a cut that
+    would leave one is dropped, its clips going with the next part)."""
+    clips, total = len(off) - 1, int(off[-1])
+    cuts = np.searchsorted(off, [f * total for f in fractions]).tolist()
+    edges = [0]
+    for c in sorted(set(c for c in cuts if 0 < c < clips)):
+        if off[c] - off[edges[-1]] >= min_samples and total - off[c] >= min_samples:
+            edges.append(c)
+    edges.append(clips)
+    return edges
+
+
 def lane_order(idx: list[int], frames: list[int], groups: int | None = None) -> list[int]:
     """Orders clips `idx` (frame counts `frames[i]`) for the decoder: longest first, and
     for the graph decoder with `groups` > 1 concurrent groups, dealt round-robin into
@@ -432,14 +447,7 @@ class Engine:
             self._copy = torch.cuda.Stream(self.device)
         cur = torch.cuda.current_stream(self.device)
         self._copy.wait_stream(cur)
-        cuts = np.searchsorted(off, [f * total for f in fractions]).tolist()
-        edges = [0]
-        for c in sorted(set(c for c in cuts if 0 < c < len(clips))):
-            # No part shorter than MIN_PART_SAMPLES: such a cut is dropped, and its clips go
-            # with the next part.
-            if off[c] - off[edges[-1]] >= MIN_PART_SAMPLES and total - off[c] >= MIN_PART_SAMPLES:
-                edges.append(c)
-        edges.append(len(clips))
+        edges = part_edges(off, fractions)
 
         def pack(i: int) -> None:
             hv[off[i] : off[i + 1]] = clips[i]
