@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from tinybark_b200 import backends, lengths
-from tinybark_b200.engine import MIN_PART_SAMPLES, part_edges, plan_arrays
+from tinybark_b200.engine import MIN_PART_SAMPLES, part_edges, plan_arrays, token_list
 from tinybark_b200.text import Tokenizer
 
 
@@ -52,6 +52,23 @@ def test_upload_parts_are_never_shorter_than_the_minimum():
     assert edges[1:-1] == np.searchsorted(off, [f * off[-1] for f in fractions]).tolist()
     # A batch of 56 s in all is one part.
     assert part_edges(np.array([0, 56 * 16000]), fractions) == [0, 1]
+
+
+def test_token_lists_share_int_objects_and_equal_tolist():
+    """Token rows become lists of the same Python ints as tolist() gives, taken from one
+    shared table (no int created per token); the multi-GPU gather does the same for rows
+    of token ids and converts anything else as it is."""
+    from tinybark_b200 import dp
+
+    rng = np.random.default_rng(1)
+    row = rng.integers(0, 8193, 3700).astype(np.int32)
+    got = token_list(row)
+    assert got == row.tolist() and all(type(t) is int for t in got)
+    assert got[0] is token_list(row[:1])[0]
+    assert token_list(row[:0]) == []
+    assert dp._id_list(row) == row.tolist()
+    odd = np.array([5, -1, 9000], np.int64)
+    assert dp._id_list(odd) == [5, -1, 9000] and dp._id_list(odd[:0]) == []
 
 
 def test_plan_rejects_short_clips():
