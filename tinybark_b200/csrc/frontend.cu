@@ -6,8 +6,11 @@
 //   per mel bin (m - mean) / (std + 1e-5), std with ddof 1.
 //
 // logmel_kernel: one warp per frame. The 512-point real FFT is a 256-point complex FFT
-// of (even, odd) sample pairs (radix-2, in shared memory) followed by the standard
-// split into the 257 real-input bins. Twiddles come from sincospi in fp64 per block.
+// of (even, odd) sample pairs followed by the standard split into the 257 real-input
+// bins. The 256-point FFT runs in registers as 8 x 32 (four-step): each lane an 8-point
+// DFT of its 8 values (n = 32 n1 + lane), a twiddle, then the 32-point DFTs across lanes
+// as 4 x 8 with two transposes through shared memory. Twiddles come from sincospi in
+// fp64 per block.
 // stats_kernel / finish_kernel / normalize_kernel: per-clip mean and std per mel bin,
 // accumulated in fp64 over frame ranges, then applied in place.
 #include <mutex>
@@ -20,6 +23,41 @@ namespace tb {
 constexpr int FE_WARPS = 8;
 constexpr int FE_SPLIT = 8;  // frame ranges per clip for the statistics
 constexpr float PREEMPH = 0.97f;
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 mul_neg_i(float2 a) { return make_float2(a.y, -a.x); }  // -i a
+
+// 4-point DFT, natural order in and out: X[k] = sum_n a[n] e^{-2 pi i n k / 4}.
+__device__ __forceinline__ void dft4(float2& a0, float2& a1, float2& a2, float2& a3) {
+  const float2 e0 = cadd(a0, a2), e1 = csub(a0, a2), o0 = cadd(a1, a3), o1 = mul_neg_i(csub(a1, a3));
+  a0 = cadd(e0, o0);
+  a2 = csub(e0, o0);
+  a1 = cadd(e1, o1);
+  a3 = csub(e1, o1);
+}
+
+// 8-point DFT, natural order in and out, as two 4-point DFTs (even and odd inputs).
+__device__ __forceinline__ void dft8(float2 (&v)[8]) {
+  constexpr float C = 0.70710678118654752f;  // cos(pi / 4)
+  float2 e0 = v[0], e1 = v[2], e2 = v[4], e3 = v[6], o0 = v[1], o1 = v[3], o2 = v[5], o3 = v[7];
+  dft4(e0, e1, e2, e3);
+  dft4(o0, o1, o2, o3);
+  o1 = make_float2(C * (o1.x + o1.y), C * (o1.y - o1.x));   // e^{-i pi/4} o1
+  o2 = mul_neg_i(o2);                                         // e^{-i pi/2} o2
+  o3 = make_float2(C * (o3.y - o3.x), -C * (o3.x + o3.y));  // e^{-3i pi/4} o3
+  v[0] = cadd(e0, o0);
+  v[4] = csub(e0, o0);
+  v[1] = cadd(e1, o1);
+  v[5] = csub(e1, o1);
+  v[2] = cadd(e2, o2);
+  v[6] = csub(e2, o2);
+  v[3] = cadd(e3, o3);
+  v[7] = csub(e3, o3);
+}
 
 __device__ __forceinline__ int find_clip(const int* off, int clips, int row) {
   int lo = 0, hi = clips;  // off[lo] <= row < off[hi]
@@ -49,12 +87,12 @@ __global__ void __launch_bounds__(256) logmel_kernel(const S* __restrict__ sampl
                                                      const float* __restrict__ window, const float* __restrict__ mel_w,
                                                      const int* __restrict__ mel_start, const int* __restrict__ mel_off,
                                                      float* __restrict__ feats) {
-  __shared__ float2 tw256[128];     // e^{-2 pi i k / 256}
+  __shared__ float2 tw256[256];     // e^{-2 pi i k / 256}
   __shared__ float2 tw512[257];     // e^{-2 pi i k / 512}
-  __shared__ float2 z[FE_WARPS][256];
+  __shared__ float2 z[FE_WARPS][264];  // per warp: the two transposes, then the spectrum
   __shared__ float pw[FE_WARPS][260];
   __shared__ float win[512];
-  for (int k = threadIdx.x; k < 128; k += 256) {
+  for (int k = threadIdx.x; k < 256; k += 256) {
     double s, c;
     sincospi(-2.0 * k / 256.0, &s, &c);
     tw256[k] = make_float2((float)c, (float)s);
@@ -76,32 +114,59 @@ __global__ void __launch_bounds__(256) logmel_kernel(const S* __restrict__ sampl
   const long long len = sample_off[clip + 1] - sample_off[clip];
   float2* zw = z[warp];
 
-  // Windowed frame, paired as complex z[n] = w[2n] + i w[2n+1], stored bit-reversed.
-  for (int n = lane; n < 256; n += 32) {
-    const int k0 = 2 * n, k1 = 2 * n + 1;
+  // Windowed frame, paired as complex z[n] = w[2n] + i w[2n+1]; lane L holds
+  // z[32 n1 + L], n1 = 0..7.
+  float2 v[8];
+#pragma unroll
+  for (int n1 = 0; n1 < 8; ++n1) {
+    const int n = 32 * n1 + lane, k0 = 2 * n, k1 = 2 * n + 1;
     const long long p0 = (long long)f * 160 + k0 - 256, p1 = p0 + 1;
     const float a = win[k0] != 0.f ? __fmul_rn(preemph_sample(x, p0, len), win[k0]) : 0.f;
     const float b = win[k1] != 0.f ? __fmul_rn(preemph_sample(x, p1, len), win[k1]) : 0.f;
-    zw[__brev(n) >> 24] = make_float2(a, b);
+    v[n1] = make_float2(a, b);
+  }
+  // Z[k1 + 8 k2] = sum_n2 W32^(n2 k2) W256^(n2 k1) sum_n1 z[32 n1 + n2] W8^(n1 k1).
+  dft8(v);  // over n1: lane L = n2 now holds Y[k1], k1 = 0..7
+#pragma unroll
+  for (int k1 = 1; k1 < 8; ++k1) v[k1] = cmul(v[k1], tw256[lane * k1]);
+  // The 32-point DFTs over n2 (one per k1), as 4 x 8 with n2 = 8 a + b, k2 = c + 4 d:
+  // Z32[c + 4 d] = sum_b W8^(b d) W32^(b c) sum_a y[8 a + b] W4^(a c).
+  // Transpose 1: T1[k1][n2] (rows of 33). Lane L then takes (k1, b) = (L / 8, L % 8) and
+  // (L / 8 + 4, L % 8): a 4-point DFT over a each, then the W32^(b c) twiddle.
+#pragma unroll
+  for (int k1 = 0; k1 < 8; ++k1) zw[k1 * 33 + lane] = v[k1];
+  __syncwarp();
+  const int b = lane & 7;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int k1 = (lane >> 3) + 4 * h;
+    float2 a0 = zw[k1 * 33 + b], a1 = zw[k1 * 33 + 8 + b], a2 = zw[k1 * 33 + 16 + b], a3 = zw[k1 * 33 + 24 + b];
+    dft4(a0, a1, a2, a3);  // now indexed by c
+    v[4 * h] = a0;
+    v[4 * h + 1] = cmul(a1, tw256[8 * b]);
+    v[4 * h + 2] = cmul(a2, tw256[16 * b]);
+    v[4 * h + 3] = cmul(a3, tw256[24 * b]);
   }
   __syncwarp();
-  // 8 radix-2 stages, 128 butterflies each, 4 per lane.
+  // Transpose 2: T2[k1][c][b]. Lane L then takes (k1, c) = (L / 4, L % 4): an 8-point DFT
+  // over b, whose output d is Z[k1 + 8 c + 32 d].
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    const int half = 1 << s;
+  for (int h = 0; h < 2; ++h) {
+    const int k1 = (lane >> 3) + 4 * h;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int bfly = lane + 32 * i;
-      const int grp = bfly >> s, pos = bfly & (half - 1);
-      const int i0 = (grp << (s + 1)) + pos, i1 = i0 + half;
-      const float2 t = tw256[pos << (7 - s)];
-      const float2 u = zw[i0], v = zw[i1];
-      const float2 vt = make_float2(v.x * t.x - v.y * t.y, v.x * t.y + v.y * t.x);
-      zw[i0] = make_float2(u.x + vt.x, u.y + vt.y);
-      zw[i1] = make_float2(u.x - vt.x, u.y - vt.y);
-    }
-    __syncwarp();
+    for (int c = 0; c < 4; ++c) zw[(k1 * 4 + c) * 8 + b] = v[4 * h + c];
   }
+  __syncwarp();
+  {
+    const int k1 = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int bb = 0; bb < 8; ++bb) v[bb] = zw[(k1 * 4 + c) * 8 + bb];
+  }
+  dft8(v);
+  __syncwarp();
+#pragma unroll
+  for (int d = 0; d < 8; ++d) zw[(lane >> 2) + 8 * (lane & 3) + 32 * d] = v[d];
+  __syncwarp();
   // Split into the real-input spectrum, power per bin.
   for (int k = lane; k <= 256; k += 32) {
     const float2 zk = zw[k & 255], zc = zw[(256 - k) & 255];
