@@ -17,7 +17,7 @@ namespace tb {
 
 constexpr int S_T2 = 8;          // depthwise-1 output rows per block: one warp each
 constexpr int S_C = 64;          // channels per block: two per lane
-constexpr int S_F1 = 64, S_F2 = 32, S_F3 = 16;
+constexpr int S_F2 = 32, S_F3 = 16;  // frequencies after depthwise 1 and 2 (conv 0 makes 64)
 constexpr int S_FEAT_ROWS = 4 * S_T2 + 3;  // feature rows behind S_T2 depthwise-1 rows
 constexpr int S_FEAT_COLS = TB_MELS + 2;   // frequency padded by one each side
 
